@@ -1,0 +1,455 @@
+#!/usr/bin/env python
+"""MoE decode benchmark of the B200 NVFP4 expert path.
+
+Workload: one decode token (batch 1) through 24 stacked routed-MoE layers of
+the Nemotron 30B-A3B shape -- 128 NVFP4 experts per layer (up 1856x2688,
+relu^2, down 2688x1856), all HBM-resident (17.24 GB), sigmoid top-6 routing
+from random logits per layer and token, x_{L+1} = x_L + moe_L(x_L) in fp32.
+A "step" is one token through all 24 layers.  Weights are seeded synthetic
+(N(0, 0.02) quantised to NVFP4 on the device): the real checkpoint is not
+available.  With --gpus N the experts are sharded by id (e % N) and the
+per-slot outputs are all-gathered over NCCL before the route-order sum.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+HIDDEN, INTER, N_EXPERTS, TOP_K, N_LAYERS = 2688, 1856, 128, 6, 24
+METRIC = "moe_decode_tok_s"
+UNIT = "tok/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=N_LAYERS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def dist_setup(n):
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}")
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, torch.device("cuda", local if world > 1 else 0)
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}",
+                                       f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self):
+        self.f.flush()
+        rows = []
+        for line in Path(self.f.name).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def time_region(fn, steps, device):
+    """CUDA-event time of `steps` calls of fn on the current stream (ms)."""
+    torch.cuda.synchronize(device)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(steps):
+        fn(i)
+    b.record()
+    b.synchronize()
+    return a.elapsed_time(b)
+
+
+def kernel_roofline(dec, bank, device, hbm, iters=192):
+    """Average device time of the two grouped expert kernels, each launch on
+    a different (layer, token) routing so that weights come from HBM."""
+    from ervf_b200.fused_nvfp4 import FusedNVFP4
+
+    f = dec.fused
+    g = torch.Generator(device=device)
+    g.manual_seed(12345)
+    L = bank.n_layers
+    ids = torch.stack([torch.randperm(N_EXPERTS, generator=g, device=device)[:TOP_K]
+                       for _ in range(iters)]).to(torch.int32)
+    w = torch.full((TOP_K,), 1.0 / TOP_K, device=device)
+    x = torch.randn(HIDDEN, device=device)
+    act = torch.zeros(TOP_K * INTER, device=device)
+    out = torch.zeros(HIDDEN, device=device)
+
+    def up(i):
+        l = i % L
+        f.moe_up_grouped(bank.up_codes[l], bank.up_scales[l], bank.up_code_bytes,
+                         bank.up_scale_bytes, ids[i], bank.globals[l], TOP_K, x, act, INTER, HIDDEN)
+
+    def down(i):
+        l = i % L
+        f.moe_down_routesum(bank.dn_codes[l], bank.dn_scales[l], bank.dn_code_bytes,
+                            bank.dn_scale_bytes, ids[i], bank.globals[l], w, TOP_K, act, out,
+                            HIDDEN, INTER, resid=x)
+
+    for fn in (up, down):
+        for i in range(8):
+            fn(i)
+    t_up = time_region(up, iters, device) / iters
+    t_dn = time_region(down, iters, device) / iters
+    rec = INTER * HIDDEN // 2 + INTER * HIDDEN // 16
+    up_bytes = TOP_K * rec + HIDDEN * 4 + TOP_K * INTER * 4
+    dn_bytes = TOP_K * rec + TOP_K * INTER * 4 + 2 * HIDDEN * 4
+    res = {
+        "moe_up_grouped": {"ms": t_up, "bytes": up_bytes, "gbs": up_bytes / t_up / 1e6},
+        "moe_down_routesum": {"ms": t_dn, "bytes": dn_bytes, "gbs": dn_bytes / t_dn / 1e6},
+    }
+    for v in res.values():
+        v["frac"] = v["gbs"] / hbm
+    return res
+
+
+def gemv_config0(device, hbm):
+    """Config 0 (one 1856x2688 NVFP4 GEMV) over an L2-cold replica pool
+    (>= 8 x L2), B200 schedule, CUDA-event time per call."""
+    from ervf_b200 import FusedNVFP4
+    from ervf_b200.formats import quantize_nvfp4_torch
+
+    f = FusedNVFP4(device=device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    codes, scales, gsc = quantize_nvfp4_torch(torch.randn(INTER, HIDDEN, generator=gen,
+                                                          device=device) * 0.02)
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    rec = codes.numel() + scales.numel()
+    n = max(8, (8 * l2) // rec + 1)
+    pc = codes.reshape(1, -1).repeat(n, 1)
+    ps = scales.reshape(1, -1).repeat(n, 1)
+    x = torch.randn(HIDDEN, device=device)
+    out = torch.zeros(INTER, device=device)
+    g = float(gsc)
+
+    def call(i):
+        j = i % n
+        f.gemv_into(out, pc[j], ps[j], x, g, INTER, HIDDEN, apply_relu2=True)
+
+    for i in range(10):
+        call(i)
+    iters = 4 * n
+    ms = time_region(call, iters, device) / iters
+    algo = rec + 4 + HIDDEN * 4 + INTER * 4
+    return {"rows": INTER, "cols": HIDDEN, "us": ms * 1e3, "gbs": algo / ms / 1e6,
+            "frac": algo / ms / 1e6 / hbm, "pool_replicas": n, "bytes_per_call": algo}
+
+
+def cpu_sample(bank, layers_sampled=2, tokens=2):
+    """Reference-path CPU baseline on a bounded sample: `tokens` tokens x
+    `layers_sampled` layers of the same workload, torch FP32 dequant + matmul
+    with all host threads; extrapolated to tok/s over 24 layers."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import cpu_baseline as cb
+
+    cores = cb.use_all_cores()
+    g = np.random.default_rng(7)
+    times = []
+    for t in range(tokens):
+        x = torch.from_numpy(g.standard_normal(HIDDEN).astype(np.float32))
+        for l in range(layers_sampled):
+            ids = g.choice(N_EXPERTS, TOP_K, replace=False)
+            experts = {}
+            for e in ids:
+                (uc, us, ug), (dc, ds, dg) = bank.expert_host(l, int(e))
+                experts[int(e)] = ((torch.from_numpy(uc), torch.from_numpy(us), float(ug)),
+                                   (torch.from_numpy(dc), torch.from_numpy(ds), float(dg)))
+            w = np.full(TOP_K, 1.0 / TOP_K, np.float32)
+            t0 = time.perf_counter()
+            x = cb.moe_layer(x, experts, ids, w, HIDDEN, INTER)
+            times.append(time.perf_counter() - t0)
+    per_layer = statistics.median(times)
+    return {"value": 1.0 / (per_layer * N_LAYERS), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{tokens} tokens x {layers_sampled} of {N_LAYERS} layers (6 experts each), "
+                      f"median {per_layer * 1e3:.1f} ms/layer, extrapolated x{N_LAYERS} layers"}
+
+
+def reference_arm(args, rank, world):
+    """CPU reference path (torch FP32 dequant-then-matmul, all host cores) on
+    the same workload: each step is one token through a bounded sample of one
+    layer, extrapolated to 24 layers."""
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import cpu_baseline as cb
+    from ervf_b200.formats import synthetic_nvfp4
+
+    cores = cb.use_all_cores()
+    g = np.random.default_rng(11)
+    n_pool = 12
+    pool = {}
+    for e in range(n_pool):
+        uc, us, ug = synthetic_nvfp4(INTER, HIDDEN, seed=e)
+        dc, ds, dg = synthetic_nvfp4(HIDDEN, INTER, seed=500 + e)
+        pool[e] = ((torch.from_numpy(uc.reshape(-1)), torch.from_numpy(us.reshape(-1)), float(ug)),
+                   (torch.from_numpy(dc.reshape(-1)), torch.from_numpy(ds.reshape(-1)), float(dg)))
+    times = []
+    for step in range(args.warmup + args.steps):
+        x = torch.from_numpy(g.standard_normal(HIDDEN).astype(np.float32))
+        ids = g.choice(n_pool, TOP_K, replace=False)
+        w = np.full(TOP_K, 1.0 / TOP_K, np.float32)
+        t0 = time.perf_counter()
+        cb.moe_layer(x, pool, ids, w, HIDDEN, INTER)
+        if step >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    per_layer = sum(times) / len(times)
+    value = 1.0 / (per_layer * N_LAYERS)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_layer * N_LAYERS * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "config4: 24 MoE layers x 128 NVFP4 experts (2688/1856), top-6, "
+                               "batch 1", "parallelism": "cpu", "l2": "n/a"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": "each step: 1 token x 1 of 24 layers (6 experts, dequant + "
+                                   "matmul), extrapolated x24"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", 0))
+        world = int(os.environ.get("WORLD_SIZE", 1))
+        reference_arm(args, rank, world)
+        return
+    rank, world, device = dist_setup(args.gpus)
+    sys.path.insert(0, str(ROOT))
+    from ervf_b200 import build
+    from ervf_b200.moe import ExpertBank, MoEDecoder
+
+    build.build()
+    hbm, peak_kind = peaks()
+    L = args.layers
+    t0 = time.time()
+    bank = ExpertBank(L, N_EXPERTS, HIDDEN, INTER, device)
+    # every rank builds only the experts it owns (e % world == rank)
+    from ervf_b200.formats import quantize_nvfp4_torch
+
+    gen = torch.Generator(device=device)
+    for l in range(L):
+        for e in range(rank, N_EXPERTS, world):
+            recs = []
+            for off, (r, c) in ((0, (INTER, HIDDEN)), (500, (HIDDEN, INTER))):
+                gen.manual_seed(1000 * l + e + off)
+                recs.append(quantize_nvfp4_torch(torch.randn(r, c, generator=gen, device=device)
+                                                 * 0.02))
+            bank.upload_expert(l, e, recs[0], recs[1])
+    torch.cuda.synchronize(device)
+    build_s = time.time() - t0
+
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+
+        group = dist.group.WORLD
+    dec = MoEDecoder(bank, TOP_K, ep_ranks=world, ep_rank=rank, group=group)
+
+    T = args.warmup + args.steps
+    g = torch.Generator(device=device)
+    g.manual_seed(2)
+    rlogs = torch.randn(T, L, N_EXPERTS, generator=g, device=device)
+    xs = torch.randn(T, HIDDEN, generator=g, device=device)
+    xs = (xs.view(torch.int32) & -65536).view(torch.float32)  # bf16-valued hidden states
+    x_buf = torch.zeros(HIDDEN, device=device)
+    r_buf = torch.zeros(L, N_EXPERTS, device=device)
+
+    use_graph = world == 1 and not args.no_graph
+    graph = None
+    if use_graph:
+        s = torch.cuda.Stream(device)
+        s.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                y = dec.step(x_buf, r_buf)
+        torch.cuda.current_stream(device).wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            y_graph = dec.step(x_buf, r_buf)
+
+    def step(i):
+        x_buf.copy_(xs[i])
+        r_buf.copy_(rlogs[i])
+        if graph is not None:
+            graph.replay()
+        else:
+            dec.step(x_buf, r_buf)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    for i in range(args.warmup):
+        step(i)
+    barrier()
+    with Clocks(device.index) as clk:
+        ms = time_region(lambda i: step(args.warmup + i), args.steps, device)
+        barrier()
+    clocks = clk.summary()
+    ms_t = torch.tensor([ms], device=device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    value = args.steps / (ms / 1e3)
+
+    # ---- end to end through the public API with host buffers
+    xh = xs.cpu().pin_memory()
+    rh = rlogs.cpu().pin_memory()
+    yh = torch.zeros(args.steps, HIDDEN, pin_memory=True)
+    out_dev = y_graph if graph is not None else dec.xs[(L - 1) & 1]
+
+    def e2e_step(i):
+        x_buf.copy_(xh[i], non_blocking=True)
+        r_buf.copy_(rh[i], non_blocking=True)
+        if graph is not None:
+            graph.replay()
+        else:
+            dec.step(x_buf, r_buf)
+        yh[i % args.steps].copy_(out_dev, non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+
+    for i in range(min(3, args.warmup)):
+        e2e_step(i)
+    barrier()
+    e2e_ms = time_region(lambda i: e2e_step(args.warmup + i), args.steps, device)
+    barrier()
+    e_t = torch.tensor([e2e_ms], device=device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
+    e2e_value = args.steps / (float(e_t.item()) / 1e3)
+
+    kern = kernel_roofline(dec, bank, device, hbm) if world == 1 else None
+    gemv0 = gemv_config0(device, hbm) if (world == 1 and rank == 0) else None
+
+    if rank == 0:
+        # bytes one token streams: distinct (layer, expert) pairs x expert bytes
+        token_bytes = L * TOP_K * bank.expert_bytes()
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "nvfp4-w/f32-acc", "data": "synthetic",
+            "config": {"workload": f"config4: {L} MoE layers x {N_EXPERTS} NVFP4 experts "
+                                   f"(hidden {HIDDEN}, inter {INTER}), top-{TOP_K} sigmoid, batch 1",
+                       "global_batch": 1, "parallelism": f"ep{world}",
+                       "l2": "inputs larger than L2 (17.2 GB bank, 808 MB streamed per token)",
+                       "cuda_graph": graph is not None},
+            "gpu_launches": 3 * L * args.steps if world == 1 else 4 * L * args.steps,
+            "token_bytes": token_bytes,
+            "token_roofline_frac": (token_bytes / (ms / args.steps / 1e3) / 1e9) / (hbm * world),
+            "clocks": clocks,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": (HIDDEN + L * N_EXPERTS) * 4,
+                    "d2h_bytes_per_step": HIDDEN * 4},
+            "bank_build_s": build_s,
+        }
+        if kern is not None:
+            dom = max(kern, key=lambda k: kern[k]["ms"])
+            traffic = None
+            tfile = ROOT / "profiles" / "traffic.json"
+            if tfile.exists():
+                traffic = json.loads(tfile.read_text()).get(dom)
+            line["roofline"] = {"bound": "hbm", "kernel": dom, "achieved": kern[dom]["gbs"],
+                                "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
+                                "frac": kern[dom]["frac"], "traffic": traffic,
+                                "algorithmic_bytes": kern[dom]["bytes"]}
+            line["kernels"] = kern
+        if gemv0 is not None:
+            line["gemv_config0"] = gemv0
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_sample(bank)
+        print(json.dumps(line), flush=True)
+    if graph is not None:
+        del graph
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

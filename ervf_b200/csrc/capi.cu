@@ -1,0 +1,326 @@
+// capi.cu -- the extern "C" boundary (include/ervf_b200.h): argument checks,
+// then one or two launches on the caller's stream.  No allocation, no host
+// synchronisation (except ervf_device_status, which is documented as such).
+#include "../../include/ervf_b200.h"
+
+#include "aux.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace ervf;
+
+namespace {
+
+inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+inline bool al(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+inline bool width_ok(int w) { return w == 0 || w == 4 || w == 8 || w == 16 || w == 32; }
+
+// Shape limits of the NVFP4 schedules: cols % 16 == 0 and the width-32
+// fallback's shared-memory footprint (activation + LUT + 8 rows of chains).
+int check_nvfp4_shape(int rows, int cols, int width) {
+  if (rows <= 0 || cols <= 0 || (cols & 15)) return kErrShape;
+  if (!width_ok(width)) return kErrArg;
+  const int rp = width ? 256 / width : 8;
+  const long long smem = (long long)(cols + 256 + rp * kRowPitch) * 4;
+  if (smem > device_smem_optin()) return kErrShape;
+  return kOk;
+}
+
+MatRef direct(const uint8_t* c, const uint8_t* s, float g) {
+  MatRef m{};
+  m.codes = c;
+  m.scales = s;
+  m.g = g;
+  return m;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ervf_version(void) { return 100; }
+
+int ervf_device_status(void) { return read_device_error(true); }
+
+int ervf_nvfp4_gemv(const uint8_t* codes, const uint8_t* scales, const float* x, float* out,
+                    float global_scale, int rows, int cols, int apply_relu2, float out_scale,
+                    int width, int legacy_tree, void* stream) {
+  if (!codes || !scales || !x || !out) return kErrNull;
+  if (int e = check_nvfp4_shape(rows, cols, width)) return e;
+  if (!al(codes, 4) || !al(x, 4) || !al(out, 4)) return kErrAlign;
+  GemvBatch b{};
+  b.rows = rows;
+  b.cols = cols;
+  b.njobs = 1;
+  b.mode = 0;
+  b.relu2 = apply_relu2 ? 1 : 0;
+  b.out_scale = out_scale;
+  b.legacy_tree = legacy_tree ? 1 : 0;
+  b.job[0].mat = direct(codes, scales, global_scale);
+  b.job[0].x = x;
+  b.job[0].out = out;
+  return launch_nvfp4_batch(b, width, S(stream));
+}
+
+int ervf_nvfp4_gemv_ind(const uint8_t* codes_base, const uint8_t* scales_base,
+                        const int32_t* slot_ptr, const int32_t* id_ptr, const float* globals,
+                        int gsel, const float* x, float* out, int rows, int cols, int apply_relu2,
+                        float out_scale, size_t code_stride, size_t scale_stride, int width,
+                        void* stream) {
+  if (!codes_base || !scales_base || !slot_ptr || !id_ptr || !globals || !x || !out) return kErrNull;
+  if (int e = check_nvfp4_shape(rows, cols, width)) return e;
+  if (gsel < 0 || gsel > 1) return kErrArg;
+  if (!al(codes_base, 4) || (code_stride & 3) || !al(x, 4) || !al(out, 4)) return kErrAlign;
+  GemvBatch b{};
+  b.rows = rows;
+  b.cols = cols;
+  b.njobs = 1;
+  b.relu2 = apply_relu2 ? 1 : 0;
+  b.out_scale = out_scale;
+  MatRef m{};
+  m.codes = codes_base;
+  m.scales = scales_base;
+  m.slot_ptr = slot_ptr;
+  m.id_ptr = id_ptr;
+  m.globals = globals;
+  m.gsel = gsel;
+  m.code_stride = code_stride;
+  m.scale_stride = scale_stride;
+  b.job[0].mat = m;
+  b.job[0].x = x;
+  b.job[0].out = out;
+  return launch_nvfp4_batch(b, width, S(stream));
+}
+
+int ervf_nvfp4_gemv_grouped(int njobs, const uint8_t* const* codes, const uint8_t* const* scales,
+                            const float* global_scales, const float* const* xs, float* const* outs,
+                            int rows, int cols, int apply_relu2, float out_scale, int width,
+                            void* stream) {
+  if (!codes || !scales || !global_scales || !xs || !outs) return kErrNull;
+  if (njobs <= 0 || njobs > kMaxJobs) return kErrShape;
+  if (int e = check_nvfp4_shape(rows, cols, width)) return e;
+  GemvBatch b{};
+  b.rows = rows;
+  b.cols = cols;
+  b.njobs = njobs;
+  b.relu2 = apply_relu2 ? 1 : 0;
+  b.out_scale = out_scale;
+  for (int j = 0; j < njobs; ++j) {
+    if (!codes[j] || !scales[j] || !xs[j] || !outs[j]) return kErrNull;
+    if (!al(codes[j], 4) || !al(xs[j], 4) || !al(outs[j], 4)) return kErrAlign;
+    b.job[j].mat = direct(codes[j], scales[j], global_scales[j]);
+    b.job[j].x = xs[j];
+    b.job[j].out = outs[j];
+  }
+  return launch_nvfp4_batch(b, width, S(stream));
+}
+
+int ervf_weighted_accumulate(float* dst, const float* src, float weight, int n, void* stream) {
+  if (!dst || !src) return kErrNull;
+  if (n < 0) return kErrShape;
+  if (n == 0) return kOk;
+  return launch_weighted_accumulate(dst, src, weight, nullptr, n, S(stream));
+}
+
+int ervf_weighted_accumulate_ind(float* dst, const float* src, const float* w_ptr, int n,
+                                 void* stream) {
+  if (!dst || !src || !w_ptr) return kErrNull;
+  if (n < 0) return kErrShape;
+  if (n == 0) return kOk;
+  return launch_weighted_accumulate(dst, src, 0.0f, w_ptr, n, S(stream));
+}
+
+int ervf_moe_up_grouped(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
+                        size_t up_scale_stride, const int32_t* ids, const float* globals, int top_k,
+                        const float* x, float* act, int inter, int hidden, int width, void* stream) {
+  if (!up_codes || !up_scales || !ids || !globals || !x || !act) return kErrNull;
+  if (top_k <= 0 || top_k > kMaxJobs) return kErrShape;
+  if (int e = check_nvfp4_shape(inter, hidden, width)) return e;
+  if (!al(up_codes, 4) || (up_code_stride & 3) || !al(x, 4) || !al(act, 4)) return kErrAlign;
+  GemvBatch b{};
+  b.rows = inter;
+  b.cols = hidden;
+  b.njobs = top_k;
+  b.relu2 = 1;
+  b.out_scale = 1.0f;
+  for (int s = 0; s < top_k; ++s) {
+    MatRef m{};
+    m.codes = up_codes;
+    m.scales = up_scales;
+    m.slot_ptr = ids + s;
+    m.id_ptr = ids + s;
+    m.globals = globals;
+    m.gsel = 1;
+    m.code_stride = up_code_stride;
+    m.scale_stride = up_scale_stride;
+    b.job[s].mat = m;
+    b.job[s].x = x;
+    b.job[s].out = act + (size_t)s * inter;
+  }
+  return launch_nvfp4_batch(b, width, S(stream));
+}
+
+int ervf_moe_down_routesum(const uint8_t* dn_codes, const uint8_t* dn_scales,
+                           size_t dn_code_stride, size_t dn_scale_stride, const int32_t* ids,
+                           const float* globals, const float* route_w, int top_k, const float* act,
+                           const float* base, const float* resid, float* out, int hidden, int inter,
+                           int width, void* stream) {
+  if (!dn_codes || !dn_scales || !ids || !globals || !route_w || !act || !out) return kErrNull;
+  if (top_k <= 0 || top_k > kMaxJobs) return kErrShape;
+  if (int e = check_nvfp4_shape(hidden, inter, width)) return e;
+  if (!al(dn_codes, 4) || (dn_code_stride & 3) || !al(act, 4) || !al(out, 4)) return kErrAlign;
+  GemvBatch b{};
+  b.rows = hidden;
+  b.cols = inter;
+  b.njobs = top_k;
+  b.mode = 1;
+  b.out_scale = 1.0f;
+  b.route_w = route_w;
+  b.base = base;
+  b.resid = resid;
+  b.rs_out = out;
+  for (int s = 0; s < top_k; ++s) {
+    MatRef m{};
+    m.codes = dn_codes;
+    m.scales = dn_scales;
+    m.slot_ptr = ids + s;
+    m.id_ptr = ids + s;
+    m.globals = globals;
+    m.gsel = 0;
+    m.code_stride = dn_code_stride;
+    m.scale_stride = dn_scale_stride;
+    b.job[s].mat = m;
+    b.job[s].x = act + (size_t)s * inter;
+    b.job[s].out = nullptr;
+  }
+  return launch_nvfp4_batch(b, width, S(stream));
+}
+
+int ervf_ep_expert_slots(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
+                         size_t up_scale_stride, const uint8_t* dn_codes, const uint8_t* dn_scales,
+                         size_t dn_code_stride, size_t dn_scale_stride, const int32_t* ids,
+                         const float* globals, int top_k, const float* x, float* act,
+                         float* contrib, int hidden, int inter, int ep_ranks, int ep_rank,
+                         int width, void* stream) {
+  if (!up_codes || !up_scales || !dn_codes || !dn_scales || !ids || !globals || !x || !act || !contrib)
+    return kErrNull;
+  if (top_k <= 0 || top_k > kMaxJobs || ep_ranks < 1 || ep_rank < 0 || ep_rank >= ep_ranks)
+    return kErrShape;
+  if (int e = check_nvfp4_shape(inter, hidden, width)) return e;
+  if (int e = check_nvfp4_shape(hidden, inter, width)) return e;
+  if (!al(up_codes, 4) || !al(dn_codes, 4) || (up_code_stride & 3) || (dn_code_stride & 3) ||
+      !al(x, 4) || !al(act, 4) || !al(contrib, 4))
+    return kErrAlign;
+  GemvBatch b{};
+  b.njobs = top_k;
+  b.out_scale = 1.0f;
+  b.ep_ids = ids;
+  b.ep_ranks = ep_ranks;
+  b.ep_rank = ep_rank;
+  b.rows = inter;
+  b.cols = hidden;
+  b.relu2 = 1;
+  for (int s = 0; s < top_k; ++s) {
+    MatRef m{};
+    m.codes = up_codes;
+    m.scales = up_scales;
+    m.slot_ptr = ids + s;
+    m.id_ptr = ids + s;
+    m.globals = globals;
+    m.gsel = 1;
+    m.code_stride = up_code_stride;
+    m.scale_stride = up_scale_stride;
+    b.job[s].mat = m;
+    b.job[s].x = x;
+    b.job[s].out = act + (size_t)s * inter;
+  }
+  if (int e = launch_nvfp4_batch(b, width, S(stream))) return e;
+  b.rows = hidden;
+  b.cols = inter;
+  b.relu2 = 0;
+  for (int s = 0; s < top_k; ++s) {
+    MatRef& m = b.job[s].mat;
+    m.codes = dn_codes;
+    m.scales = dn_scales;
+    m.gsel = 0;
+    m.code_stride = dn_code_stride;
+    m.scale_stride = dn_scale_stride;
+    b.job[s].x = act + (size_t)s * inter;
+    b.job[s].out = contrib + (size_t)s * hidden;
+  }
+  return launch_nvfp4_batch(b, width, S(stream));
+}
+
+int ervf_ep_route_sum(const float* gathered, const int32_t* ids, const float* route_w, int top_k,
+                      const float* x, float* out, int hidden, int ep_ranks, void* stream) {
+  if (!gathered || !ids || !route_w || !out) return kErrNull;
+  if (top_k <= 0 || hidden <= 0 || ep_ranks < 1) return kErrShape;
+  return launch_ep_route_sum(gathered, ids, route_w, top_k, x, out, hidden, ep_ranks, S(stream));
+}
+
+int ervf_down_masked(float* out, const uint8_t* bank, const float* act, uint32_t* masks,
+                     int32_t* plist, int32_t* pcount, int32_t* nz, int32_t* nzc,
+                     float global_scale, int hidden, int inter, int nchunks, void* stream) {
+  if (!out || !bank || !act || !masks || !plist || !pcount || !nz || !nzc) return kErrNull;
+  if (hidden <= 0 || (hidden & 1) || inter <= 0 || (inter & 15) || inter > 65536) return kErrShape;
+  if (nchunks <= 0 || nchunks > 32) return kErrArg;
+  return launch_down_masked(bank, act, masks, plist, pcount, nz, nzc, global_scale, nullptr,
+                            nullptr, 0, out, hidden, inter, nchunks, S(stream));
+}
+
+int ervf_down_masked_ind(float* out, const uint8_t* down_base, const int32_t* id_ptr,
+                         size_t panel_bytes, const float* globals, const float* act,
+                         uint32_t* masks, int32_t* plist, int32_t* pcount, int32_t* nz,
+                         int32_t* nzc, int hidden, int inter, int nchunks, void* stream) {
+  if (!out || !down_base || !id_ptr || !globals || !act || !masks || !plist || !pcount || !nz || !nzc)
+    return kErrNull;
+  if (hidden <= 0 || (hidden & 1) || inter <= 0 || (inter & 15) || inter > 65536) return kErrShape;
+  if (nchunks <= 0 || nchunks > 32) return kErrArg;
+  return launch_down_masked(down_base, act, masks, plist, pcount, nz, nzc, 0.0f, id_ptr, globals,
+                            panel_bytes, out, hidden, inter, nchunks, S(stream));
+}
+
+int ervf_panel_major(const uint8_t* codes, const uint8_t* scales, uint8_t* block, int rows,
+                     int inter, void* stream) {
+  if (!codes || !scales || !block) return kErrNull;
+  if (rows <= 0 || (rows & 1) || inter <= 0 || (inter & 15)) return kErrShape;
+  return launch_panel_major(codes, scales, block, rows, inter, S(stream));
+}
+
+int ervf_bf16_gemv(const uint16_t* W, const float* x, float* out, int rows, int cols, int batch,
+                   void* stream) {
+  if (!W || !x || !out) return kErrNull;
+  if (rows <= 0 || cols <= 0 || (cols & 7)) return kErrShape;
+  if (batch < 1 || batch > 8) return kErrArg;
+  if (!al(W, 16) || !al(x, 16) || !al(out, 4)) return kErrAlign;
+  return launch_bf16_gemv(W, x, out, rows, cols, batch, S(stream));
+}
+
+int ervf_route_topk(const float* rlog, const float* gate_b, int32_t* ids, float* w, int n,
+                    int top_k, float scaling, int bad_pick, void* stream) {
+  if (!rlog || !gate_b || !ids || !w) return kErrNull;
+  if (n <= 0 || n > 1024 || top_k <= 0 || top_k > 64 || top_k > n) return kErrShape;
+  return launch_route_topk(rlog, gate_b, ids, w, n, top_k, scaling, bad_pick, S(stream));
+}
+
+int ervf_cache_assign(int32_t* slot_of, int32_t* expert_of, int32_t* last_used, int32_t* state2,
+                      const int32_t* ids, int32_t* slots, int32_t* need, int32_t* stats2, int cap,
+                      int top_k, void* stream) {
+  if (!slot_of || !expert_of || !last_used || !state2 || !ids || !slots || !need || !stats2)
+    return kErrNull;
+  if (cap <= 0 || top_k <= 0) return kErrShape;
+  return launch_cache_assign(slot_of, expert_of, last_used, state2, ids, slots, need, stats2, cap,
+                             top_k, S(stream));
+}
+
+int ervf_cache_fetch(const uint8_t* bank_c, const uint8_t* bank_s, uint8_t* cache_c,
+                     uint8_t* cache_s, const int32_t* ids, const int32_t* slots,
+                     const int32_t* need, size_t code_bytes, size_t scale_bytes, int top_k,
+                     void* stream) {
+  if (!bank_c || !bank_s || !cache_c || !cache_s || !ids || !slots || !need) return kErrNull;
+  if (top_k <= 0 || top_k > 65535) return kErrShape;
+  return launch_cache_fetch(bank_c, bank_s, cache_c, cache_s, ids, slots, need, code_bytes,
+                            scale_bytes, top_k, S(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,83 @@
+// kernels.h -- host-side launch interfaces shared by the .cu files and capi.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace ervf {
+
+constexpr int kMaxJobs = 16;
+
+// Where one NVFP4 matrix lives.  Direct: codes/scales/g as given.  Indirect
+// (the reference's *_ind kernels, fused_nvfp4.py:548-646): codes/scales are
+// cache bases offset by (*slot_ptr) * stride, and g = globals[(*id_ptr)*2+gsel]
+// is read on the device.
+struct MatRef {
+  const uint8_t* codes;
+  const uint8_t* scales;
+  float g;
+  const int* slot_ptr;
+  const int* id_ptr;
+  const float* globals;
+  int gsel;
+  size_t code_stride;
+  size_t scale_stride;
+};
+
+struct GemvJob {
+  MatRef mat;
+  const float* x;
+  float* out;
+};
+
+// One launch over `njobs` matrices of identical shape [rows x cols].
+//   mode 0: every job writes out[r] = epilogue(row sum)           (grouped GEMV)
+//   mode 1: row block r gets, in ROUTE order s = 0..njobs-1,
+//           acc = fmaf(y_s[r], route_w[s], acc) from acc = base[r] (or 0),
+//           then rs_out[r] = resid[r] + acc (or acc)               (down + routed sum)
+struct GemvBatch {
+  int rows, cols, njobs, mode;
+  int relu2;
+  float out_scale;
+  int legacy_tree;  // 1: the 256-thread kernel's combine (S + 0.0 per group sum)
+  GemvJob job[kMaxJobs];
+  const float* route_w;
+  const float* base;
+  const float* resid;
+  float* rs_out;
+  // Expert parallelism (mode 0 only): job j runs only on the rank that owns
+  // expert ep_ids[j], i.e. ep_ids[j] % ep_ranks == ep_rank (read on device).
+  const int* ep_ids;
+  int ep_ranks, ep_rank;
+};
+
+__host__ __device__ inline bool job_active(const GemvBatch& b, int job) {
+#ifdef __CUDA_ARCH__
+  return b.ep_ranks <= 1 || (b.ep_ids[job] % b.ep_ranks) == b.ep_rank;
+#else
+  (void)b;
+  (void)job;
+  return true;
+#endif
+}
+
+// width 0: the TMA-staged B200 schedule (falls back to width 32 where its
+// preconditions do not hold); 4/8/16/32: W lanes per row, lane L owning the
+// chains L + W*i.  Every schedule returns the same bits.
+int launch_nvfp4_batch(const GemvBatch& b, int width, cudaStream_t stream);
+
+// BF16 GEMV (gpu_kernels.py:21-49 semantics), out[b*rows + r].
+int launch_bf16_gemv(const uint16_t* W, const float* x, float* out, int rows, int cols,
+                     int batch, cudaStream_t stream);
+
+int launch_weighted_accumulate(float* dst, const float* src, float weight, const float* w_ptr,
+                               int n, cudaStream_t stream);
+
+int device_sm_count();
+int device_smem_optin();
+
+// Reads (and optionally clears) the device error word set by bounded waits.
+int read_device_error(bool clear);
+
+}  // namespace ervf

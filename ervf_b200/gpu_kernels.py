@@ -1,0 +1,41 @@
+"""``GPUKernels.mv_bf16`` -- the BF16 dense GEMV of the reference's kernel
+wrapper (kennydd001/ervf src/moe_lab/lightningstream_nemotron/
+gpu_kernels.py:1549-1551) on the B200 C ABI, plus a batched form.
+
+Only the GEMV that lies on the expert-decode path is provided; the
+reference's attention / Mamba / norm kernels are out of scope.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .fused_nvfp4 import _need, ptr
+
+
+class GPUKernels:
+    def __init__(self, block: int = 256, device=None):
+        _lib.load()
+        self.block = block
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None \
+            else torch.device(device)
+        self.stream = None
+
+    def _s(self) -> int:
+        if self.stream is not None:
+            return int(self.stream.cuda_stream)
+        return int(torch.cuda.current_stream(self.device).cuda_stream)
+
+    def mv_bf16(self, out, W, x, rows: int, cols: int) -> None:
+        """out[rows] = bf16 W[rows, cols] @ x[cols] (fp32), bit-exact to the
+        reference's gemv_bf16."""
+        self.mv_bf16_batched(out, W, x, rows, cols, 1)
+
+    def mv_bf16_batched(self, out, W, x, rows: int, cols: int, batch: int) -> None:
+        """out[b*rows + r] for x[b*cols + k], b < batch <= 8."""
+        _need(out, batch * rows, "out")
+        _need(W, rows * cols, "W")
+        _need(x, batch * cols, "x")
+        _lib.call("ervf_bf16_gemv", ptr(W), ptr(x), ptr(out), int(rows), int(cols), int(batch),
+                  self._s())

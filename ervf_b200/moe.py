@@ -1,0 +1,166 @@
+"""HBM-resident routed experts and the MoE decode step on the C ABI.
+
+``ExpertBank`` is the residency / upload path: every routed expert of every
+MoE layer lives in HBM for the life of the process, uploaded once, in the
+layout the grouped kernels read directly (replaces the reference's pinned
+host bank + LRU device cache, runtime.py:216-267, :324-381, whose slot map
+becomes the identity when everything is resident).  Per layer:
+
+    up_codes   u8[E][inter * hidden / 2]    row-major, low nibble first
+    up_scales  u8[E][inter * hidden / 16]   E4M3
+    dn_codes   u8[E][hidden * inter / 2]
+    dn_scales  u8[E][hidden * inter / 16]
+    globals    f32[E][2] = (g_down, g_up)   (runtime.py:246-247)
+
+Every record starts on a 16-byte boundary (the per-expert byte counts of
+the supported shapes are multiples of 16), so the TMA schedule streams them
+with 1-D bulk copies.
+
+``MoEDecoder`` runs routed MoE layers of one token: device router
+(route_topk), one launch for the top-k up projections with relu^2, one
+launch for the top-k down projections fused with the route-order weighted
+sum and the residual add x + moe(x).  With expert parallelism (``ep_ranks``
+> 1) each rank owns experts e with e % ep_ranks == rank, computes only its
+slots' down outputs, and the per-slot outputs are all-gathered before the
+same route-order sum -- so every rank's result is bit-identical to one GPU.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _lib
+from .formats import quantize_nvfp4_torch
+from .fused_nvfp4 import FusedNVFP4, ptr
+
+
+class ExpertBank:
+    def __init__(self, n_layers: int, n_experts: int, hidden: int, inter: int, device=None,
+                 layers=None):
+        self.n_layers, self.n_experts = n_layers, n_experts
+        self.hidden, self.inter = hidden, inter
+        self.device = torch.device(device or "cuda")
+        self.up_code_bytes = inter * hidden // 2
+        self.up_scale_bytes = inter * hidden // 16
+        self.dn_code_bytes = hidden * inter // 2
+        self.dn_scale_bytes = hidden * inter // 16
+        for b in (self.up_code_bytes, self.up_scale_bytes, self.dn_code_bytes, self.dn_scale_bytes):
+            if b % 16:
+                raise ValueError("per-expert record sizes must be multiples of 16 bytes")
+        self.owned = list(range(n_experts)) if layers is None else layers
+        E, d = n_experts, self.device
+        u8 = torch.uint8
+        self.up_codes = [torch.empty(E * self.up_code_bytes, dtype=u8, device=d) for _ in range(n_layers)]
+        self.up_scales = [torch.empty(E * self.up_scale_bytes, dtype=u8, device=d) for _ in range(n_layers)]
+        self.dn_codes = [torch.empty(E * self.dn_code_bytes, dtype=u8, device=d) for _ in range(n_layers)]
+        self.dn_scales = [torch.empty(E * self.dn_scale_bytes, dtype=u8, device=d) for _ in range(n_layers)]
+        self.globals = [torch.zeros(E, 2, dtype=torch.float32, device=d) for _ in range(n_layers)]
+
+    @property
+    def nbytes(self) -> int:
+        per = self.up_code_bytes + self.up_scale_bytes + self.dn_code_bytes + self.dn_scale_bytes
+        return self.n_layers * self.n_experts * per
+
+    def expert_bytes(self) -> int:
+        return self.up_code_bytes + self.up_scale_bytes + self.dn_code_bytes + self.dn_scale_bytes
+
+    # -------------------------------------------------------------- upload
+    def upload_expert(self, layer: int, e: int, up, dn, non_blocking: bool = False) -> None:
+        """up / dn = (codes, scales, g) as numpy arrays or tensors (host or
+        device, row-major as in the checkpoint)."""
+        for (c, s, g), codes, scales, cb, sb, gi in (
+                (up, self.up_codes, self.up_scales, self.up_code_bytes, self.up_scale_bytes, 1),
+                (dn, self.dn_codes, self.dn_scales, self.dn_code_bytes, self.dn_scale_bytes, 0)):
+            ct = torch.as_tensor(c).reshape(-1)
+            st = torch.as_tensor(s).reshape(-1)
+            if ct.numel() != cb or st.numel() != sb:
+                raise ValueError("record size does not match the bank shape")
+            codes[layer][e * cb:(e + 1) * cb].copy_(ct, non_blocking=non_blocking)
+            scales[layer][e * sb:(e + 1) * sb].copy_(st, non_blocking=non_blocking)
+            self.globals[layer][e, gi] = float(np.float32(g.item() if hasattr(g, "item") else g))
+
+    def expert_host(self, layer: int, e: int):
+        """(up, dn) records of one expert, copied back to numpy."""
+        cb, sb = self.up_code_bytes, self.up_scale_bytes
+        db, ds = self.dn_code_bytes, self.dn_scale_bytes
+        g = self.globals[layer][e].cpu().numpy()
+        up = (self.up_codes[layer][e * cb:(e + 1) * cb].cpu().numpy(),
+              self.up_scales[layer][e * sb:(e + 1) * sb].cpu().numpy(), np.float32(g[1]))
+        dn = (self.dn_codes[layer][e * db:(e + 1) * db].cpu().numpy(),
+              self.dn_scales[layer][e * ds:(e + 1) * ds].cpu().numpy(), np.float32(g[0]))
+        return up, dn
+
+    @classmethod
+    def synthetic(cls, n_layers: int, n_experts: int, hidden: int, inter: int, device=None,
+                  seed: int = 0, std: float = 0.02) -> "ExpertBank":
+        """Seeded synthetic bank built on the device: weights ~ N(0, std)
+        from a torch generator seeded with seed*1e6 + 1000*layer + expert
+        (+0 up, +500 down), quantised by ``quantize_nvfp4_torch``."""
+        bank = cls(n_layers, n_experts, hidden, inter, device)
+        gen = torch.Generator(device=bank.device)
+        for layer in range(n_layers):
+            for e in range(n_experts):
+                recs = []
+                for off, (r, c) in ((0, (inter, hidden)), (500, (hidden, inter))):
+                    gen.manual_seed(seed * 1_000_000 + 1000 * layer + e + off)
+                    w = torch.randn(r, c, generator=gen, device=bank.device) * std
+                    recs.append(quantize_nvfp4_torch(w))
+                bank.upload_expert(layer, e, recs[0], recs[1])
+        torch.cuda.synchronize(bank.device)
+        return bank
+
+
+class MoEDecoder:
+    """Routed MoE layers of one token on a resident ``ExpertBank``."""
+
+    def __init__(self, bank: ExpertBank, top_k: int, scaling: float = 1.0, fused=None,
+                 ep_ranks: int = 1, ep_rank: int = 0, group=None):
+        self.bank, self.top_k, self.scaling = bank, top_k, scaling
+        self.fused = fused or FusedNVFP4(device=bank.device)
+        self.ep_ranks, self.ep_rank, self.group = ep_ranks, ep_rank, group
+        d, L, k = bank.device, bank.n_layers, top_k
+        self.ids = torch.zeros(L, k, dtype=torch.int32, device=d)
+        self.w = torch.zeros(L, k, dtype=torch.float32, device=d)
+        self.act = torch.zeros(k * bank.inter, dtype=torch.float32, device=d)
+        self.gate_b = torch.zeros(bank.n_experts, dtype=torch.float32, device=d)
+        self.xs = [torch.zeros(bank.hidden, dtype=torch.float32, device=d) for _ in range(2)]
+        if ep_ranks > 1:
+            self.contrib = torch.zeros(k * bank.hidden, dtype=torch.float32, device=d)
+            self.gathered = torch.zeros(ep_ranks * k * bank.hidden, dtype=torch.float32, device=d)
+        self.graph = None
+
+    def _s(self) -> int:
+        return int(torch.cuda.current_stream(self.bank.device).cuda_stream)
+
+    def layer(self, l: int, x: torch.Tensor, rlog: torch.Tensor, out: torch.Tensor) -> None:
+        """out = x + sum_s w_s * down_{e_s}(relu2(up_{e_s}(x))) in route order."""
+        b, f, k = self.bank, self.fused, self.top_k
+        ids, w = self.ids[l], self.w[l]
+        f.route_topk(rlog, self.gate_b, ids, w, b.n_experts, k, self.scaling)
+        if self.ep_ranks == 1:
+            f.moe_up_grouped(b.up_codes[l], b.up_scales[l], b.up_code_bytes, b.up_scale_bytes, ids,
+                             b.globals[l], k, x, self.act, b.inter, b.hidden)
+            f.moe_down_routesum(b.dn_codes[l], b.dn_scales[l], b.dn_code_bytes, b.dn_scale_bytes,
+                                ids, b.globals[l], w, k, self.act, out, b.hidden, b.inter, resid=x)
+            return
+        import torch.distributed as dist
+
+        _lib.call("ervf_ep_expert_slots", ptr(b.up_codes[l]), ptr(b.up_scales[l]),
+                  int(b.up_code_bytes), int(b.up_scale_bytes), ptr(b.dn_codes[l]),
+                  ptr(b.dn_scales[l]), int(b.dn_code_bytes), int(b.dn_scale_bytes), ptr(ids),
+                  ptr(b.globals[l]), k, ptr(x), ptr(self.act), ptr(self.contrib), b.hidden, b.inter,
+                  self.ep_ranks, self.ep_rank, f._width(), self._s())
+        dist.all_gather_into_tensor(self.gathered, self.contrib, group=self.group)
+        _lib.call("ervf_ep_route_sum", ptr(self.gathered), ptr(ids), ptr(w), k, ptr(x), ptr(out),
+                  b.hidden, self.ep_ranks, self._s())
+
+    def step(self, x_in: torch.Tensor, rlogs: torch.Tensor) -> torch.Tensor:
+        """One decode token through all layers; rlogs f32[L][E]. Returns the
+        buffer holding x after the last layer."""
+        cur = x_in
+        for l in range(self.bank.n_layers):
+            nxt = self.xs[l & 1]
+            self.layer(l, cur, rlogs[l], nxt)
+            cur = nxt
+        return cur

@@ -1,0 +1,182 @@
+/*
+ * ervf_b200.h -- C ABI of the B200 (sm_100a) NVFP4 expert-GEMV path.
+ *
+ * Every entry point is extern "C", takes plain device pointers, sizes and a
+ * cudaStream_t passed as void*, launches asynchronously on that stream,
+ * allocates nothing and returns an int status (ERVF_OK or a negative
+ * ERVF_ERR_*).  Each one replaces a kernel / wrapper of kennydd001/ervf,
+ * cited as file:line of src/moe_lab/lightningstream_nemotron/.
+ *
+ * Numeric contract: the NVFP4 GEMV entry points return, bit for bit, what the
+ * reference's gemv_nvfp4_ervf kernel returns on the same bytes
+ * (fused_nvfp4.py:295-406), for every `width`; legacy_tree=1 returns what
+ * gemv_nvfp4_rows returns (fused_nvfp4.py:31-122).
+ *
+ * Shapes the reference silently assumed are checked here: cols % 16 == 0,
+ * codes 4-byte aligned, pointers non-null.
+ */
+#ifndef ERVF_B200_H
+#define ERVF_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ERVF_API __attribute__((visibility("default")))
+#else
+#define ERVF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ERVF_OK 0
+#define ERVF_ERR_NULL -1     /* a required pointer is NULL */
+#define ERVF_ERR_SHAPE -2    /* rows/cols/k outside what the kernels support */
+#define ERVF_ERR_ALIGN -3    /* a pointer or stride is misaligned */
+#define ERVF_ERR_LAUNCH -4   /* the CUDA launch failed */
+#define ERVF_ERR_TIMEOUT -5  /* a bounded device wait ran out (ervf_device_status) */
+#define ERVF_ERR_ARG -6      /* an argument value is invalid (width, batch, ...) */
+
+/* Library version, e.g. 100 for 0.1.0. */
+ERVF_API int ervf_version(void);
+
+/* Reads and clears the device-side error word of the current device
+ * (ERVF_OK or ERVF_ERR_TIMEOUT).  Synchronous. */
+ERVF_API int ervf_device_status(void);
+
+/* out[r] = op(sum_k dequant(W)[r,k] * x[k]) for one NVFP4 matrix.
+ * codes u8[rows][cols/2] (low nibble first), scales E4M3 u8[rows][cols/16],
+ * x f32[cols], out f32[rows].  op = relu(v)^2 if apply_relu2 else v*out_scale.
+ * width: 0 = B200 schedule, or 4/8/16/32 = the ERVF subwarp widths.
+ * Replaces gemv_nvfp4_ervf / gemv_nvfp4_rows and FusedNVFP4.gemv_into
+ * (fused_nvfp4.py:295-406, :31-122, :944-968). */
+ERVF_API int ervf_nvfp4_gemv(const uint8_t* codes, const uint8_t* scales, const float* x, float* out,
+                    float global_scale, int rows, int cols, int apply_relu2, float out_scale,
+                    int width, int legacy_tree, void* stream);
+
+/* Indirect form: codes = codes_base + slot_ptr[0]*code_stride, scales likewise,
+ * global scale = globals[id_ptr[0]*2 + gsel], all read on the device.
+ * Replaces gemv_nvfp4_ervf_ind / FusedNVFP4.gemv_ervf_indirect
+ * (fused_nvfp4.py:548-646, :817-830). */
+ERVF_API int ervf_nvfp4_gemv_ind(const uint8_t* codes_base, const uint8_t* scales_base,
+                        const int32_t* slot_ptr, const int32_t* id_ptr, const float* globals,
+                        int gsel, const float* x, float* out, int rows, int cols, int apply_relu2,
+                        float out_scale, size_t code_stride, size_t scale_stride, int width,
+                        void* stream);
+
+/* njobs (<= 16) same-shape NVFP4 GEMVs in one launch; the pointer arrays
+ * live in HOST memory.  Equal, per job, to ervf_nvfp4_gemv.  Replaces the
+ * per-expert gemv_into loop of the MoE layer (runtime.py:571-578). */
+ERVF_API int ervf_nvfp4_gemv_grouped(int njobs, const uint8_t* const* codes, const uint8_t* const* scales,
+                            const float* global_scales, const float* const* xs, float* const* outs,
+                            int rows, int cols, int apply_relu2, float out_scale, int width,
+                            void* stream);
+
+/* dst[i] = fmaf(src[i], weight, dst[i]).  Replaces weighted_accumulate /
+ * FusedNVFP4.accumulate_into (fused_nvfp4.py:125-133, :980-984). */
+ERVF_API int ervf_weighted_accumulate(float* dst, const float* src, float weight, int n, void* stream);
+
+/* Same with the weight read from device memory.  Replaces
+ * weighted_accumulate_ind (fused_nvfp4.py:736-744, :855-859). */
+ERVF_API int ervf_weighted_accumulate_ind(float* dst, const float* src, const float* w_ptr, int n,
+                                 void* stream);
+
+/* Routed up projections of one token, one launch: for s in [0, top_k),
+ * e = ids[s] (device), act[s*inter + r] = relu(up_e(x)[r])^2 with
+ * up_e = (up_codes + e*up_code_stride, up_scales + e*up_scale_stride,
+ * globals[e*2 + 1]).  Equal, per slot, to FusedNVFP4.gemv_into(...,
+ * apply_relu2=True) (fused_nvfp4.py:970-978, first half). */
+ERVF_API int ervf_moe_up_grouped(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
+                        size_t up_scale_stride, const int32_t* ids, const float* globals, int top_k,
+                        const float* x, float* act, int inter, int hidden, int width, void* stream);
+
+/* Routed down projections plus the route-order sum, one launch: for every
+ * output row r, acc = base ? base[r] : 0; for s = 0..top_k-1 in ROUTE order
+ * acc = fmaf(down_{ids[s]}(act[s])[r], route_w[s], acc); out[r] = resid ?
+ * resid[r] + acc : acc.  Equal to top_k down gemv_into calls followed by
+ * accumulate_into in route order (fused_nvfp4.py:970-984; route-order
+ * contract runtime.py:588-596), with no contribution buffer. */
+ERVF_API int ervf_moe_down_routesum(const uint8_t* dn_codes, const uint8_t* dn_scales,
+                           size_t dn_code_stride, size_t dn_scale_stride, const int32_t* ids,
+                           const float* globals, const float* route_w, int top_k, const float* act,
+                           const float* base, const float* resid, float* out, int hidden, int inter,
+                           int width, void* stream);
+
+/* Expert parallelism, per rank and layer: for the route slots whose expert
+ * this rank owns (ids[s] % ep_ranks == ep_rank, read on the device), act[s] =
+ * relu(up(x))^2 and contrib[s*hidden + r] = down(act[s])[r] (unweighted); the
+ * other slots are left untouched.  Two launches.  The reference is single-GPU
+ * only; this is the per-rank half of its routed block (fused_nvfp4.py:970-978)
+ * with the route-order sum deferred to ervf_ep_route_sum. */
+ERVF_API int ervf_ep_expert_slots(const uint8_t* up_codes, const uint8_t* up_scales,
+                                  size_t up_code_stride, size_t up_scale_stride,
+                                  const uint8_t* dn_codes, const uint8_t* dn_scales,
+                                  size_t dn_code_stride, size_t dn_scale_stride, const int32_t* ids,
+                                  const float* globals, int top_k, const float* x, float* act,
+                                  float* contrib, int hidden, int inter, int ep_ranks, int ep_rank,
+                                  int width, void* stream);
+
+/* After an all-gather of every rank's contrib buffer into
+ * gathered[ep_ranks][top_k][hidden]: out[r] = x[r] + acc with acc =
+ * fmaf(gathered[ids[s] % ep_ranks][s][r], route_w[s], acc) for s = 0..top_k-1
+ * from 0.0 (x may be NULL: out = acc).  Bit-identical to the single-GPU
+ * ervf_moe_down_routesum (route-order contract runtime.py:588-596). */
+ERVF_API int ervf_ep_route_sum(const float* gathered, const int32_t* ids, const float* route_w,
+                               int top_k, const float* x, float* out, int hidden, int ep_ranks,
+                               void* stream);
+
+/* The runtime's masked down path over one panel-major down record
+ * (runtime.py:34-52): panel_scan + gemv_down_masked_partial +
+ * reduce_partials, same order (fused_nvfp4.py:157-187, :225-271, :408-419,
+ * :902-942).  state buffers: masks u32[inter/16], plist i32[inter/16],
+ * pcount i32[1], nz i32[inter], nzc i32[1].  bank is a device or mapped host
+ * pointer. */
+ERVF_API int ervf_down_masked(float* out, const uint8_t* bank, const float* act, uint32_t* masks,
+                     int32_t* plist, int32_t* pcount, int32_t* nz, int32_t* nzc,
+                     float global_scale, int hidden, int inter, int nchunks, void* stream);
+
+/* Indirect form: bank = down_base + ids_s[0]*panel_bytes, global scale =
+ * globals[ids_s[0]*2 + 0].  Replaces down_masked_into_indirect
+ * (fused_nvfp4.py:832-853). */
+ERVF_API int ervf_down_masked_ind(float* out, const uint8_t* down_base, const int32_t* id_ptr,
+                         size_t panel_bytes, const float* globals, const float* act,
+                         uint32_t* masks, int32_t* plist, int32_t* pcount, int32_t* nz,
+                         int32_t* nzc, int hidden, int inter, int nchunks, void* stream);
+
+/* Row-major NVFP4 down record -> panel-major record (runtime.py:34-52). */
+ERVF_API int ervf_panel_major(const uint8_t* codes, const uint8_t* scales, uint8_t* block, int rows,
+                     int inter, void* stream);
+
+/* BF16 GEMV, batch 1..8: out[b*rows + r] = sum_k bf16(W[r,k]) * x[b*cols + k],
+ * bit-exact per column to gemv_bf16 (gpu_kernels.py:21-49) and
+ * GPUKernels.mv_bf16 (gpu_kernels.py:1549-1551).  cols % 8 == 0, W and x
+ * 16-byte aligned. */
+ERVF_API int ervf_bf16_gemv(const uint16_t* W, const float* x, float* out, int rows, int cols, int batch,
+                   void* stream);
+
+/* Device router head: replaces route_topk_f32 / FusedNVFP4.route_topk
+ * (fused_nvfp4.py:433-465, :797-801).  n <= 1024, top_k <= 64. */
+ERVF_API int ervf_route_topk(const float* rlog, const float* gate_b, int32_t* ids, float* w, int n,
+                    int top_k, float scaling, int bad_pick, void* stream);
+
+/* Device LRU slot assignment: replaces cache_assign / FusedNVFP4.cache_assign
+ * (fused_nvfp4.py:470-511, :803-808). */
+ERVF_API int ervf_cache_assign(int32_t* slot_of, int32_t* expert_of, int32_t* last_used, int32_t* state2,
+                      const int32_t* ids, int32_t* slots, int32_t* need, int32_t* stats2, int cap,
+                      int top_k, void* stream);
+
+/* Copies the records of missed route slots from the bank (device or mapped
+ * host) into cache slots: replaces cache_fetch / FusedNVFP4.cache_fetch
+ * (fused_nvfp4.py:516-543, :810-815). */
+ERVF_API int ervf_cache_fetch(const uint8_t* bank_c, const uint8_t* bank_s, uint8_t* cache_c,
+                     uint8_t* cache_s, const int32_t* ids, const int32_t* slots,
+                     const int32_t* need, size_t code_bytes, size_t scale_bytes, int top_k,
+                     void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ERVF_B200_H */

@@ -1,0 +1,121 @@
+"""Routed-expert block on the GPU: the fused expert (up -> relu^2 -> down),
+the route-order weighted sum, and the one-launch grouped forms, against the
+CPU oracle bit for bit (config 1 shape: hidden 2688, inter 1856, top-6)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import bits_equal, random_nvfp4, rel_l2, x_regime
+
+pytestmark = pytest.mark.gpu
+
+HIDDEN, INTER = 2688, 1856
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+@pytest.fixture(scope="module")
+def bank(cuda):
+    """8 experts, stacked like the resident bank: up row-major, down row-major."""
+    n = 8
+    ups = [random_nvfp4(INTER, HIDDEN, seed=1000 + e) for e in range(n)]
+    dns = [random_nvfp4(HIDDEN, INTER, seed=1500 + e) for e in range(n)]
+    globals_h = np.array([[d[2], u[2]] for u, d in zip(ups, dns)], np.float32)
+    return {
+        "ups": ups, "dns": dns, "globals": globals_h,
+        "up_c": _t(np.concatenate([u[0] for u in ups]), cuda),
+        "up_s": _t(np.concatenate([u[1] for u in ups]), cuda),
+        "dn_c": _t(np.concatenate([d[0] for d in dns]), cuda),
+        "dn_s": _t(np.concatenate([d[1] for d in dns]), cuda),
+        "g_d": _t(globals_h, cuda),
+    }
+
+
+def test_expert_matches_oracle(fused, oracle, bank, cuda):
+    x = x_regime(HIDDEN, "bf16", seed=1)
+    for e in (0, 5):
+        (uc, us, ug), (dc, ds, dg) = bank["ups"][e], bank["dns"][e]
+        act = torch.zeros(INTER, device=cuda)
+        out = torch.zeros(HIDDEN, device=cuda)
+        fused.expert(_t(uc, cuda), _t(us, cuda), ug, _t(dc, cuda), _t(ds, cuda), dg, _t(x, cuda),
+                     act, out, HIDDEN, INTER)
+        torch.cuda.synchronize()
+        want_act, want_out = oracle.expert(uc, us, ug, dc, ds, dg, x, HIDDEN, INTER)
+        assert bits_equal(act.cpu().numpy(), want_act)
+        assert bits_equal(out.cpu().numpy(), want_out)
+
+
+def test_accumulate_route_order(fused, oracle, cuda):
+    r = np.random.default_rng(3)
+    dst = r.standard_normal(HIDDEN).astype(np.float32)
+    d = _t(dst, cuda)
+    want = dst
+    for s in range(6):
+        src = r.standard_normal(HIDDEN).astype(np.float32)
+        w = np.float32(r.uniform(0.05, 0.4))
+        fused.accumulate_into(d, _t(src, cuda), float(w), HIDDEN)
+        want = oracle.weighted_accumulate(want, src, w)
+    torch.cuda.synchronize()
+    assert bits_equal(d.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("width", [0, 16, 4])
+def test_grouped_up_and_routesum_match_unfused(fused, oracle, bank, cuda, width):
+    k = 6
+    ids_h = np.array([3, 7, 0, 5, 1, 6], np.int32)
+    rlog = np.random.default_rng(5).standard_normal(8).astype(np.float32)
+    w_h = np.abs(rlog[:k]) / np.abs(rlog[:k]).sum()
+    w_h = w_h.astype(np.float32)
+    x = x_regime(HIDDEN, "bf16", seed=2)
+    base = x_regime(HIDDEN, "random", seed=4)
+    ids = _t(ids_h, cuda)
+    w = _t(w_h, cuda)
+    act = torch.zeros(k * INTER, device=cuda)
+    out = torch.zeros(HIDDEN, device=cuda)
+    fused.ervf_width = width
+    fused.moe_up_grouped(bank["up_c"], bank["up_s"], INTER * HIDDEN // 2, INTER * HIDDEN // 16,
+                         ids, bank["g_d"], k, _t(x, cuda), act, INTER, HIDDEN)
+    fused.moe_down_routesum(bank["dn_c"], bank["dn_s"], HIDDEN * INTER // 2, HIDDEN * INTER // 16,
+                            ids, bank["g_d"], w, k, act, out, HIDDEN, INTER, base=_t(base, cuda))
+    fused.ervf_width = 0
+    torch.cuda.synchronize()
+    experts = {e: (*bank["ups"][e], *bank["dns"][e]) for e in range(8)}
+    want = oracle.moe_block(x, experts, ids_h, w_h, HIDDEN, INTER, init=base)
+    assert bits_equal(out.cpu().numpy(), want)
+    # act slots are the unfused up GEMVs
+    for s, e in enumerate(ids_h):
+        uc, us, ug = bank["ups"][e]
+        a = oracle.nvfp4_gemv(uc, us, x, ug, INTER, HIDDEN, apply_relu2=True)
+        assert bits_equal(act[s * INTER:(s + 1) * INTER].cpu().numpy(), a)
+
+
+def test_routesum_residual_matches_f64(fused, oracle, bank, cuda):
+    """x + moe(x) against a float64 dequant reference (tolerance, not bits)."""
+    from ervf_b200.formats import dequantize
+
+    k = 6
+    ids_h = np.array([2, 4, 6, 1, 0, 3], np.int32)
+    w_h = np.full(k, 1.0 / k, np.float32)
+    x = x_regime(HIDDEN, "bf16", seed=7)
+    act = torch.zeros(k * INTER, device=cuda)
+    out = torch.zeros(HIDDEN, device=cuda)
+    xd = _t(x, cuda)
+    fused.moe_up_grouped(bank["up_c"], bank["up_s"], INTER * HIDDEN // 2, INTER * HIDDEN // 16,
+                         _t(ids_h, cuda), bank["g_d"], k, xd, act, INTER, HIDDEN)
+    fused.moe_down_routesum(bank["dn_c"], bank["dn_s"], HIDDEN * INTER // 2, HIDDEN * INTER // 16,
+                            _t(ids_h, cuda), bank["g_d"], _t(w_h, cuda), k, act, out, HIDDEN, INTER,
+                            resid=xd)
+    torch.cuda.synchronize()
+    ref = x.astype(np.float64).copy()
+    for s, e in enumerate(ids_h):
+        uc, us, ug = bank["ups"][e]
+        dc, ds, dg = bank["dns"][e]
+        h = dequantize(uc, us, ug, INTER, HIDDEN) @ x.astype(np.float64)
+        a = np.maximum(h, 0) ** 2
+        ref += float(w_h[s]) * (dequantize(dc, ds, dg, HIDDEN, INTER) @ a)
+    assert rel_l2(out.cpu().numpy(), ref) < 1e-5
