@@ -70,11 +70,23 @@ __host__ __device__ __forceinline__ float e2m1_value(uint32_t c) {
   return (c & 8u) ? -v : v;
 }
 
-// Two E2M1 codes of one byte to f16x2 (low nibble -> .x, high nibble -> .y)
-// with the sm_100a converter, then widened exactly to binary32.
-__device__ __forceinline__ float2 e2m1x2_to_f32x2(uint32_t byte) {
-  const __half2_raw h = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)byte, __NV_E2M1);
-  return __half22float2(__half2(h));
+// The eight E2M1 codes of one 32-bit word to four f16x2 (byte i -> h[i];
+// low nibble -> low half) with the sm_100a hardware converter
+// (cvt.rn.f16x2.e2m1x2, exact: every E2M1 value is an f16).
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t q, uint32_t (&h)[4]) {
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(q));
+}
+
+// f16x2 -> two binary32 (exact widening).
+__device__ __forceinline__ float2 f16x2_to_f32x2(uint32_t h) {
+  __half2_raw r;
+  r.x = (unsigned short)(h & 0xFFFFu);
+  r.y = (unsigned short)(h >> 16);
+  return __half22float2(__half2(r));
 }
 
 // ------------------------------------------------- packed fp32 arithmetic

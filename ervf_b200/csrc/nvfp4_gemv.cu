@@ -173,13 +173,17 @@ __device__ __forceinline__ void tile_coords(const GemvBatch& p, const TmaCfg& c,
 // (0,2), pair B = chains (1,3); both pairs use the scale pair (s_2u, s_2u+1).
 __device__ __forceinline__ void unit_fma(const uint4 q, const float2 s, const float2 (&xa)[8],
                                          const float2 (&xb)[8], float2& accA, float2& accB) {
+  uint32_t h0[4], h1[4], h2[4], h3[4];
+  e2m1x8_to_f16x2(q.x, h0);
+  e2m1x8_to_f16x2(q.y, h1);
+  e2m1x8_to_f16x2(q.z, h2);
+  e2m1x8_to_f16x2(q.w, h3);
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
-    const int sh = 8 * b;
-    const float2 e0 = e2m1x2_to_f32x2((q.x >> sh) & 0xFFu);
-    const float2 e2 = e2m1x2_to_f32x2((q.z >> sh) & 0xFFu);
-    const float2 e1 = e2m1x2_to_f32x2((q.y >> sh) & 0xFFu);
-    const float2 e3 = e2m1x2_to_f32x2((q.w >> sh) & 0xFFu);
+    const float2 e0 = f16x2_to_f32x2(h0[b]);
+    const float2 e2 = f16x2_to_f32x2(h2[b]);
+    const float2 e1 = f16x2_to_f32x2(h1[b]);
+    const float2 e3 = f16x2_to_f32x2(h3[b]);
     accA = fma2(mul2(make_float2(e0.x, e2.x), s), xa[2 * b], accA);
     accB = fma2(mul2(make_float2(e1.x, e3.x), s), xb[2 * b], accB);
     accA = fma2(mul2(make_float2(e0.y, e2.y), s), xa[2 * b + 1], accA);

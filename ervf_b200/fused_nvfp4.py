@@ -23,6 +23,8 @@ Differences a caller can observe:
 
 from __future__ import annotations
 
+import sys
+
 import numpy as np
 import torch
 
@@ -42,6 +44,22 @@ def ptr(a) -> int:
     if cai is not None:
         return int(cai["data"][0])
     raise TypeError(f"expected a CUDA tensor, CUDA array or int address, got {type(a)!r}")
+
+
+def current_stream(explicit, device) -> int:
+    """Stream handle for a launch: an explicit stream (torch / CuPy stream
+    object or raw handle), else CuPy's current stream when the caller runs
+    on CuPy (as the reference runtime does), else torch's current stream."""
+    if explicit is not None:
+        if hasattr(explicit, "cuda_stream"):
+            return int(explicit.cuda_stream)
+        if hasattr(explicit, "ptr"):
+            return int(explicit.ptr)
+        return int(explicit)
+    cp = sys.modules.get("cupy")
+    if cp is not None:
+        return int(cp.cuda.get_current_stream().ptr)
+    return int(torch.cuda.current_stream(device).cuda_stream)
 
 
 def _numel(a) -> int | None:
@@ -78,10 +96,7 @@ class FusedNVFP4:
 
     # ------------------------------------------------------------ plumbing
     def _s(self) -> int:
-        if self.stream is not None:
-            return ptr(self.stream) if not hasattr(self.stream, "cuda_stream") \
-                else int(self.stream.cuda_stream)
-        return int(torch.cuda.current_stream(self.device).cuda_stream)
+        return current_stream(self.stream, self.device)
 
     def _width(self) -> int:
         w = int(self.ervf_width)

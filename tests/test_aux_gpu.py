@@ -101,8 +101,9 @@ def test_masked_down_matches_oracle(fused, oracle, cuda, nchunks):
     # the device repack equals the oracle's restatement of down_panel_major
     blk = torch.zeros(bank.size, dtype=torch.uint8, device=cuda)
     from ervf_b200 import _lib
-    _lib.call("ervf_panel_major", _t(codes, cuda).data_ptr(), _t(scales, cuda).data_ptr(),
-              blk.data_ptr(), hidden, inter, torch.cuda.current_stream().cuda_stream)
+    cd, sd = _t(codes, cuda), _t(scales, cuda)  # alive until the launch has run
+    _lib.call("ervf_panel_major", cd.data_ptr(), sd.data_ptr(), blk.data_ptr(), hidden, inter,
+              torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     assert np.array_equal(blk.cpu().numpy(), bank)
     st = fused.alloc_masked_state(hidden, inter)

@@ -1,0 +1,58 @@
+"""The C-ABI library without a GPU: it loads, exports every entry point that
+include/ervf_b200.h declares (and ctypes knows them all), and rejects bad
+arguments before touching the device."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from ervf_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "ervf_b200.h"
+
+
+def declared():
+    return re.findall(r"^ERVF_API int (ervf_\w+)\(", HEADER.read_text(), flags=re.M)
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    assert len(names) >= 18 and len(set(names)) == len(names)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared():
+        assert hasattr(lib, name), name
+
+
+def test_binding_covers_header_exactly():
+    assert set(declared()) == set(_lib.SIGNATURES)
+
+
+def test_version():
+    assert _lib.load().ervf_version() == 100
+
+
+def test_null_and_shape_checks_need_no_device():
+    lib = _lib.load()
+    assert lib.ervf_nvfp4_gemv(None, None, None, None, 1.0, 8, 16, 0, 1.0, 0, 0, None) == _lib.ERR_NULL
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.addressof(buf)
+    # cols % 16 != 0 is rejected before any CUDA call
+    assert lib.ervf_nvfp4_gemv(p, p, p, p, 1.0, 8, 24, 0, 1.0, 0, 0, None) == _lib.ERR_SHAPE
+    assert lib.ervf_nvfp4_gemv(p, p, p, p, 1.0, 0, 16, 0, 1.0, 0, 0, None) == _lib.ERR_SHAPE
+    assert lib.ervf_bf16_gemv(p, p, p, 4, 12, 1, None) == _lib.ERR_SHAPE
+    assert lib.ervf_bf16_gemv(p, p, p, 4, 16, 9, None) == _lib.ERR_ARG
+    assert lib.ervf_route_topk(p, p, p, p, 2000, 6, 1.0, 0, None) == _lib.ERR_SHAPE
+    assert lib.ervf_weighted_accumulate(None, p, 1.0, 4, None) == _lib.ERR_NULL
+    assert lib.ervf_down_masked(p, p, p, p, p, p, p, p, 1.0, 2688, 1856, 0, None) == _lib.ERR_ARG
+
+
+def test_python_shim_raises_value_error():
+    with pytest.raises(ValueError):
+        _lib.call("ervf_nvfp4_gemv", None, None, None, None, 1.0, 8, 16, 0, 1.0, 0, 0, None)

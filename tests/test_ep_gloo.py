@@ -1,0 +1,133 @@
+"""Expert-parallel exchange on CPU ranks (gloo, world size 2): each rank
+computes only the slots of the experts it owns (oracle arithmetic), one
+all-gather, then the route-order sum -- bit-identical to one rank.  And a
+rank that dies before the collective makes the survivor fail fast instead of
+hanging."""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import sys
+import traceback
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parents[1]
+HIDDEN, INTER, K, E = 256, 128, 6, 12
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _experts():
+    sys.path.insert(0, str(ROOT / "tests"))
+    from conftest import random_nvfp4
+
+    out = {}
+    for e in range(E):
+        uc, us, ug = random_nvfp4(INTER, HIDDEN, seed=50 + e)
+        dc, ds, dg = random_nvfp4(HIDDEN, INTER, seed=90 + e)
+        out[e] = (uc, us, ug, dc, ds, dg)
+    return out
+
+
+def _worker(rank, world, port, mode, q):
+    try:
+        sys.path[:0] = [str(ROOT), str(ROOT / "oracle")]
+        import oracle
+
+        from ervf_b200 import ep
+
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=10))
+        experts = _experts()
+        r = np.random.default_rng(3)
+        x = r.standard_normal(HIDDEN).astype(np.float32)
+        results = []
+        for layer in range(3):
+            rlog = r.standard_normal(E).astype(np.float32)
+            ids, w = oracle.route_topk(rlog, np.zeros(E, np.float32), K)
+            if mode == "die" and rank == 1 and layer == 1:
+                os._exit(3)  # leaves between steps, nothing in flight
+            contrib = np.zeros((K, HIDDEN), np.float32)
+            for s in ep.owned_slots(ids, world, rank):
+                uc, us, ug, dc, ds, dg = experts[int(ids[s])]
+                _, contrib[s] = oracle.expert(uc, us, ug, dc, ds, dg, x, HIDDEN, INTER)
+            gathered = torch.zeros(world * K * HIDDEN)
+            dist.all_gather_into_tensor(gathered, torch.from_numpy(contrib.reshape(-1)))
+            g = gathered.numpy()
+            acc = np.zeros(HIDDEN, np.float32)
+            for s in range(K):
+                o = ep.gathered_index(ids, s, world, K, HIDDEN)
+                acc = oracle.weighted_accumulate(acc, g[o:o + HIDDEN], w[s])
+            x = (x + acc).astype(np.float32)
+            results.append(x.copy())
+        q.put((rank, "ok", np.stack(results)))
+        dist.destroy_process_group()
+    except Exception as exc:  # noqa: BLE001
+        q.put((rank, "error", f"{type(exc).__name__}: {exc}\n{traceback.format_exc()[-400:]}"))
+
+
+def _single():
+    sys.path[:0] = [str(ROOT), str(ROOT / "oracle")]
+    import oracle
+
+    experts = _experts()
+    r = np.random.default_rng(3)
+    x = r.standard_normal(HIDDEN).astype(np.float32)
+    out = []
+    for layer in range(3):
+        rlog = r.standard_normal(E).astype(np.float32)
+        ids, w = oracle.route_topk(rlog, np.zeros(E, np.float32), K)
+        x = (x + oracle.moe_block(x, experts, ids, w, HIDDEN, INTER)).astype(np.float32)
+        out.append(x.copy())
+    return np.stack(out)
+
+
+def _run(mode, world=2, wait=60):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = {}
+    for p in ps:
+        p.join(wait)
+    while not q.empty():
+        rank, status, payload = q.get()
+        res[rank] = (status, payload)
+    for p in ps:
+        if p.is_alive():
+            p.kill()
+    return res, [p.exitcode for p in ps]
+
+
+def test_ep_exchange_is_bit_identical_to_one_rank(oracle):
+    res, codes = _run("ok")
+    want = _single()
+    assert codes == [0, 0]
+    for rank in (0, 1):
+        status, got = res[rank]
+        assert status == "ok", got
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_dead_rank_is_detected_by_collective_timeout(oracle):
+    res, codes = _run("die")
+    assert codes[1] == 3
+    status, msg = res.get(0, ("missing", ""))
+    assert status == "error", (status, msg)

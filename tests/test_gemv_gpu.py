@@ -77,7 +77,7 @@ def test_gemv_out_scale_and_nan_scales(fused, oracle, cuda):
 def test_legacy_tree_differs_only_in_zero_sign(fused, oracle, cuda):
     # tiny products underflow to -0.0 chains; the legacy combine turns an
     # all -0.0 row into +0.0, ERVF keeps -0.0 (fused_nvfp4.py:107-112 vs :397-403)
-    rows, cols = 16, 256
+    rows, cols = 16, 2048  # every one of the 256 chains has work
     codes = np.full(rows * cols // 2, 0x99, np.uint8)  # -0.5 codes
     scales = np.full(rows * cols // 16, 0x01, np.uint8)  # 2^-9
     x = np.full(cols, 1e-40, np.float32)

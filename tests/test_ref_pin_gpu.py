@@ -73,7 +73,8 @@ def test_bf16_oracle_equals_reference(ref, oracle, cuda):
     W = W.astype(np.uint16)
     x = r.standard_normal(cols).astype(np.float32)
     out = torch.zeros(rows, device=cuda)
-    ref.call("ref_gemv_bf16", _t(W, cuda).data_ptr(), _t(x, cuda).data_ptr(), out.data_ptr(),
+    Wd, xd = _t(W, cuda), _t(x, cuda)
+    ref.call("ref_gemv_bf16", Wd.data_ptr(), xd.data_ptr(), out.data_ptr(),
              rows, cols, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     assert bits_equal(out.cpu().numpy(), oracle.bf16_gemv(W, x, rows, cols)[0])
@@ -107,7 +108,8 @@ def test_router_and_lru_oracle_equal_reference(ref, oracle, cuda):
         bias = np.zeros(n, np.float32)
         ids = torch.zeros(k, dtype=torch.int32, device=cuda)
         w = torch.zeros(k, device=cuda)
-        ref.call("ref_route_topk", _t(rlog, cuda).data_ptr(), _t(bias, cuda).data_ptr(),
+        rlog_d, bias_d = _t(rlog, cuda), _t(bias, cuda)  # keep alive across the launch
+        ref.call("ref_route_topk", rlog_d.data_ptr(), bias_d.data_ptr(),
                  ids.data_ptr(), w.data_ptr(), n, k, 1.0, 0, torch.cuda.current_stream().cuda_stream)
         torch.cuda.synchronize()
         oid, ow = oracle.route_topk(rlog, bias, k)
