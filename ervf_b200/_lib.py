@@ -20,6 +20,9 @@ ERR_LAUNCH = -4
 ERR_TIMEOUT = -5
 ERR_ARG = -6
 
+LAUNCH_PDL = 1
+LAUNCH_IDS_READY = 2
+
 _NAMES = {
     ERR_NULL: "null pointer",
     ERR_SHAPE: "unsupported shape",
@@ -43,9 +46,11 @@ SIGNATURES: dict[str, list] = {
     "ervf_nvfp4_gemv_grouped": [_i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _vp],
     "ervf_weighted_accumulate": [_vp, _vp, _f, _i, _vp],
     "ervf_weighted_accumulate_ind": [_vp, _vp, _vp, _i, _vp],
-    "ervf_moe_up_grouped": [_vp, _vp, _sz, _sz, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _vp],
+    "ervf_moe_up_grouped": [_vp, _vp, _sz, _sz, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _vp],
     "ervf_moe_down_routesum": [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i,
-                               _i, _vp],
+                               _vp, _sz, _i, _i, _vp],
+    "ervf_routesum_scratch_bytes": [_i, _i],
+    "ervf_route_topk_batched": [_vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp],
     "ervf_ep_expert_slots": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _i, _vp, _vp, _vp,
                              _i, _i, _i, _i, _i, _vp],
     "ervf_ep_route_sum": [_vp, _vp, _vp, _i, _vp, _vp, _i, _i, _vp],
@@ -57,6 +62,8 @@ SIGNATURES: dict[str, list] = {
     "ervf_cache_assign": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp],
     "ervf_cache_fetch": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _i, _vp],
 }
+
+SIZE_RESULT = {"ervf_routesum_scratch_bytes"}
 
 _lib = None
 
@@ -79,7 +86,7 @@ def load():
         for name, argtypes in SIGNATURES.items():
             fn = getattr(lib, name)
             fn.argtypes = argtypes
-            fn.restype = ctypes.c_int
+            fn.restype = ctypes.c_size_t if name in SIZE_RESULT else ctypes.c_int
         _lib = lib
     return _lib
 

@@ -9,6 +9,9 @@ namespace ervf {
 
 int launch_route_topk(const float* rlog, const float* gate_b, int* ids, float* w, int n, int top_k,
                       float scaling, int bad_pick, cudaStream_t stream);
+int launch_route_topk_batched(const float* rlog, const float* gate_b, int* ids, float* w, int layers,
+                              int n, int top_k, float scaling, int bad_pick, int bias_stride,
+                              cudaStream_t stream);
 int launch_cache_assign(int* slot_of, int* expert_of, int* last_used, int* state2, const int* ids,
                         int* slots, int* need, int* stats2, int cap, int top_k, cudaStream_t stream);
 int launch_cache_fetch(const uint8_t* bank_c, const uint8_t* bank_s, uint8_t* cache_c, uint8_t* cache_s,

@@ -132,7 +132,8 @@ int ervf_weighted_accumulate_ind(float* dst, const float* src, const float* w_pt
 
 int ervf_moe_up_grouped(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
                         size_t up_scale_stride, const int32_t* ids, const float* globals, int top_k,
-                        const float* x, float* act, int inter, int hidden, int width, void* stream) {
+                        const float* x, float* act, int inter, int hidden, int width, int flags,
+                        void* stream) {
   if (!up_codes || !up_scales || !ids || !globals || !x || !act) return kErrNull;
   if (top_k <= 0 || top_k > kMaxJobs) return kErrShape;
   if (int e = check_nvfp4_shape(inter, hidden, width)) return e;
@@ -143,6 +144,8 @@ int ervf_moe_up_grouped(const uint8_t* up_codes, const uint8_t* up_scales, size_
   b.njobs = top_k;
   b.relu2 = 1;
   b.out_scale = 1.0f;
+  b.pdl = (flags & ERVF_LAUNCH_PDL) ? 1 : 0;
+  b.ids_ready = (flags & ERVF_LAUNCH_IDS_READY) ? 1 : 0;
   for (int s = 0; s < top_k; ++s) {
     MatRef m{};
     m.codes = up_codes;
@@ -164,8 +167,10 @@ int ervf_moe_down_routesum(const uint8_t* dn_codes, const uint8_t* dn_scales,
                            size_t dn_code_stride, size_t dn_scale_stride, const int32_t* ids,
                            const float* globals, const float* route_w, int top_k, const float* act,
                            const float* base, const float* resid, float* out, int hidden, int inter,
-                           int width, void* stream) {
+                           void* scratch, size_t scratch_bytes, int width, int flags, void* stream) {
   if (!dn_codes || !dn_scales || !ids || !globals || !route_w || !act || !out) return kErrNull;
+  if (scratch && (scratch_bytes < routesum_scratch_bytes(hidden, top_k) || !al(scratch, 16)))
+    return kErrArg;
   if (top_k <= 0 || top_k > kMaxJobs) return kErrShape;
   if (int e = check_nvfp4_shape(hidden, inter, width)) return e;
   if (!al(dn_codes, 4) || (dn_code_stride & 3) || !al(act, 4) || !al(out, 4)) return kErrAlign;
@@ -179,6 +184,12 @@ int ervf_moe_down_routesum(const uint8_t* dn_codes, const uint8_t* dn_scales,
   b.base = base;
   b.resid = resid;
   b.rs_out = out;
+  if (scratch) {
+    b.contrib = reinterpret_cast<float*>(scratch);
+    b.row_count = reinterpret_cast<int*>(b.contrib + (size_t)top_k * hidden);
+  }
+  b.pdl = (flags & ERVF_LAUNCH_PDL) ? 1 : 0;
+  b.ids_ready = (flags & ERVF_LAUNCH_IDS_READY) ? 1 : 0;
   for (int s = 0; s < top_k; ++s) {
     MatRef m{};
     m.codes = dn_codes;
@@ -194,6 +205,11 @@ int ervf_moe_down_routesum(const uint8_t* dn_codes, const uint8_t* dn_scales,
     b.job[s].out = nullptr;
   }
   return launch_nvfp4_batch(b, width, S(stream));
+}
+
+size_t ervf_routesum_scratch_bytes(int hidden, int top_k) {
+  if (hidden <= 0 || top_k <= 0) return 0;
+  return routesum_scratch_bytes(hidden, top_k);
 }
 
 int ervf_ep_expert_slots(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
@@ -301,6 +317,17 @@ int ervf_route_topk(const float* rlog, const float* gate_b, int32_t* ids, float*
   if (!rlog || !gate_b || !ids || !w) return kErrNull;
   if (n <= 0 || n > 1024 || top_k <= 0 || top_k > 64 || top_k > n) return kErrShape;
   return launch_route_topk(rlog, gate_b, ids, w, n, top_k, scaling, bad_pick, S(stream));
+}
+
+int ervf_route_topk_batched(const float* rlog, const float* gate_b, int32_t* ids, float* w,
+                            int layers, int n, int top_k, float scaling, int bad_pick,
+                            int bias_stride, void* stream) {
+  if (!rlog || !ids || !w) return kErrNull;
+  if (layers <= 0 || n <= 0 || n > 1024 || top_k <= 0 || top_k > 64 || top_k > n || bias_stride < 0)
+    return kErrShape;
+  if (n > 256 && !gate_b) return kErrNull;
+  return launch_route_topk_batched(rlog, gate_b, ids, w, layers, n, top_k, scaling, bad_pick,
+                                   bias_stride, S(stream));
 }
 
 int ervf_cache_assign(int32_t* slot_of, int32_t* expert_of, int32_t* last_used, int32_t* state2,

@@ -83,10 +83,53 @@ __device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t q, uint32_t (&h)[4]) {
 
 // f16x2 -> two binary32 (exact widening).
 __device__ __forceinline__ float2 f16x2_to_f32x2(uint32_t h) {
-  __half2_raw r;
-  r.x = (unsigned short)(h & 0xFFFFu);
-  r.y = (unsigned short)(h >> 16);
-  return __half22float2(__half2(r));
+  float2 r;
+  asm("{\n .reg .b16 lo, hi;\n mov.b32 {lo, hi}, %2;\n cvt.f32.f16 %0, lo;\n cvt.f32.f16 %1, hi;\n}"
+      : "=f"(r.x), "=f"(r.y)
+      : "r"(h));
+  return r;
+}
+
+// Two E4M3 block-scale bytes (low byte first) as binary32 with the device
+// table's NaN -> +0.0 rule: hardware e4m3x2 -> f16x2 (exact), f16 -> f32
+// (exact).  The bytes 0x7F / 0xFF (NaN) are cleared to 0x00 first.
+__device__ __forceinline__ float2 e4m3x2_to_f32x2(uint32_t sv) {
+  // a byte is NaN iff its low 7 bits are all ones
+  const uint32_t nan = ((sv & 0x7F7Fu) + 0x0101u) & 0x8080u;
+  const uint32_t keep = ~((nan >> 7) * 0xFFu);  // 0x00 over NaN bytes
+  const uint16_t v = (uint16_t)(sv & keep & 0xFFFFu);
+  float2 r;
+  asm("{\n .reg .b32 h;\n .reg .b16 lo, hi;\n cvt.rn.f16x2.e4m3x2 h, %2;\n mov.b32 {lo, hi}, h;\n"
+      " cvt.f32.f16 %0, lo;\n cvt.f32.f16 %1, hi;\n}"
+      : "=f"(r.x), "=f"(r.y)
+      : "h"(v));
+  return r;
+}
+
+// The eight E2M1 codes of a 32-bit word (code i = nibble i, low first) as
+// exact binary32 values f[0..7]: hardware e2m1x2 -> f16x2, then f16 -> f32.
+__device__ __forceinline__ void e2m1x8_to_f32(uint32_t q, float (&f)[8]) {
+  asm("{\n"
+      " .reg .b8 b0, b1, b2, b3;\n"
+      " .reg .b32 h0, h1, h2, h3;\n"
+      " .reg .b16 l0, u0, l1, u1, l2, u2, l3, u3;\n"
+      " mov.b32 {b0, b1, b2, b3}, %8;\n"
+      " cvt.rn.f16x2.e2m1x2 h0, b0;\n"
+      " cvt.rn.f16x2.e2m1x2 h1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 h2, b2;\n"
+      " cvt.rn.f16x2.e2m1x2 h3, b3;\n"
+      " mov.b32 {l0, u0}, h0;\n"
+      " mov.b32 {l1, u1}, h1;\n"
+      " mov.b32 {l2, u2}, h2;\n"
+      " mov.b32 {l3, u3}, h3;\n"
+      " cvt.f32.f16 %0, l0;\n cvt.f32.f16 %1, u0;\n"
+      " cvt.f32.f16 %2, l1;\n cvt.f32.f16 %3, u1;\n"
+      " cvt.f32.f16 %4, l2;\n cvt.f32.f16 %5, u2;\n"
+      " cvt.f32.f16 %6, l3;\n cvt.f32.f16 %7, u3;\n"
+      "}"
+      : "=f"(f[0]), "=f"(f[1]), "=f"(f[2]), "=f"(f[3]), "=f"(f[4]), "=f"(f[5]), "=f"(f[6]),
+        "=f"(f[7])
+      : "r"(q));
 }
 
 // ------------------------------------------------- packed fp32 arithmetic
@@ -176,6 +219,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
   return ok != 0;
 }
+
+// Non-blocking probe: has the phase with this parity completed?
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ void nanosleep_ns(uint32_t ns) { asm volatile("nanosleep.u32 %0;" ::"r"(ns)); }
 
 // Bounded wait: gives up after ~`budget` cycles, records kErrTimeout in the
 // device error word and returns false.  A wait that completes returns true.

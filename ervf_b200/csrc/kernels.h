@@ -50,7 +50,25 @@ struct GemvBatch {
   // expert ep_ids[j], i.e. ep_ids[j] % ep_ranks == ep_rank (read on device).
   const int* ep_ids;
   int ep_ranks, ep_rank;
+  // Launch with programmatic stream serialisation (PDL): the kernel may start
+  // while its predecessor drains; it waits (griddepcontrol.wait) before it
+  // reads activations.  ids_ready: the slot / id tables and globals were
+  // written by a kernel that finished before the predecessor started, so
+  // weight streaming may begin before the wait.
+  int pdl;
+  int ids_ready;
+  // mode 1 scratch on the TMA schedule: contrib[njobs][rows] fp32 and
+  // row_count[rows] int32 (all zero before the first call; every call leaves
+  // them zero).  Each job's row sums land in contrib; the last job to finish a
+  // row adds the row up in route order.  NULL: the width schedules are used.
+  float* contrib;
+  int* row_count;
 };
+
+// Scratch bytes the routed-sum launch needs: contrib + row counters.
+inline size_t routesum_scratch_bytes(int rows, int njobs) {
+  return (size_t)njobs * rows * sizeof(float) + (size_t)rows * sizeof(int);
+}
 
 __host__ __device__ inline bool job_active(const GemvBatch& b, int job) {
 #ifdef __CUDA_ARCH__

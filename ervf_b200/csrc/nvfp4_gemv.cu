@@ -145,97 +145,121 @@ __global__ void __launch_bounds__(256) nvfp4_gemv_sched(GemvBatch p, int tiles_p
 // ======================================================================
 // TMA-staged B200 schedule
 // ======================================================================
+//
+// CTA = 4 consumer warps + 1 producer warp, three CTAs per SM.  A work item
+// is a block of kRt rows of one job; the items of a launch (job-major) are
+// dealt to the CTAs round-robin.
+//
+// Producer warp: bulk-copies an item's codes and scale bytes into a free
+// stage and, when the job's activation differs per item (mode 1), copies the
+// activation into the stage in a rotated layout (float4 i of unit u at slot
+// (i + u) & 7) so that the consumers of eight consecutive units read eight
+// different bank groups.
+//
+// Consumer thread (row_off, c): chain group c = reference chains 4c..4c+3,
+// i.e. one 16-byte code unit per round, for rows row_off, row_off + p_rows,
+// ... of the item, activation of its columns in registers.  Codes are decoded
+// with the hardware e2m1x2 converter; each weight is w = RN(e2m1 * s) (FMUL)
+// and acc = fmaf(w, x, acc) (FFMA), in the reference's order.  Chain values
+// go to shared memory; after a consumer barrier two warps run the 256-leaf
+// tree of the item's rows.
+//
+// mode 1 (routed sum): a tree thread writes its row's job output y_s to
+// contrib[s][row], publishes it with a release fence and a per-row atomic
+// count, and the thread that completes a row's count adds the row up in
+// ROUTE order, acc = fmaf(y_s, w_s, acc) for s = 0..njobs-1, writes x + acc
+// and resets the count.  Rows therefore spread over all CTAs, and the sum is
+// the same as one thread walking the slots in order.
+
+constexpr int kRt = 8;  // rows per item
 
 struct TmaCfg {
-  int rt;           // rows per sub-tile
   int stages;
   int stage_bytes;  // bytes per stage (128-aligned)
-  int scale_off;    // offset of scales inside a stage
-  int x_off;        // offset of the activation inside a stage (stage_x)
-  int stage_x;      // 1: the activation travels with each sub-tile (mode 1)
+  int scale_off;    // scale bytes inside a stage
+  int x_off;        // mode 1: rotated activation inside a stage
+  int part_off;     // chain buffers [2][kRt][kRowPitch] floats
+  int stage_base;
   int n_u, gw, p_rows;
-  int tiles_per_job, ntiles, nsub;
+  int tiles_per_job;  // row blocks per job
+  int ntiles;         // njobs * tiles_per_job
+  int stage_x;        // 1: the activation travels with each item (mode 1)
 };
 
-__device__ __forceinline__ void tile_coords(const GemvBatch& p, const TmaCfg& c, int T, int sub,
-                                            int& job, int& r0, int& nrows) {
-  if (p.mode == 0) {
-    job = T / c.tiles_per_job;
-    r0 = (T % c.tiles_per_job) * c.rt;
-  } else {
-    job = sub;
-    r0 = T * c.rt;
-  }
-  nrows = min(c.rt, p.rows - r0);
+__device__ __forceinline__ void item_of(const TmaCfg& c, int T, int& job, int& rb) {
+  job = T / c.tiles_per_job;
+  rb = T - job * c.tiles_per_job;
 }
 
-// One 16-byte code unit (4 chains x 8 codes) of one row.  Pair A = chains
-// (0,2), pair B = chains (1,3); both pairs use the scale pair (s_2u, s_2u+1).
-__device__ __forceinline__ void unit_fma(const uint4 q, const float2 s, const float2 (&xa)[8],
-                                         const float2 (&xb)[8], float2& accA, float2& accB) {
-  uint32_t h0[4], h1[4], h2[4], h3[4];
-  e2m1x8_to_f16x2(q.x, h0);
-  e2m1x8_to_f16x2(q.y, h1);
-  e2m1x8_to_f16x2(q.z, h2);
-  e2m1x8_to_f16x2(q.w, h3);
-#pragma unroll
-  for (int b = 0; b < 4; ++b) {
-    const float2 e0 = f16x2_to_f32x2(h0[b]);
-    const float2 e2 = f16x2_to_f32x2(h2[b]);
-    const float2 e1 = f16x2_to_f32x2(h1[b]);
-    const float2 e3 = f16x2_to_f32x2(h3[b]);
-    accA = fma2(mul2(make_float2(e0.x, e2.x), s), xa[2 * b], accA);
-    accB = fma2(mul2(make_float2(e1.x, e3.x), s), xb[2 * b], accB);
-    accA = fma2(mul2(make_float2(e0.y, e2.y), s), xa[2 * b + 1], accA);
-    accB = fma2(mul2(make_float2(e1.y, e3.y), s), xb[2 * b + 1], accB);
-  }
-}
-
-// Activation columns of unit u as the chain pairs use them:
-// xa[m] = (x[32u+m], x[32u+16+m]), xb[m] = (x[32u+8+m], x[32u+24+m]).
-__device__ __forceinline__ void load_x_unit(const float* __restrict__ x, int u, float2 (&xa)[8],
-                                            float2 (&xb)[8]) {
-  const float4* p = reinterpret_cast<const float4*>(x + 32 * u);
-  float v[32];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float4 f = p[i];
-    v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
-  }
+// One 16-byte code unit (4 chains x 8 codes) of one row.  Chains 0,1 use the
+// block scale s0 = s_2u, chains 2,3 use s1 = s_2u+1; xr[8j + m] is the
+// activation of chain j's m-th code.
+__device__ __forceinline__ void unit_fma(const uint4 q, const float s0, const float s1,
+                                         const float (&xr)[32], float (&acc)[4]) {
+  float f0[8], f1[8], f2[8], f3[8];
+  e2m1x8_to_f32(q.x, f0);
+  e2m1x8_to_f32(q.y, f1);
+  e2m1x8_to_f32(q.z, f2);
+  e2m1x8_to_f32(q.w, f3);
 #pragma unroll
   for (int m = 0; m < 8; ++m) {
-    xa[m] = make_float2(v[m], v[16 + m]);
-    xb[m] = make_float2(v[8 + m], v[24 + m]);
+    acc[0] = fmaf(f0[m] * s0, xr[m], acc[0]);
+    acc[1] = fmaf(f1[m] * s0, xr[8 + m], acc[1]);
+    acc[2] = fmaf(f2[m] * s1, xr[16 + m], acc[2]);
+    acc[3] = fmaf(f3[m] * s1, xr[24 + m], acc[3]);
   }
+}
+
+__device__ __forceinline__ void unpack_x(const float4 (&v4)[8], float (&xr)[32]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    xr[4 * i] = v4[i].x; xr[4 * i + 1] = v4[i].y; xr[4 * i + 2] = v4[i].z; xr[4 * i + 3] = v4[i].w;
+  }
+}
+
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 template <int ROUNDS>
-__global__ void __launch_bounds__(288, 1) nvfp4_gemv_tma(GemvBatch p, TmaCfg c) {
+__global__ void __launch_bounds__(160, 3) nvfp4_gemv_tma(GemvBatch p, TmaCfg c) {
   extern __shared__ __align__(128) uint8_t smem[];
-  const int NC = blockDim.x - 32;  // consumer threads
+  constexpr int NC = 128;  // consumer threads
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int S = c.stages;
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + S;
-  float* luts = reinterpret_cast<float*>(smem + 128);
-  float* part = luts + p.njobs * 256;                    // [2][rt][kRowPitch]
-  uint8_t* stages = reinterpret_cast<uint8_t*>(part + 2 * c.rt * kRowPitch);
+  const uint8_t** jc = reinterpret_cast<const uint8_t**>(smem + 128);
+  const uint8_t** js = jc + kMaxJobs;
+  float* jg = reinterpret_cast<float*>(js + kMaxJobs);
+  float* luts = reinterpret_cast<float*>(smem + 448);  // [njobs][256]
+  float* part = reinterpret_cast<float*>(smem + c.part_off);
+  uint8_t* stages = smem + c.stage_base;
 
   if (tid == 0) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(&full[i], 1);
+      mbar_init(&full[i], c.stage_x ? 2 : 1);
       mbar_init(&empty[i], NC / 32);
     }
     fence_mbar_init();
   }
-  for (int i = tid; i < p.njobs * 256; i += blockDim.x) {
+  for (int i = tid; i < 2 * kRt * kRowPitch; i += blockDim.x) part[i] = 0.0f;
+  // Slot / id tables and globals: readable now if they were produced before
+  // the predecessor kernel, otherwise only after the dependency wait.
+  if (!p.ids_ready) grid_dep_wait();
+  if (tid < p.njobs) {
     const uint8_t *cc, *ss;
     float g;
-    resolve(p.job[i >> 8].mat, cc, ss, g);
-    luts[i] = e4m3_lut_value((uint32_t)(i & 255)) * g;
+    resolve(p.job[tid].mat, cc, ss, g);
+    jc[tid] = cc;
+    js[tid] = ss;
+    jg[tid] = g;
   }
-  for (int i = tid; i < 2 * c.rt * kRowPitch; i += blockDim.x) part[i] = 0.0f;
+  __syncthreads();
+  for (int i = tid; i < p.njobs * 256; i += blockDim.x)
+    luts[i] = e4m3_lut_value((uint32_t)(i & 255)) * jg[i >> 8];
   __syncthreads();
 
   const int cols = p.cols;
@@ -243,117 +267,150 @@ __global__ void __launch_bounds__(288, 1) nvfp4_gemv_tma(GemvBatch p, TmaCfg c) 
 
   // ------------------------------------------------------------ producer
   if (warp == NC / 32) {
-    if (lane == 0) {
-      int it = 0;
-      bool ok = true;
-      for (int T = blockIdx.x; ok && T < c.ntiles; T += gridDim.x) {
-        for (int sub = 0; sub < c.nsub; ++sub) {
-          int job, r0, nrows;
-          tile_coords(p, c, T, sub, job, r0, nrows);
-          if (!job_active(p, job)) continue;
-          const int st = it % S;
-          if (!mbar_wait(&empty[st], ((it / S) & 1) ^ 1)) { ok = false; break; }
-          ++it;
-          const uint8_t *cc, *ss;
-          float g;
-          resolve(p.job[job].mat, cc, ss, g);
-          uint8_t* dst = stages + (size_t)st * c.stage_bytes;
-          const uint32_t code_bytes = (uint32_t)(nrows * cb);
-          const uint32_t scale_bytes = (uint32_t)(nrows * sb);
-          const uint32_t s16 = scale_bytes & ~15u;
-          const uint8_t* ssrc = ss + (size_t)r0 * sb;
-          for (uint32_t i = s16; i < scale_bytes; ++i) dst[c.scale_off + i] = ssrc[i];
-          const uint32_t xbytes = c.stage_x ? (uint32_t)(cols * 4) : 0u;
-          mbar_arrive_expect_tx(&full[st], code_bytes + s16 + xbytes);
-          bulk_g2s(dst, cc + (size_t)r0 * cb, code_bytes, &full[st]);
-          if (s16) bulk_g2s(dst + c.scale_off, ssrc, s16, &full[st]);
-          if (xbytes) bulk_g2s(dst + c.x_off, p.job[job].x, xbytes, &full[st]);
-        }
+    int it = 0;
+    bool waited = false;
+    for (int T = blockIdx.x; T < c.ntiles; T += gridDim.x) {
+      int job, rb;
+      item_of(c, T, job, rb);
+      if (!job_active(p, job)) continue;
+      const int st = it % S;
+      if (!mbar_wait(&empty[st], ((it / S) & 1) ^ 1)) break;
+      ++it;
+      const int r0 = rb * kRt;
+      const int nrows = min(kRt, p.rows - r0);
+      uint8_t* dst = stages + (size_t)st * c.stage_bytes;
+      if (lane == 0) {
+        const uint32_t code_bytes = (uint32_t)(nrows * cb);
+        const uint32_t scale_bytes = (uint32_t)(nrows * sb);
+        const uint32_t s16 = scale_bytes & ~15u;
+        const uint8_t* ssrc = js[job] + (size_t)r0 * sb;
+        for (uint32_t i = s16; i < scale_bytes; ++i) dst[c.scale_off + i] = ssrc[i];
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive_expect_tx(&full[st], code_bytes + s16);
+        bulk_g2s(dst, jc[job] + (size_t)r0 * cb, code_bytes, &full[st]);
+        if (s16) bulk_g2s(dst + c.scale_off, ssrc, s16, &full[st]);
       }
-      // Leave no bulk copy in flight: wait (bounded) for the last issued stages.
-      for (int k = (it > S ? it - S : 0); k < it; ++k) mbar_wait(&full[k % S], (k / S) & 1);
+      if (c.stage_x) {
+        if (!waited) { grid_dep_wait(); waited = true; }
+        const float4* src = reinterpret_cast<const float4*>(p.job[job].x);
+        float4* xs = reinterpret_cast<float4*>(dst + c.x_off);
+        for (int f = lane; f < (cols >> 2); f += 32) {
+          const int u = f >> 3, i = f & 7;
+          xs[u * 8 + ((i + u) & 7)] = src[f];
+        }
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[st]);
+      }
     }
+    if (lane == 0)  // leave no bulk copy in flight: wait (bounded) for the last stages
+      for (int k = (it > S ? it - S : 0); k < it; ++k) mbar_wait(&full[k % S], (k / S) & 1);
+    if (!waited) grid_dep_wait();
+    grid_dep_launch();
     return;
   }
 
   // ----------------------------------------------------------- consumers
+  grid_dep_wait();  // activations / residual are written by the predecessor
+  grid_dep_launch();
   const int row_off = tid / c.gw, cg = tid % c.gw;
   const bool active = row_off < c.p_rows;
-  float2 xa[ROUNDS][8], xb[ROUNDS][8];
+  float xr[ROUNDS][32];
 #pragma unroll
   for (int i = 0; i < ROUNDS; ++i)
 #pragma unroll
-    for (int m = 0; m < 8; ++m) { xa[i][m] = make_float2(0.f, 0.f); xb[i][m] = xa[i][m]; }
+    for (int m = 0; m < 32; ++m) xr[i][m] = 0.0f;
   const float* cur_x = nullptr;
-  float racc = 0.0f;
-  const int tr = tid >> 3, tw = tid & 7;
-  const bool tree_warp = warp < (8 * c.rt + 31) / 32;
+  // The tree runs on warps 1 and 3: with 64 chain groups per row these hold
+  // groups 32..63, which have no second round when 64 < cols/32 <= 128, so
+  // the tree lands on the warps with the least decode work.
+  const bool tree_warp = (warp & 1) == 1;
+  const int tt = ((warp >> 1) << 5) | lane;  // 0..63 over warps 1 and 3
+  const int tr = tt >> 3, tw = tt & 7;
 
   int it = 0;
-  bool dead = false;
-  for (int T = blockIdx.x; !dead && T < c.ntiles; T += gridDim.x) {
-    for (int sub = 0; sub < c.nsub; ++sub) {
-      int job, r0, nrows;
-      tile_coords(p, c, T, sub, job, r0, nrows);
-      if (!job_active(p, job)) continue;
-      const int cur = it++;
-      const int st = cur % S, pb = cur & 1;
-      const GemvJob& J = p.job[job];
-      if (!c.stage_x && active && J.x != cur_x) {
+  for (int T = blockIdx.x; T < c.ntiles; T += gridDim.x) {
+    int job, rb;
+    item_of(c, T, job, rb);
+    if (!job_active(p, job)) continue;
+    const int cur = it++;
+    const int st = cur % S, pb = cur & 1;
+    const int r0 = rb * kRt;
+    const int nrows = min(kRt, p.rows - r0);
+    const GemvJob& J = p.job[job];
+    if (!c.stage_x && J.x != cur_x) {
+      if (active) {
 #pragma unroll
         for (int i = 0; i < ROUNDS; ++i) {
           const int u = cg + 64 * i;
-          if (u < c.n_u) load_x_unit(J.x, u, xa[i], xb[i]);
-        }
-        cur_x = J.x;
-      }
-      const bool to = !mbar_wait(&full[st], (cur / S) & 1);
-      const uint8_t* stage = stages + (size_t)st * c.stage_bytes;
-      if (active && !to) {
-        if (c.stage_x) {
-          const float* xs = reinterpret_cast<const float*>(stage + c.x_off);
+          if (u < c.n_u) {
+            const float4* src = reinterpret_cast<const float4*>(J.x + 32 * u);
+            float4 v4[8];
 #pragma unroll
-          for (int i = 0; i < ROUNDS; ++i) {
-            const int u = cg + 64 * i;
-            if (u < c.n_u) load_x_unit(xs, u, xa[i], xb[i]);
+            for (int m = 0; m < 8; ++m) v4[m] = src[m];
+            unpack_x(v4, xr[i]);
           }
         }
-        const float* lut = luts + job * 256;
-        float* pbuf = part + pb * c.rt * kRowPitch;
+      }
+      cur_x = J.x;
+    }
+    const bool to = !mbar_wait(&full[st], (cur / S) & 1);
+    const uint8_t* stage = stages + (size_t)st * c.stage_bytes;
+    if (active && !to) {
+      if (c.stage_x) {
+        const float4* xs = reinterpret_cast<const float4*>(stage + c.x_off);
+#pragma unroll
+        for (int i = 0; i < ROUNDS; ++i) {
+          const int u = cg + 64 * i;
+          if (u < c.n_u) {
+            float4 v4[8];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) v4[m] = xs[u * 8 + ((m + u) & 7)];
+            unpack_x(v4, xr[i]);
+          }
+        }
+      }
+      const float* lut = luts + job * 256;
+      float* pbuf = part + pb * kRt * kRowPitch;
 #pragma unroll 2
-        for (int rr = row_off; rr < nrows; rr += c.p_rows) {
-          float2 accA = make_float2(0.f, 0.f), accB = make_float2(0.f, 0.f);
+      for (int rr = row_off; rr < nrows; rr += c.p_rows) {
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-          for (int i = 0; i < ROUNDS; ++i) {
-            const int u = cg + 64 * i;
-            if (i == 0 || u < c.n_u) {
-              const uint4 q = *reinterpret_cast<const uint4*>(stage + rr * cb + 16 * u);
-              const uint32_t sv = *reinterpret_cast<const uint16_t*>(stage + c.scale_off + rr * sb + 2 * u);
-              const float2 s = make_float2(lut[sv & 0xFFu], lut[sv >> 8]);
-              unit_fma(q, s, xa[i], xb[i], accA, accB);
-            }
+        for (int i = 0; i < ROUNDS; ++i) {
+          const int u = cg + 64 * i;
+          if (i == 0 || u < c.n_u) {
+            const uint4 q = *reinterpret_cast<const uint4*>(stage + rr * cb + 16 * u);
+            const uint32_t sv = *reinterpret_cast<const uint16_t*>(stage + c.scale_off + rr * sb + 2 * u);
+            unit_fma(q, lut[sv & 0xFFu], lut[sv >> 8], xr[i], acc);
           }
-          *reinterpret_cast<float4*>(pbuf + rr * kRowPitch + part_index(4 * cg)) =
-              make_float4(accA.x, accB.x, accA.y, accB.y);
         }
+        *reinterpret_cast<float4*>(pbuf + rr * kRowPitch + part_index(4 * cg)) =
+            make_float4(acc[0], acc[1], acc[2], acc[3]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
-      if (named_bar_or(1, NC, to)) { dead = true; break; }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (named_bar_or(1, NC, to)) break;
 
-      if (tree_warp) {
-        const float* pbuf = part + pb * c.rt * kRowPitch;
-        float y = 0.0f;
-        if (tr < nrows) y = group_tree(pbuf + tr * kRowPitch + tw * kGroupPitch);
-        y = combine8(legacy_fix(y, p.legacy_tree));
-        if (tw == 0 && tr < nrows) {
-          const int r = r0 + tr;
-          if (p.mode == 0) {
-            J.out[r] = epilogue(y, p.relu2, p.out_scale);
-          } else {
-            if (sub == 0) racc = p.base ? p.base[r] : 0.0f;
-            racc = fmaf(y, p.route_w[sub], racc);
-            if (sub == c.nsub - 1) p.rs_out[r] = p.resid ? p.resid[r] + racc : racc;
+    if (tree_warp) {
+      const float* pbuf = part + pb * kRt * kRowPitch;
+      float y = 0.0f;
+      if (tr < nrows) y = group_tree(pbuf + tr * kRowPitch + tw * kGroupPitch);
+      y = combine8(legacy_fix(y, p.legacy_tree));
+      if (tw == 0 && tr < nrows) {
+        const int r = r0 + tr;
+        if (p.mode == 0) {
+          J.out[r] = epilogue(y, p.relu2, p.out_scale);
+        } else {
+          p.contrib[(size_t)job * p.rows + r] = y;
+          __threadfence();
+          if (atomicAdd(&p.row_count[r], 1) == p.njobs - 1) {
+            __threadfence();
+            float acc = p.base ? p.base[r] : 0.0f;
+            for (int s = 0; s < p.njobs; ++s)
+              acc = fmaf(__ldcg(&p.contrib[(size_t)s * p.rows + r]), p.route_w[s], acc);
+            p.rs_out[r] = p.resid ? p.resid[r] + acc : acc;
+            p.row_count[r] = 0;
           }
         }
       }
@@ -368,7 +425,7 @@ __global__ void __launch_bounds__(288, 1) nvfp4_gemv_tma(GemvBatch p, TmaCfg c) 
 namespace {
 
 struct DevInfo {
-  int sms = 0, smem_optin = 0;
+  int sms = 0, smem_optin = 0, smem_sm = 0;
 };
 
 DevInfo& dev_info() {
@@ -379,6 +436,7 @@ DevInfo& dev_info() {
   if (i.sms == 0) {
     cudaDeviceGetAttribute(&i.sms, cudaDevAttrMultiProcessorCount, d);
     cudaDeviceGetAttribute(&i.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, d);
+    cudaDeviceGetAttribute(&i.smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, d);
   }
   return i;
 }
@@ -395,6 +453,7 @@ int set_smem(K kernel, int bytes) {
 
 bool tma_ok(const GemvBatch& b) {
   if (b.cols % 32 != 0 || b.cols > 4096) return false;
+  if (b.mode == 1 && (!b.contrib || !b.row_count)) return false;
   for (int j = 0; j < b.njobs; ++j) {
     const MatRef& m = b.job[j].mat;
     if (!al16(m.codes) || !al16(m.scales) || !al16(b.job[j].x)) return false;
@@ -403,46 +462,59 @@ bool tma_ok(const GemvBatch& b) {
   return true;
 }
 
+template <typename K>
+int launch_ex(K kernel, dim3 grid, dim3 block, int smem, cudaStream_t stream, bool pdl,
+              const GemvBatch& b, const TmaCfg& c) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, b, c) == cudaSuccess ? kOk : kErrLaunch;
+}
+
+constexpr int kCtasPerSm = 3;
+
 int launch_tma(const GemvBatch& b, cudaStream_t stream) {
   const DevInfo& di = dev_info();
   TmaCfg c{};
   c.n_u = b.cols / 32;
   c.gw = c.n_u < 64 ? c.n_u : 64;
   const int rounds = (c.n_u + 63) / 64;
-  const int NC = 256;
+  const int NC = 128;
   c.p_rows = NC / c.gw;
+  const int cb = b.cols / 2, sb = b.cols / 16;
   c.stage_x = b.mode == 1 ? 1 : 0;
-  c.rt = 16;
-  const int fixed = 128 + b.njobs * 1024 + 2 * c.rt * kRowPitch * 4;
-  c.scale_off = c.rt * (b.cols / 2);
-  c.x_off = c.scale_off + align_up(c.rt * (b.cols / 16), 16);
+  c.part_off = align_up(448 + b.njobs * 1024, 16);
+  c.stage_base = align_up(c.part_off + 2 * kRt * kRowPitch * 4, 128);
+  c.scale_off = kRt * cb;
+  c.x_off = c.scale_off + align_up(kRt * sb, 16);
   c.stage_bytes = align_up(c.x_off + (c.stage_x ? b.cols * 4 : 0), 128);
-  c.stages = (di.smem_optin - fixed) / c.stage_bytes;
-  if (c.stages > 4) c.stages = 4;
-  if (c.stages < 2) return kErrShape;
-  const int tiles = (b.rows + c.rt - 1) / c.rt;
-  if (b.mode == 0) {
-    c.tiles_per_job = tiles;
-    c.ntiles = tiles * b.njobs;
-    c.nsub = 1;
-  } else {
-    c.tiles_per_job = tiles;
-    c.ntiles = tiles;
-    c.nsub = b.njobs;
+  const int budget = (di.smem_sm - kCtasPerSm * 1024) / kCtasPerSm;
+  c.stages = (budget - c.stage_base) / c.stage_bytes;
+  if (c.stages > 6) c.stages = 6;
+  if (c.stages < 2) {
+    c.stages = 2;
+    if (c.stage_base + 2 * c.stage_bytes > di.smem_optin) return kErrShape;
   }
-  const int smem = fixed + c.stages * c.stage_bytes;
-  int grid = c.ntiles < di.sms ? c.ntiles : di.sms;
+  const int smem = c.stage_base + c.stages * c.stage_bytes;
+  c.tiles_per_job = (b.rows + kRt - 1) / kRt;
+  c.ntiles = c.tiles_per_job * b.njobs;
+  int grid = di.sms * kCtasPerSm;
+  if (grid > c.ntiles) grid = c.ntiles;
   const dim3 block(NC + 32);
-  cudaError_t e;
+  const bool pdl = b.pdl != 0;
   if (rounds == 1) {
     if (set_smem(nvfp4_gemv_tma<1>, smem)) return kErrLaunch;
-    nvfp4_gemv_tma<1><<<grid, block, smem, stream>>>(b, c);
-  } else {
-    if (set_smem(nvfp4_gemv_tma<2>, smem)) return kErrLaunch;
-    nvfp4_gemv_tma<2><<<grid, block, smem, stream>>>(b, c);
+    return launch_ex(nvfp4_gemv_tma<1>, dim3(grid), block, smem, stream, pdl, b, c);
   }
-  e = cudaGetLastError();
-  return e == cudaSuccess ? kOk : kErrLaunch;
+  if (set_smem(nvfp4_gemv_tma<2>, smem)) return kErrLaunch;
+  return launch_ex(nvfp4_gemv_tma<2>, dim3(grid), block, smem, stream, pdl, b, c);
 }
 
 template <int W>

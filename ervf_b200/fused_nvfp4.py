@@ -6,8 +6,9 @@ same method names, argument order and meaning, same in-place outputs and
 ``None`` returns, same attribute flags.  Buffers are caller-owned CUDA
 tensors (torch tensors, or any object exposing ``__cuda_array_interface__``
 such as CuPy arrays); raw device / mapped-host addresses are Python ints, as
-in the reference.  Launches go on the current torch CUDA stream unless
-``self.stream`` is set.
+in the reference.  Launches go on ``self.stream`` if set, else on CuPy's
+current stream when CuPy is in use (as in the reference runtime), else on
+torch's current stream.
 
 Differences a caller can observe:
   * ``ervf_width`` selects a schedule: 0 (default) is the TMA-staged B200
@@ -218,17 +219,43 @@ class FusedNVFP4:
 
     # -------------------------------------------------- grouped (B200)
     def moe_up_grouped(self, up_codes, up_scales, up_code_stride: int, up_scale_stride: int,
-                       ids, globals_dev, top_k: int, x, act, inter: int, hidden: int) -> None:
-        """All routed up projections of a token in one launch (relu^2)."""
+                       ids, globals_dev, top_k: int, x, act, inter: int, hidden: int,
+                       flags: int = 0) -> None:
+        """All routed up projections of a token in one launch (relu^2).
+        ``flags``: ervf_b200._lib.LAUNCH_PDL | LAUNCH_IDS_READY (see the header)."""
         _lib.call("ervf_moe_up_grouped", ptr(up_codes), ptr(up_scales), int(up_code_stride),
                   int(up_scale_stride), ptr(ids), ptr(globals_dev), int(top_k), ptr(x), ptr(act),
-                  int(inter), int(hidden), self._width(), self._s())
+                  int(inter), int(hidden), self._width(), int(flags), self._s())
 
     def moe_down_routesum(self, dn_codes, dn_scales, dn_code_stride: int, dn_scale_stride: int,
                           ids, globals_dev, route_w, top_k: int, act, out, hidden: int,
-                          inter: int, base=None, resid=None) -> None:
-        """All routed down projections plus the route-order weighted sum."""
+                          inter: int, base=None, resid=None, flags: int = 0, scratch=None) -> None:
+        """All routed down projections plus the route-order weighted sum.
+        ``scratch``: a zero-initialised uint8 device buffer of
+        ``routesum_scratch_bytes(hidden, top_k)`` bytes; by default one owned
+        by this object is used (so calls through one FusedNVFP4 on different
+        streams must not overlap)."""
+        if scratch is None:
+            scratch = self._scratch(hidden, top_k)
         _lib.call("ervf_moe_down_routesum", ptr(dn_codes), ptr(dn_scales), int(dn_code_stride),
                   int(dn_scale_stride), ptr(ids), ptr(globals_dev), ptr(route_w), int(top_k),
                   ptr(act), ptr(base), ptr(resid), ptr(out), int(hidden), int(inter),
-                  self._width(), self._s())
+                  ptr(scratch), int(_numel(scratch) or 0), self._width(), int(flags), self._s())
+
+    def routesum_scratch_bytes(self, hidden: int, top_k: int) -> int:
+        return int(_lib.load().ervf_routesum_scratch_bytes(int(hidden), int(top_k)))
+
+    def _scratch(self, hidden: int, top_k: int):
+        key = (int(hidden), int(top_k))
+        cache = self.__dict__.setdefault("_scratch_cache", {})
+        if key not in cache:
+            cache[key] = torch.zeros(self.routesum_scratch_bytes(*key), dtype=torch.uint8,
+                                     device=self.device)
+        return cache[key]
+
+    def route_topk_batched(self, rlogs, gate_b, ids, w, layers: int, n: int, top_k: int,
+                           scaling: float, bad_pick: int = 0, bias_stride: int = 0) -> None:
+        """route_topk for `layers` independent logit rows in one launch."""
+        _lib.call("ervf_route_topk_batched", ptr(rlogs), ptr(gate_b), ptr(ids), ptr(w),
+                  int(layers), int(n), int(top_k), float(np.float32(scaling)), int(bad_pick),
+                  int(bias_stride), self._s())

@@ -129,20 +129,35 @@ class MoEDecoder:
             self.contrib = torch.zeros(k * bank.hidden, dtype=torch.float32, device=d)
             self.gathered = torch.zeros(ep_ranks * k * bank.hidden, dtype=torch.float32, device=d)
         self.graph = None
+        self.pdl = True
 
     def _s(self) -> int:
         return int(torch.cuda.current_stream(self.bank.device).cuda_stream)
 
-    def layer(self, l: int, x: torch.Tensor, rlog: torch.Tensor, out: torch.Tensor) -> None:
-        """out = x + sum_s w_s * down_{e_s}(relu2(up_{e_s}(x))) in route order."""
+    def route(self, rlogs: torch.Tensor) -> None:
+        """Routes every layer of the token in one launch (rlogs f32[L][E])."""
+        b = self.bank
+        self.fused.route_topk_batched(rlogs, None, self.ids, self.w, b.n_layers, b.n_experts,
+                                      self.top_k, self.scaling)
+
+    def layer(self, l: int, x: torch.Tensor, out: torch.Tensor, first: bool = False) -> None:
+        """out = x + sum_s w_s * down_{e_s}(relu2(up_{e_s}(x))) in route order,
+        with layer l's route already in self.ids[l] / self.w[l]."""
         b, f, k = self.bank, self.fused, self.top_k
         ids, w = self.ids[l], self.w[l]
-        f.route_topk(rlog, self.gate_b, ids, w, b.n_experts, k, self.scaling)
         if self.ep_ranks == 1:
+            # The routing launch precedes the first up launch directly, so
+            # that one must wait before reading ids; every later launch may
+            # start streaming its experts while its predecessor drains.
+            up_flags = _lib.LAUNCH_PDL | (0 if first else _lib.LAUNCH_IDS_READY)
+            dn_flags = _lib.LAUNCH_PDL | _lib.LAUNCH_IDS_READY
+            if not self.pdl:
+                up_flags = dn_flags = 0
             f.moe_up_grouped(b.up_codes[l], b.up_scales[l], b.up_code_bytes, b.up_scale_bytes, ids,
-                             b.globals[l], k, x, self.act, b.inter, b.hidden)
+                             b.globals[l], k, x, self.act, b.inter, b.hidden, flags=up_flags)
             f.moe_down_routesum(b.dn_codes[l], b.dn_scales[l], b.dn_code_bytes, b.dn_scale_bytes,
-                                ids, b.globals[l], w, k, self.act, out, b.hidden, b.inter, resid=x)
+                                ids, b.globals[l], w, k, self.act, out, b.hidden, b.inter, resid=x,
+                                flags=dn_flags)
             return
         import torch.distributed as dist
 
@@ -156,11 +171,13 @@ class MoEDecoder:
                   b.hidden, self.ep_ranks, self._s())
 
     def step(self, x_in: torch.Tensor, rlogs: torch.Tensor) -> torch.Tensor:
-        """One decode token through all layers; rlogs f32[L][E]. Returns the
-        buffer holding x after the last layer."""
+        """One decode token through all layers; rlogs f32[L][E] are the
+        router logits of every layer.  Returns the buffer holding x after
+        the last layer."""
+        self.route(rlogs)
         cur = x_in
         for l in range(self.bank.n_layers):
             nxt = self.xs[l & 1]
-            self.layer(l, cur, rlogs[l], nxt)
+            self.layer(l, cur, nxt, first=(l == 0))
             cur = nxt
         return cur

@@ -39,6 +39,17 @@ extern "C" {
 #define ERVF_ERR_TIMEOUT -5  /* a bounded device wait ran out (ervf_device_status) */
 #define ERVF_ERR_ARG -6      /* an argument value is invalid (width, batch, ...) */
 
+/* Launch flags of the grouped MoE entry points.
+ * ERVF_LAUNCH_PDL: launch with programmatic stream serialisation, so the
+ *   kernel's prologue and weight streaming overlap the previous kernel on the
+ *   stream; it waits for that kernel before reading activations.
+ * ERVF_LAUNCH_IDS_READY: the route ids / globals were written by a kernel that
+ *   completed before the previous kernel on the stream started (e.g. one
+ *   routing launch for all layers at the start of a decode step), so they may
+ *   be read -- and the routed experts' weights streamed -- before the wait. */
+#define ERVF_LAUNCH_PDL 1
+#define ERVF_LAUNCH_IDS_READY 2
+
 /* Library version, e.g. 100 for 0.1.0. */
 ERVF_API int ervf_version(void);
 
@@ -90,19 +101,28 @@ ERVF_API int ervf_weighted_accumulate_ind(float* dst, const float* src, const fl
  * apply_relu2=True) (fused_nvfp4.py:970-978, first half). */
 ERVF_API int ervf_moe_up_grouped(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
                         size_t up_scale_stride, const int32_t* ids, const float* globals, int top_k,
-                        const float* x, float* act, int inter, int hidden, int width, void* stream);
+                        const float* x, float* act, int inter, int hidden, int width, int flags,
+                        void* stream);
 
 /* Routed down projections plus the route-order sum, one launch: for every
  * output row r, acc = base ? base[r] : 0; for s = 0..top_k-1 in ROUTE order
  * acc = fmaf(down_{ids[s]}(act[s])[r], route_w[s], acc); out[r] = resid ?
  * resid[r] + acc : acc.  Equal to top_k down gemv_into calls followed by
  * accumulate_into in route order (fused_nvfp4.py:970-984; route-order
- * contract runtime.py:588-596), with no contribution buffer. */
+ * contract runtime.py:588-596).
+ * scratch: caller-owned device buffer of ervf_routesum_scratch_bytes(hidden,
+ * top_k) bytes, 16-byte aligned, zero-filled once before its first use; each
+ * call leaves it ready for the next (calls that share it must not overlap on
+ * the GPU).  With scratch the rows spread over all SMs; scratch = NULL runs a
+ * slower schedule that needs none. */
 ERVF_API int ervf_moe_down_routesum(const uint8_t* dn_codes, const uint8_t* dn_scales,
                            size_t dn_code_stride, size_t dn_scale_stride, const int32_t* ids,
                            const float* globals, const float* route_w, int top_k, const float* act,
                            const float* base, const float* resid, float* out, int hidden, int inter,
-                           int width, void* stream);
+                           void* scratch, size_t scratch_bytes, int width, int flags, void* stream);
+
+/* Bytes of scratch ervf_moe_down_routesum uses for (hidden, top_k). */
+ERVF_API size_t ervf_routesum_scratch_bytes(int hidden, int top_k);
 
 /* Expert parallelism, per rank and layer: for the route slots whose expert
  * this rank owns (ids[s] % ep_ranks == ep_rank, read on the device), act[s] =
@@ -160,6 +180,14 @@ ERVF_API int ervf_bf16_gemv(const uint16_t* W, const float* x, float* out, int r
  * (fused_nvfp4.py:433-465, :797-801).  n <= 1024, top_k <= 64. */
 ERVF_API int ervf_route_topk(const float* rlog, const float* gate_b, int32_t* ids, float* w, int n,
                     int top_k, float scaling, int bad_pick, void* stream);
+
+/* The device router for `layers` independent problems in one launch (one
+ * warp each): rlog f32[layers][n], gate_b f32[layers][bias_stride] (NULL for
+ * no bias when n <= 256), ids i32[layers][top_k], w f32[layers][top_k].
+ * Same selections and weights as ervf_route_topk per layer. */
+ERVF_API int ervf_route_topk_batched(const float* rlog, const float* gate_b, int32_t* ids, float* w,
+                                     int layers, int n, int top_k, float scaling, int bad_pick,
+                                     int bias_stride, void* stream);
 
 /* Device LRU slot assignment: replaces cache_assign / FusedNVFP4.cache_assign
  * (fused_nvfp4.py:470-511, :803-808). */

@@ -53,6 +53,28 @@ def test_route_topk_matches_oracle(fused, oracle, cuda):
         np.testing.assert_allclose(w.cpu().numpy(), ow, rtol=3e-7)
 
 
+def test_route_topk_batched_matches_per_layer(fused, oracle, cuda):
+    r = np.random.default_rng(12)
+    for n, k in ((128, 6), (128, 8), (200, 6), (512, 4)):
+        L = 24
+        rl = r.standard_normal((L, n)).astype(np.float32)
+        bias = (r.standard_normal((L, n)) * 0.05).astype(np.float32)
+        ids = torch.zeros(L, k, dtype=torch.int32, device=cuda)
+        w = torch.zeros(L, k, device=cuda)
+        rd, bd = _t(rl, cuda), _t(bias, cuda)
+        fused.route_topk_batched(rd, bd, ids, w, L, n, k, 1.0, 0, n)
+        torch.cuda.synchronize()
+        for l in range(L):
+            oid, ow = oracle.route_topk(rl[l], bias[l], k)
+            assert np.array_equal(ids[l].cpu().numpy(), oid), (n, k, l)
+            np.testing.assert_allclose(w[l].cpu().numpy(), ow, rtol=3e-7)
+            one_ids = torch.zeros(k, dtype=torch.int32, device=cuda)
+            one_w = torch.zeros(k, device=cuda)
+            fused.route_topk(rd[l], bd[l], one_ids, one_w, n, k, 1.0)
+            torch.cuda.synchronize()
+            assert torch.equal(one_ids, ids[l]) and torch.equal(one_w, w[l])
+
+
 def test_route_topk_ties_pick_lowest_index(fused, cuda):
     rlog = np.zeros(128, np.float32)
     rlog[[5, 9, 77]] = 3.0

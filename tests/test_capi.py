@@ -16,7 +16,7 @@ HEADER = Path(__file__).resolve().parents[1] / "include" / "ervf_b200.h"
 
 
 def declared():
-    return re.findall(r"^ERVF_API int (ervf_\w+)\(", HEADER.read_text(), flags=re.M)
+    return re.findall(r"^ERVF_API (?:int|size_t) (ervf_\w+)\(", HEADER.read_text(), flags=re.M)
 
 
 def test_header_declares_entry_points():

@@ -94,6 +94,44 @@ def test_grouped_up_and_routesum_match_unfused(fused, oracle, bank, cuda, width)
         assert bits_equal(act[s * INTER:(s + 1) * INTER].cpu().numpy(), a)
 
 
+def test_decoder_step_pdl_chain_matches_oracle(fused, oracle, bank, cuda):
+    """Three layers of the decode step (batched routing, PDL-chained grouped
+    launches, CUDA graph) equal the oracle's route-order recurrence."""
+    from ervf_b200.moe import ExpertBank, MoEDecoder
+
+    L, E, k = 3, 8, 6
+    eb = ExpertBank(L, E, HIDDEN, INTER, cuda)
+    for l in range(L):
+        for e in range(E):
+            eb.upload_expert(l, e, bank["ups"][(e + l) % E], bank["dns"][(e + 2 * l) % E])
+    dec = MoEDecoder(eb, k)
+    r = np.random.default_rng(17)
+    rl = r.standard_normal((L, E)).astype(np.float32)
+    x = x_regime(HIDDEN, "bf16", seed=21)
+    xd, rd = _t(x, cuda), _t(rl, cuda)
+    for use_graph in (False, True):
+        if use_graph:
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                dec.step(xd, rd)
+            torch.cuda.current_stream().wait_stream(s)
+            with torch.cuda.graph(g):
+                y = dec.step(xd, rd)
+            g.replay()
+        else:
+            y = dec.step(xd, rd)
+        torch.cuda.synchronize()
+        want = x.copy()
+        for l in range(L):
+            ids, w = oracle.route_topk(rl[l], np.zeros(E, np.float32), k)
+            experts = {e: (*bank["ups"][(e + l) % E], *bank["dns"][(e + 2 * l) % E]) for e in range(E)}
+            want = (want + oracle.moe_block(want, experts, ids, w, HIDDEN, INTER)).astype(np.float32)
+            assert np.array_equal(dec.ids[l].cpu().numpy(), ids)
+        assert bits_equal(y.cpu().numpy(), want), use_graph
+
+
 def test_routesum_residual_matches_f64(fused, oracle, bank, cuda):
     """x + moe(x) against a float64 dequant reference (tolerance, not bits)."""
     from ervf_b200.formats import dequantize
