@@ -90,9 +90,17 @@ class Clocks:
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}",
                                        f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                       "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
         except FileNotFoundError:
             self.p = None
+        # nvidia-smi takes a moment to start: wait (bounded) for its first
+        # sample so that the timed region that follows is covered.
+        t_end = time.time() + 5.0
+        while self.p is not None and time.time() < t_end and self.p.poll() is None:
+            self.f.flush()
+            if Path(self.f.name).stat().st_size > 0:
+                break
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *a):

@@ -19,6 +19,7 @@ ERR_ALIGN = -3
 ERR_LAUNCH = -4
 ERR_TIMEOUT = -5
 ERR_ARG = -6
+ERR_SCRATCH_LIMIT = -8
 
 LAUNCH_PDL = 1
 LAUNCH_IDS_READY = 2
@@ -30,6 +31,7 @@ _NAMES = {
     ERR_LAUNCH: "CUDA launch failed",
     ERR_TIMEOUT: "device wait timed out",
     ERR_ARG: "invalid argument",
+    ERR_SCRATCH_LIMIT: "larger than the fixed scratch array (hidden <= 8192, top_k <= 8)",
 }
 
 _vp = ctypes.c_void_p
@@ -50,6 +52,8 @@ SIGNATURES: dict[str, list] = {
     "ervf_moe_down_routesum": [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i,
                                _vp, _sz, _i, _i, _vp],
     "ervf_routesum_scratch_bytes": [_i, _i],
+    "ervf_moe_down_routesum_static": [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp,
+                                      _i, _i, _i, _i, _vp],
     "ervf_route_topk_batched": [_vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp],
     "ervf_ep_expert_slots": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _i, _vp, _vp, _vp,
                              _i, _i, _i, _i, _i, _vp],
@@ -95,6 +99,6 @@ def call(name: str, *args) -> None:
     """Call one C entry point and raise ErvfError on a non-zero status."""
     status = getattr(load(), name)(*args)
     if status != OK:
-        if status in (ERR_SHAPE, ERR_ALIGN, ERR_ARG, ERR_NULL):
+        if status in (ERR_SHAPE, ERR_ALIGN, ERR_ARG, ERR_NULL, ERR_SCRATCH_LIMIT):
             raise ValueError(f"{name}: {_NAMES.get(status, 'error')} ({status})")
         raise ErvfError(name, status)

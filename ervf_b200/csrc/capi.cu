@@ -3,6 +3,8 @@
 // synchronisation (except ervf_device_status, which is documented as such).
 #include "../../include/ervf_b200.h"
 
+#include <atomic>
+
 #include "aux.h"
 #include "common.cuh"
 #include "kernels.h"
@@ -348,6 +350,69 @@ int ervf_cache_fetch(const uint8_t* bank_c, const uint8_t* bank_s, uint8_t* cach
   if (top_k <= 0 || top_k > 65535) return kErrShape;
   return launch_cache_fetch(bank_c, bank_s, cache_c, cache_s, ids, slots, need, code_bytes,
                             scale_bytes, top_k, S(stream));
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free routed sum (no counterpart in the reference).
+//
+// The scratch of the spread-rows routed sum (contrib[top_k][hidden] floats +
+// hidden row counters) lives in this file-scope device array instead of a
+// caller buffer.  Limits: hidden <= kStaticRows, top_k <= kStaticJobs
+// (294,912 bytes).  Its device address is looked up once per device, with
+// that device current, on the first call.  Every call clears the row
+// counters on the stream (cudaMemsetAsync; no allocation) before the launch.
+// All calls on one device share the array: calls that overlap on the GPU race.
+
+namespace {
+
+constexpr int kStaticRows = 8192;
+constexpr int kStaticJobs = 8;
+constexpr size_t kStaticScratchBytes =
+    (size_t)kStaticJobs * kStaticRows * sizeof(float) + (size_t)kStaticRows * sizeof(int);
+
+static __device__ __align__(256) unsigned char g_routesum_static[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::atomic<void*> g_static_addr[kMaxDevices];
+
+// Device address of g_routesum_static on the current device (cached).
+void* static_scratch() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kMaxDevices) return nullptr;
+  void* p = g_static_addr[d].load(std::memory_order_acquire);
+  if (!p) {
+    if (cudaGetSymbolAddress(&p, g_routesum_static) != cudaSuccess) return nullptr;
+    g_static_addr[d].store(p, std::memory_order_release);
+  }
+  return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ervf_moe_down_routesum_static(const uint8_t* dn_codes, const uint8_t* dn_scales,
+                                  size_t dn_code_stride, size_t dn_scale_stride,
+                                  const int32_t* ids, const float* globals, const float* route_w,
+                                  int top_k, const float* act, const float* base,
+                                  const float* resid, float* out, int hidden, int inter,
+                                  int width, int flags, void* stream) {
+  if (hidden > kStaticRows || top_k > kStaticJobs) return ERVF_ERR_SCRATCH_LIMIT;
+  if (!dn_codes || !dn_scales || !ids || !globals || !route_w || !act || !out) return kErrNull;
+  if (top_k <= 0 || hidden <= 0) return kErrShape;
+  void* scratch = static_scratch();
+  if (!scratch) return kErrLaunch;
+  int* row_count = reinterpret_cast<int*>(reinterpret_cast<float*>(scratch) + (size_t)top_k * hidden);
+  if (cudaMemsetAsync(row_count, 0, (size_t)hidden * sizeof(int), S(stream)) != cudaSuccess)
+    return kErrLaunch;
+  // A memset now precedes the launch, so it runs without programmatic
+  // dependent launch; ERVF_LAUNCH_IDS_READY only matters with it.
+  return ervf_moe_down_routesum(dn_codes, dn_scales, dn_code_stride, dn_scale_stride, ids, globals,
+                                route_w, top_k, act, base, resid, out, hidden, inter, scratch,
+                                kStaticScratchBytes, width, flags & ~(ERVF_LAUNCH_PDL | ERVF_LAUNCH_IDS_READY),
+                                stream);
 }
 
 }  // extern "C"

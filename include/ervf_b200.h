@@ -38,6 +38,7 @@ extern "C" {
 #define ERVF_ERR_LAUNCH -4   /* the CUDA launch failed */
 #define ERVF_ERR_TIMEOUT -5  /* a bounded device wait ran out (ervf_device_status) */
 #define ERVF_ERR_ARG -6      /* an argument value is invalid (width, batch, ...) */
+#define ERVF_ERR_SCRATCH_LIMIT -8 /* larger than the library's fixed scratch array */
 
 /* Launch flags of the grouped MoE entry points.
  * ERVF_LAUNCH_PDL: launch with programmatic stream serialisation, so the
@@ -123,6 +124,24 @@ ERVF_API int ervf_moe_down_routesum(const uint8_t* dn_codes, const uint8_t* dn_s
 
 /* Bytes of scratch ervf_moe_down_routesum uses for (hidden, top_k). */
 ERVF_API size_t ervf_routesum_scratch_bytes(int hidden, int top_k);
+
+/* ervf_moe_down_routesum without a scratch argument.  No counterpart in the
+ * reference.  The scratch is a fixed device array inside the library, so the
+ * call allocates nothing: hidden <= 8192 and top_k <= 8, else
+ * ERVF_ERR_SCRATCH_LIMIT before anything runs.  The first call on a device
+ * looks up the array's address with that device current; make it before any
+ * stream capture begins.  Each call clears the array's row counters with
+ * cudaMemsetAsync on `stream`, then launches without programmatic dependent
+ * launch (the PDL / IDS_READY bits of `flags` are ignored).  All calls on a
+ * device share the one array: calls that overlap on the GPU race.  Results
+ * are bit-identical to ervf_moe_down_routesum. */
+ERVF_API int ervf_moe_down_routesum_static(const uint8_t* dn_codes, const uint8_t* dn_scales,
+                                           size_t dn_code_stride, size_t dn_scale_stride,
+                                           const int32_t* ids, const float* globals,
+                                           const float* route_w, int top_k, const float* act,
+                                           const float* base, const float* resid, float* out,
+                                           int hidden, int inter, int width, int flags,
+                                           void* stream);
 
 /* Expert parallelism, per rank and layer: for the route slots whose expert
  * this rank owns (ids[s] % ep_ranks == ep_rank, read on the device), act[s] =
