@@ -4,17 +4,15 @@
 //
 // Two families:
 //
-//  * nvfp4_gemv_tma  -- the B200 schedule.  A producer warp streams tiles of
-//    RT rows (codes, block scales and, for the routed-sum launch, the
-//    activation) into a ring of shared-memory stages with 1-D bulk copies
-//    (cp.async.bulk, no multicast) completing on mbarriers.  Each consumer
-//    thread owns one "chain group" c (four consecutive reference chains
-//    4c..4c+3, i.e. one 16-byte code unit per round) and keeps the activation
-//    of its columns in registers for the whole launch.  Codes are decoded two
-//    at a time with the sm_100a e2m1x2 converter and the fp32 products and
-//    fused multiply-adds run on the packed f32x2 pipe, pairing chains j and
-//    j+2 of the same unit (same row, same column offset).  Chain values go to
-//    shared memory and are reduced by the reference tree.
+//  * nvfp4_gemv_tma  -- the B200 schedule.  A producer warp streams items of
+//    up to 32 rows (codes and block scales) into a ring of shared-memory
+//    stages with 1-D bulk copies (cp.async.bulk, no multicast) completing on
+//    mbarriers.  Each of 256 consumer threads owns one "chain group" g (four
+//    consecutive reference chains 4g..4g+3, i.e. the 16-byte code unit g) for
+//    a slot of rows and keeps that unit's activation in registers; second-
+//    round units (cols > 2048) are spread evenly over all threads.  Codes and
+//    scales are decoded with the sm_100a e2m1x2 / e4m3x2 converters.  Chain
+//    values go to shared memory and are reduced by the reference tree.
 //
 //  * nvfp4_gemv_sched<W> -- the reference's ERVF widths 4/8/16/32 as
 //    schedules: W lanes per row, lane L owns chains L + W*i.  Same chains,
@@ -146,56 +144,67 @@ __global__ void __launch_bounds__(256) nvfp4_gemv_sched(GemvBatch p, int tiles_p
 // TMA-staged B200 schedule
 // ======================================================================
 //
-// CTA = 4 consumer warps + 1 producer warp, three CTAs per SM.  A work item
-// is a block of kRt rows of one job; the items of a launch (job-major) are
-// dealt to the CTAs round-robin.
+// CTA = 8 consumer warps + 1 producer warp, two CTAs per SM.  Each CTA owns a
+// contiguous, balanced range of "row blocks" (rs consecutive rows of one job)
+// over the launch's active jobs and walks it in items of up to kRt rows.
 //
-// Producer warp: bulk-copies an item's codes and scale bytes into a free
-// stage and, when the job's activation differs per item (mode 1), copies the
-// activation into the stage in a rotated layout (float4 i of unit u at slot
-// (i + u) & 7) so that the consumers of eight consecutive units read eight
-// different bank groups.
+// Producer warp (lane 0): per item, one bulk copy of the item's code rows and
+// one of its scale rows (cp.async.bulk, no multicast) into a ring of stages
+// completing on mbarriers; the consumers release a stage through a second
+// mbarrier.  Weight streaming starts before the dependency wait of a
+// programmatic launch (the weights do not depend on the predecessor).
 //
-// Consumer thread (row_off, c): chain group c = reference chains 4c..4c+3,
-// i.e. one 16-byte code unit per round, for rows row_off, row_off + p_rows,
-// ... of the item, activation of its columns in registers.  Codes are decoded
-// with the hardware e2m1x2 converter; each weight is w = RN(e2m1 * s) (FMUL)
-// and acc = fmaf(w, x, acc) (FFMA), in the reference's order.  Chain values
-// go to shared memory; after a consumer barrier two warps run the 256-leaf
-// tree of the item's rows.
+// Consumer thread (row slot ro, chain group g), gw groups per row slot (64,
+// or 32 when cols <= 1024) and rs = 256 / gw row slots: chain group g is the
+// reference's chains 4g..4g+3, whose first code unit is unit g (16 bytes =
+// 4 chains x 8 codes).  The activation of unit g lives in the thread's
+// registers for as long as the job does not change.
+//   round 1: rows ro, ro + rs, ... of the item, unit g: decode with the
+//            hardware e2m1x2 / e4m3x2 converters, w = RN(e2m1 * s) (FMUL),
+//            acc = fmaf(w, x, acc) (FFMA) in the reference's order; the four
+//            chain values go to the item's chain buffer.
+//   tail:    cols > 2048 gives chain groups c < n_u - 64 a second unit
+//            64 + c.  Those (row, c) continuations are spread evenly over all
+//            256 threads: each reads the chain values of round 1, continues
+//            them over unit 64 + c (activation from a swizzled shared copy)
+//            and writes them back.  With kRt = 24 rows and cols = 2688 every
+//            thread has 6 + 2 units per item, 98 % of an even split.
+//   tree:    thread (row tr, segment tw) reduces chains 32tw..32tw+31 of its
+//            row with the reference's shuffle tree (offsets 16..1) and eight
+//            lanes combine ((S0+S4)+(S2+S6))+((S1+S5)+(S3+S7)).
 //
-// mode 1 (routed sum): a tree thread writes its row's job output y_s to
-// contrib[s][row], publishes it with a release fence and a per-row atomic
-// count, and the thread that completes a row's count adds the row up in
-// ROUTE order, acc = fmaf(y_s, w_s, acc) for s = 0..njobs-1, writes x + acc
-// and resets the count.  Rows therefore spread over all CTAs, and the sum is
-// the same as one thread walking the slots in order.
+// mode 1 (routed sum): the tree lane of a row writes the job's row value y_s
+// to contrib[s][row], publishes it (release fence + per-row atomic count), and
+// the lane that completes a row's count adds the row up in ROUTE order,
+// acc = fmaf(y_s, w_s, acc) for s = 0..njobs-1 from base or 0, writes
+// resid + acc and resets the count -- the same sum as one thread walking the
+// slots in order, with the rows spread over every SM.
 
-constexpr int kRt = 8;  // rows per item
+constexpr int kCW = 8;          // consumer warps
+constexpr int kCT = kCW * 32;   // consumer threads
+constexpr int kBarC = 1;        // named barrier of the consumer threads
 
 struct TmaCfg {
-  int stages;
+  int stages;       // ring depth
   int stage_bytes;  // bytes per stage (128-aligned)
-  int scale_off;    // scale bytes inside a stage
-  int x_off;        // mode 1: rotated activation inside a stage
-  int part_off;     // chain buffers [2][kRt][kRowPitch] floats
+  int scale_off;    // scale rows inside a stage
+  int part_off;     // chain buffer [kRt][kRowPitch] floats
+  int xt_off;       // tail activation [n_tail][8] float4, swizzled
   int stage_base;
-  int n_u, gw, p_rows;
-  int tiles_per_job;  // row blocks per job
-  int ntiles;         // njobs * tiles_per_job
-  int stage_x;        // 1: the activation travels with each item (mode 1)
+  int n_u;          // code units per row (cols / 32)
+  int n_tail;       // units per row beyond 64 (second-round units)
+  int gw;           // chain groups per row slot (64 or 32)
+  int rs;           // row slots (kCT / gw)
+  int kb;           // row blocks per item (kRt / rs)
+  int bpj;          // row blocks per job
 };
 
-__device__ __forceinline__ void item_of(const TmaCfg& c, int T, int& job, int& rb) {
-  job = T / c.tiles_per_job;
-  rb = T - job * c.tiles_per_job;
-}
-
-// One 16-byte code unit (4 chains x 8 codes) of one row.  Chains 0,1 use the
-// block scale s0 = s_2u, chains 2,3 use s1 = s_2u+1; xr[8j + m] is the
-// activation of chain j's m-th code.
+// One 16-byte code unit (4 chains x 8 codes) of one row, continuing the four
+// chain accumulators acc[0..3].  Chains 0,1 use the block scale s0 = s_2u,
+// chains 2,3 use s1 = s_2u+1; x[8j + m] is the activation of chain j's m-th
+// code.
 __device__ __forceinline__ void unit_fma(const uint4 q, const float s0, const float s1,
-                                         const float (&xr)[32], float (&acc)[4]) {
+                                         const float (&x)[32], float* acc) {
   float f0[8], f1[8], f2[8], f3[8];
   e2m1x8_to_f32(q.x, f0);
   e2m1x8_to_f32(q.y, f1);
@@ -203,18 +212,17 @@ __device__ __forceinline__ void unit_fma(const uint4 q, const float s0, const fl
   e2m1x8_to_f32(q.w, f3);
 #pragma unroll
   for (int m = 0; m < 8; ++m) {
-    acc[0] = fmaf(f0[m] * s0, xr[m], acc[0]);
-    acc[1] = fmaf(f1[m] * s0, xr[8 + m], acc[1]);
-    acc[2] = fmaf(f2[m] * s1, xr[16 + m], acc[2]);
-    acc[3] = fmaf(f3[m] * s1, xr[24 + m], acc[3]);
+    acc[0] = fmaf(f0[m] * s0, x[m], acc[0]);
+    acc[1] = fmaf(f1[m] * s0, x[8 + m], acc[1]);
+    acc[2] = fmaf(f2[m] * s1, x[16 + m], acc[2]);
+    acc[3] = fmaf(f3[m] * s1, x[24 + m], acc[3]);
   }
 }
 
-__device__ __forceinline__ void unpack_x(const float4 (&v4)[8], float (&xr)[32]) {
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    xr[4 * i] = v4[i].x; xr[4 * i + 1] = v4[i].y; xr[4 * i + 2] = v4[i].z; xr[4 * i + 3] = v4[i].w;
-  }
+// Block scales s_2u, s_2u+1 of a unit: RN(e4m3 * g) from two scale bytes.
+__device__ __forceinline__ float2 unit_scales(uint32_t sv, float g) {
+  const float2 e = e4m3x2_to_f32x2(sv);
+  return make_float2(e.x * g, e.y * g);
 }
 
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -222,30 +230,54 @@ __device__ __forceinline__ void grid_dep_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-template <int ROUNDS>
-__global__ void __launch_bounds__(160, 3) nvfp4_gemv_tma(GemvBatch p, TmaCfg c) {
+// The CTA's items: row blocks [blk, blk_end) of the flattened (active job,
+// block) space, cut at job ends and at kb blocks.
+struct ItemSeq {
+  int blk, blk_end;
+};
+
+__device__ __forceinline__ void cta_blocks(int total, ItemSeq& q) {
+  const int G = gridDim.x, b = blockIdx.x;
+  const int per = total / G, rem = total % G;
+  q.blk = b * per + min(b, rem);
+  q.blk_end = q.blk + per + (b < rem ? 1 : 0);
+}
+
+__device__ __forceinline__ bool next_item(ItemSeq& q, const TmaCfg& c, const int* jlist, int rows,
+                                          int& job, int& r0, int& nrows) {
+  if (q.blk >= q.blk_end) return false;
+  const int ji = q.blk / c.bpj, jb = q.blk - ji * c.bpj;
+  const int n = min(c.kb, min(c.bpj - jb, q.blk_end - q.blk));
+  job = jlist[ji];
+  r0 = jb * c.rs;
+  nrows = min(n * c.rs, rows - r0);
+  q.blk += n;
+  return true;
+}
+
+__global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCfg c) {
   extern __shared__ __align__(128) uint8_t smem[];
-  constexpr int NC = 128;  // consumer threads
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x;
   const int S = c.stages;
 
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + S;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [S], S <= 8
+  uint64_t* empty = full + 8;                         // [S]
   const uint8_t** jc = reinterpret_cast<const uint8_t**>(smem + 128);
   const uint8_t** js = jc + kMaxJobs;
-  float* jg = reinterpret_cast<float*>(js + kMaxJobs);
-  float* luts = reinterpret_cast<float*>(smem + 448);  // [njobs][256]
+  float* jg = reinterpret_cast<float*>(smem + 384);
+  int* jlist = reinterpret_cast<int*>(smem + 448);
+  int* nact = jlist + kMaxJobs;
   float* part = reinterpret_cast<float*>(smem + c.part_off);
+  float4* xt = reinterpret_cast<float4*>(smem + c.xt_off);
   uint8_t* stages = smem + c.stage_base;
 
   if (tid == 0) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(&full[i], c.stage_x ? 2 : 1);
-      mbar_init(&empty[i], NC / 32);
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
     }
     fence_mbar_init();
   }
-  for (int i = tid; i < 2 * kRt * kRowPitch; i += blockDim.x) part[i] = 0.0f;
   // Slot / id tables and globals: readable now if they were produced before
   // the predecessor kernel, otherwise only after the dependency wait.
   if (!p.ids_ready) grid_dep_wait();
@@ -257,29 +289,27 @@ __global__ void __launch_bounds__(160, 3) nvfp4_gemv_tma(GemvBatch p, TmaCfg c) 
     js[tid] = ss;
     jg[tid] = g;
   }
-  __syncthreads();
-  for (int i = tid; i < p.njobs * 256; i += blockDim.x)
-    luts[i] = e4m3_lut_value((uint32_t)(i & 255)) * jg[i >> 8];
+  if (tid == 0) {
+    int n = 0;
+    for (int j = 0; j < p.njobs; ++j)
+      if (job_active(p, j)) jlist[n++] = j;
+    *nact = n;
+  }
   __syncthreads();
 
-  const int cols = p.cols;
-  const int cb = cols >> 1, sb = cols >> 4;
+  const int cb = p.cols >> 1, sb = p.cols >> 4;
+  ItemSeq q;
+  cta_blocks(*nact * c.bpj, q);
 
   // ------------------------------------------------------------ producer
-  if (warp == NC / 32) {
-    int it = 0;
-    bool waited = false;
-    for (int T = blockIdx.x; T < c.ntiles; T += gridDim.x) {
-      int job, rb;
-      item_of(c, T, job, rb);
-      if (!job_active(p, job)) continue;
-      const int st = it % S;
-      if (!mbar_wait(&empty[st], ((it / S) & 1) ^ 1)) break;
-      ++it;
-      const int r0 = rb * kRt;
-      const int nrows = min(kRt, p.rows - r0);
-      uint8_t* dst = stages + (size_t)st * c.stage_bytes;
-      if (lane == 0) {
+  if (tid >= kCT) {
+    if (tid == kCT) {
+      int it = 0, job, r0, nrows;
+      while (next_item(q, c, jlist, p.rows, job, r0, nrows)) {
+        const int st = it % S;
+        if (!mbar_wait(&empty[st], ((it / S) & 1) ^ 1)) break;
+        ++it;
+        uint8_t* dst = stages + (size_t)st * c.stage_bytes;
         const uint32_t code_bytes = (uint32_t)(nrows * cb);
         const uint32_t scale_bytes = (uint32_t)(nrows * sb);
         const uint32_t s16 = scale_bytes & ~15u;
@@ -290,131 +320,119 @@ __global__ void __launch_bounds__(160, 3) nvfp4_gemv_tma(GemvBatch p, TmaCfg c) 
         bulk_g2s(dst, jc[job] + (size_t)r0 * cb, code_bytes, &full[st]);
         if (s16) bulk_g2s(dst + c.scale_off, ssrc, s16, &full[st]);
       }
-      if (c.stage_x) {
-        if (!waited) { grid_dep_wait(); waited = true; }
-        const float4* src = reinterpret_cast<const float4*>(p.job[job].x);
-        float4* xs = reinterpret_cast<float4*>(dst + c.x_off);
-        for (int f = lane; f < (cols >> 2); f += 32) {
-          const int u = f >> 3, i = f & 7;
-          xs[u * 8 + ((i + u) & 7)] = src[f];
-        }
-        __threadfence_block();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&full[st]);
-      }
-    }
-    if (lane == 0)  // leave no bulk copy in flight: wait (bounded) for the last stages
+      // Leave no bulk copy in flight: wait (bounded) for the last stages.
       for (int k = (it > S ? it - S : 0); k < it; ++k) mbar_wait(&full[k % S], (k / S) & 1);
-    if (!waited) grid_dep_wait();
+    }
+    grid_dep_wait();
     grid_dep_launch();
     return;
   }
 
   // ----------------------------------------------------------- consumers
-  grid_dep_wait();  // activations / residual are written by the predecessor
+  grid_dep_wait();  // activations / base / residual come from the predecessor
   grid_dep_launch();
-  const int row_off = tid / c.gw, cg = tid % c.gw;
-  const bool active = row_off < c.p_rows;
-  float xr[ROUNDS][32];
-#pragma unroll
-  for (int i = 0; i < ROUNDS; ++i)
-#pragma unroll
-    for (int m = 0; m < 32; ++m) xr[i][m] = 0.0f;
-  const float* cur_x = nullptr;
-  // The tree runs on warps 1 and 3: with 64 chain groups per row these hold
-  // groups 32..63, which have no second round when 64 < cols/32 <= 128, so
-  // the tree lands on the warps with the least decode work.
-  const bool tree_warp = (warp & 1) == 1;
-  const int tt = ((warp >> 1) << 5) | lane;  // 0..63 over warps 1 and 3
-  const int tr = tt >> 3, tw = tt & 7;
+  for (int i = tid; i < (c.kb * c.rs) * kRowPitch; i += kCT) part[i] = 0.0f;
 
-  int it = 0;
-  for (int T = blockIdx.x; T < c.ntiles; T += gridDim.x) {
-    int job, rb;
-    item_of(c, T, job, rb);
-    if (!job_active(p, job)) continue;
-    const int cur = it++;
-    const int st = cur % S, pb = cur & 1;
-    const int r0 = rb * kRt;
-    const int nrows = min(kRt, p.rows - r0);
+  const int g = tid % c.gw, ro = tid / c.gw;
+  const bool has_u = g < c.n_u;
+  const int tr = tid >> 3, tw = tid & 7;
+  float xr[32];
+#pragma unroll
+  for (int m = 0; m < 32; ++m) xr[m] = 0.0f;
+  const float* cur_x = nullptr;
+  named_bar_sync(kBarC, kCT);
+
+  int it = 0, job, r0, nrows;
+  while (next_item(q, c, jlist, p.rows, job, r0, nrows)) {
+    const int st = it % S;
+    const uint32_t ph = (it / S) & 1;
+    ++it;
     const GemvJob& J = p.job[job];
-    if (!c.stage_x && J.x != cur_x) {
-      if (active) {
+    if (J.x != cur_x) {
+      if (has_u) {
+        const float4* src = reinterpret_cast<const float4*>(J.x) + 8 * g;
 #pragma unroll
-        for (int i = 0; i < ROUNDS; ++i) {
-          const int u = cg + 64 * i;
-          if (u < c.n_u) {
-            const float4* src = reinterpret_cast<const float4*>(J.x + 32 * u);
-            float4 v4[8];
-#pragma unroll
-            for (int m = 0; m < 8; ++m) v4[m] = src[m];
-            unpack_x(v4, xr[i]);
-          }
+        for (int i = 0; i < 8; ++i) {
+          const float4 v = __ldg(src + i);
+          xr[4 * i] = v.x; xr[4 * i + 1] = v.y; xr[4 * i + 2] = v.z; xr[4 * i + 3] = v.w;
         }
+      }
+      // tail activation, float4 i of tail unit t at t*8 + (i ^ (t & 7)); read
+      // after the barrier that precedes the tail phase
+      const float4* src = reinterpret_cast<const float4*>(J.x) + 8 * 64;
+      for (int f = tid; f < c.n_tail * 8; f += kCT) {
+        const int t = f >> 3, i = f & 7;
+        xt[t * 8 + (i ^ (t & 7))] = __ldg(src + f);
       }
       cur_x = J.x;
     }
-    const bool to = !mbar_wait(&full[st], (cur / S) & 1);
+    const float gs = jg[job];
+    const bool to = !mbar_wait(&full[st], ph);
     const uint8_t* stage = stages + (size_t)st * c.stage_bytes;
-    if (active && !to) {
-      if (c.stage_x) {
-        const float4* xs = reinterpret_cast<const float4*>(stage + c.x_off);
-#pragma unroll
-        for (int i = 0; i < ROUNDS; ++i) {
-          const int u = cg + 64 * i;
-          if (u < c.n_u) {
-            float4 v4[8];
-#pragma unroll
-            for (int m = 0; m < 8; ++m) v4[m] = xs[u * 8 + ((m + u) & 7)];
-            unpack_x(v4, xr[i]);
-          }
-        }
-      }
-      const float* lut = luts + job * 256;
-      float* pbuf = part + pb * kRt * kRowPitch;
+
+    // round 1: unit g of rows ro, ro + rs, ...
+    if (has_u) {
 #pragma unroll 2
-      for (int rr = row_off; rr < nrows; rr += c.p_rows) {
+      for (int row = ro; row < nrows; row += c.rs) {
+        const uint4 qv = *reinterpret_cast<const uint4*>(stage + row * cb + 16 * g);
+        const uint32_t sv = *reinterpret_cast<const uint16_t*>(stage + c.scale_off + row * sb + 2 * g);
+        const float2 s = unit_scales(sv, gs);
         float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-        for (int i = 0; i < ROUNDS; ++i) {
-          const int u = cg + 64 * i;
-          if (i == 0 || u < c.n_u) {
-            const uint4 q = *reinterpret_cast<const uint4*>(stage + rr * cb + 16 * u);
-            const uint32_t sv = *reinterpret_cast<const uint16_t*>(stage + c.scale_off + rr * sb + 2 * u);
-            unit_fma(q, lut[sv & 0xFFu], lut[sv >> 8], xr[i], acc);
-          }
-        }
-        *reinterpret_cast<float4*>(pbuf + rr * kRowPitch + part_index(4 * cg)) =
+        unit_fma(qv, s.x, s.y, xr, acc);
+        *reinterpret_cast<float4*>(part + row * kRowPitch + part_index(4 * g)) =
             make_float4(acc[0], acc[1], acc[2], acc[3]);
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
-    if (named_bar_or(1, NC, to)) break;
+    // tail: continuations (row, c) over unit 64 + c, spread over all threads
+    if (c.n_tail > 0) {
+      named_bar_sync(kBarC, kCT);
+      const int ntask = nrows * c.n_tail;
+      for (int k = tid; k < ntask; k += kCT) {
+        const int row = k / c.n_tail, t = k - row * c.n_tail;
+        const int u = 64 + t;
+        float4* pp = reinterpret_cast<float4*>(part + row * kRowPitch + part_index(4 * t));
+        const float4 a = *pp;
+        float acc[4] = {a.x, a.y, a.z, a.w};
+        float x2[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 v = xt[t * 8 + (i ^ (t & 7))];
+          x2[4 * i] = v.x; x2[4 * i + 1] = v.y; x2[4 * i + 2] = v.z; x2[4 * i + 3] = v.w;
+        }
+        const uint4 qv = *reinterpret_cast<const uint4*>(stage + row * cb + 16 * u);
+        const uint32_t sv = *reinterpret_cast<const uint16_t*>(stage + c.scale_off + row * sb + 2 * u);
+        const float2 s = unit_scales(sv, gs);
+        unit_fma(qv, s.x, s.y, x2, acc);
+        *pp = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      }
+    }
+    // every read of the stage is done; a timeout anywhere stops all consumers
+    const bool stop = named_bar_or(kBarC, kCT, to);
+    if (tid == 0) mbar_arrive(&empty[st]);
+    if (stop) break;
 
-    if (tree_warp) {
-      const float* pbuf = part + pb * kRt * kRowPitch;
-      float y = 0.0f;
-      if (tr < nrows) y = group_tree(pbuf + tr * kRowPitch + tw * kGroupPitch);
-      y = combine8(legacy_fix(y, p.legacy_tree));
-      if (tw == 0 && tr < nrows) {
-        const int r = r0 + tr;
-        if (p.mode == 0) {
-          J.out[r] = epilogue(y, p.relu2, p.out_scale);
-        } else {
-          p.contrib[(size_t)job * p.rows + r] = y;
+    // tree: thread (row tr, segment tw)
+    float y = 0.0f;
+    if (tr < nrows) y = group_tree(part + tr * kRowPitch + tw * kGroupPitch);
+    y = combine8(legacy_fix(y, p.legacy_tree));
+    if (tw == 0 && tr < nrows) {
+      const int r = r0 + tr;
+      if (p.mode == 0) {
+        J.out[r] = epilogue(y, p.relu2, p.out_scale);
+      } else {
+        p.contrib[(size_t)job * p.rows + r] = y;
+        __threadfence();
+        if (atomicAdd(&p.row_count[r], 1) == p.njobs - 1) {
           __threadfence();
-          if (atomicAdd(&p.row_count[r], 1) == p.njobs - 1) {
-            __threadfence();
-            float acc = p.base ? p.base[r] : 0.0f;
-            for (int s = 0; s < p.njobs; ++s)
-              acc = fmaf(__ldcg(&p.contrib[(size_t)s * p.rows + r]), p.route_w[s], acc);
-            p.rs_out[r] = p.resid ? p.resid[r] + acc : acc;
-            p.row_count[r] = 0;
-          }
+          float acc = p.base ? p.base[r] : 0.0f;
+          for (int s = 0; s < p.njobs; ++s)
+            acc = fmaf(__ldcg(&p.contrib[(size_t)s * p.rows + r]), p.route_w[s], acc);
+          p.rs_out[r] = p.resid ? p.resid[r] + acc : acc;
+          p.row_count[r] = 0;
         }
       }
     }
+    named_bar_sync(kBarC, kCT);  // the chain buffer is rewritten by the next item
   }
 }
 
@@ -452,7 +470,10 @@ int set_smem(K kernel, int bytes) {
 }
 
 bool tma_ok(const GemvBatch& b) {
+  // Stage copies start at row blocks of rs rows: 16-byte aligned scale rows
+  // need rs * cols / 16 % 16 == 0 (rs = 4 when cols > 1024, else 8).
   if (b.cols % 32 != 0 || b.cols > 4096) return false;
+  if (b.cols > 1024 && b.cols % 64 != 0) return false;
   if (b.mode == 1 && (!b.contrib || !b.row_count)) return false;
   for (int j = 0; j < b.njobs; ++j) {
     const MatRef& m = b.job[j].mat;
@@ -478,43 +499,46 @@ int launch_ex(K kernel, dim3 grid, dim3 block, int smem, cudaStream_t stream, bo
   return cudaLaunchKernelEx(&cfg, kernel, b, c) == cudaSuccess ? kOk : kErrLaunch;
 }
 
-constexpr int kCtasPerSm = 3;
+constexpr int kCtasPerSm = 2;
 
 int launch_tma(const GemvBatch& b, cudaStream_t stream) {
   const DevInfo& di = dev_info();
   TmaCfg c{};
   c.n_u = b.cols / 32;
-  c.gw = c.n_u < 64 ? c.n_u : 64;
-  const int rounds = (c.n_u + 63) / 64;
-  const int NC = 128;
-  c.p_rows = NC / c.gw;
+  c.n_tail = c.n_u > 64 ? c.n_u - 64 : 0;
+  c.gw = c.n_u > 32 ? 64 : 32;
+  c.rs = kCT / c.gw;
   const int cb = b.cols / 2, sb = b.cols / 16;
-  c.stage_x = b.mode == 1 ? 1 : 0;
-  c.part_off = align_up(448 + b.njobs * 1024, 16);
-  c.stage_base = align_up(c.part_off + 2 * kRt * kRowPitch * 4, 128);
-  c.scale_off = kRt * cb;
-  c.x_off = c.scale_off + align_up(kRt * sb, 16);
-  c.stage_bytes = align_up(c.x_off + (c.stage_x ? b.cols * 4 : 0), 128);
   const int budget = (di.smem_sm - kCtasPerSm * 1024) / kCtasPerSm;
+  // Largest item (<= 32 rows, a multiple of rs) whose chain buffer and two
+  // stages fit two CTAs per SM.
+  int krt = 0;
+  for (int cand = 32; cand >= c.rs; cand -= c.rs) {
+    const int part_off = 576;  // after barriers, job tables and the active-job list
+    const int xt_off = align_up(part_off + cand * kRowPitch * 4, 16);
+    const int base = align_up(xt_off + c.n_tail * 128, 128);
+    const int stage = align_up(cand * cb + align_up(cand * sb, 16), 128);
+    if (base + 2 * stage <= budget) {
+      krt = cand;
+      c.part_off = part_off;
+      c.xt_off = xt_off;
+      c.stage_base = base;
+      c.scale_off = cand * cb;
+      c.stage_bytes = stage;
+      break;
+    }
+  }
+  if (krt == 0) return kErrShape;
+  c.kb = krt / c.rs;
   c.stages = (budget - c.stage_base) / c.stage_bytes;
-  if (c.stages > 6) c.stages = 6;
-  if (c.stages < 2) {
-    c.stages = 2;
-    if (c.stage_base + 2 * c.stage_bytes > di.smem_optin) return kErrShape;
-  }
+  if (c.stages > 4) c.stages = 4;
   const int smem = c.stage_base + c.stages * c.stage_bytes;
-  c.tiles_per_job = (b.rows + kRt - 1) / kRt;
-  c.ntiles = c.tiles_per_job * b.njobs;
+  c.bpj = (b.rows + c.rs - 1) / c.rs;
+  const int total = c.bpj * b.njobs;  // upper bound (inactive jobs drop out on the device)
   int grid = di.sms * kCtasPerSm;
-  if (grid > c.ntiles) grid = c.ntiles;
-  const dim3 block(NC + 32);
-  const bool pdl = b.pdl != 0;
-  if (rounds == 1) {
-    if (set_smem(nvfp4_gemv_tma<1>, smem)) return kErrLaunch;
-    return launch_ex(nvfp4_gemv_tma<1>, dim3(grid), block, smem, stream, pdl, b, c);
-  }
-  if (set_smem(nvfp4_gemv_tma<2>, smem)) return kErrLaunch;
-  return launch_ex(nvfp4_gemv_tma<2>, dim3(grid), block, smem, stream, pdl, b, c);
+  if (grid > total) grid = total;
+  if (set_smem(nvfp4_gemv_tma, smem)) return kErrLaunch;
+  return launch_ex(nvfp4_gemv_tma, dim3(grid), dim3(kCT + 32), smem, stream, b.pdl != 0, b, c);
 }
 
 template <int W>
