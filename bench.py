@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--gemv", type=int, nargs=2, metavar=("ROWS", "COLS"),
+                    help="time one NVFP4 GEMV shape instead of the decode step")
     return ap.parse_args()
 
 
@@ -185,36 +187,39 @@ def kernel_roofline(dec, bank, device, hbm, iters=192):
     return res
 
 
-def gemv_config0(device, hbm):
-    """Config 0 (one 1856x2688 NVFP4 GEMV) over an L2-cold replica pool
-    (>= 8 x L2), B200 schedule, CUDA-event time per call."""
+def gemv_shape(device, hbm, rows=INTER, cols=HIDDEN, min_iters=64):
+    """One NVFP4 GEMV [rows x cols] (config 0 by default) cycling over a
+    replica pool of >= 8 x L2 (L2-cold weights; one copy when a single matrix
+    already exceeds that), B200 schedule, CUDA-event time per call.
+    Algorithmic bytes per call: codes + scales + global scale + x + out."""
     from ervf_b200 import FusedNVFP4
     from ervf_b200.formats import quantize_nvfp4_torch
 
     f = FusedNVFP4(device=device)
     gen = torch.Generator(device=device)
     gen.manual_seed(0)
-    codes, scales, gsc = quantize_nvfp4_torch(torch.randn(INTER, HIDDEN, generator=gen,
+    codes, scales, gsc = quantize_nvfp4_torch(torch.randn(rows, cols, generator=gen,
                                                           device=device) * 0.02)
     l2 = torch.cuda.get_device_properties(device).L2_cache_size
     rec = codes.numel() + scales.numel()
-    n = max(8, (8 * l2) // rec + 1)
+    n = max(1, (8 * l2) // rec + 1) if rec < 2 * l2 else 2
     pc = codes.reshape(1, -1).repeat(n, 1)
     ps = scales.reshape(1, -1).repeat(n, 1)
-    x = torch.randn(HIDDEN, device=device)
-    out = torch.zeros(INTER, device=device)
+    del codes, scales
+    x = torch.randn(cols, device=device)
+    out = torch.zeros(rows, device=device)
     g = float(gsc)
 
     def call(i):
         j = i % n
-        f.gemv_into(out, pc[j], ps[j], x, g, INTER, HIDDEN, apply_relu2=True)
+        f.gemv_into(out, pc[j], ps[j], x, g, rows, cols, apply_relu2=True)
 
     for i in range(10):
         call(i)
-    iters = 4 * n
+    iters = max(min_iters, 4 * n)
     ms = time_region(call, iters, device) / iters
-    algo = rec + 4 + HIDDEN * 4 + INTER * 4
-    return {"rows": INTER, "cols": HIDDEN, "us": ms * 1e3, "gbs": algo / ms / 1e6,
+    algo = rec + 4 + cols * 4 + rows * 4
+    return {"rows": rows, "cols": cols, "us": ms * 1e3, "gbs": algo / ms / 1e6,
             "frac": algo / ms / 1e6 / hbm, "pool_replicas": n, "bytes_per_call": algo}
 
 
@@ -305,6 +310,11 @@ def main():
 
     build.build()
     hbm, peak_kind = peaks()
+    if args.gemv:
+        r = gemv_shape(device, hbm, args.gemv[0], args.gemv[1])
+        r.update({"peak_gbs": hbm, "peak_kind": peak_kind})
+        print(json.dumps({"gemv": r}))
+        return
     L = args.layers
     t0 = time.time()
     bank = ExpertBank(L, N_EXPERTS, HIDDEN, INTER, device)
@@ -411,7 +421,7 @@ def main():
     e2e_value = args.steps / (float(e_t.item()) / 1e3)
 
     kern = kernel_roofline(dec, bank, device, hbm) if world == 1 else None
-    gemv0 = gemv_config0(device, hbm) if (world == 1 and rank == 0) else None
+    gemv0 = gemv_shape(device, hbm) if (world == 1 and rank == 0) else None
 
     if rank == 0:
         # bytes one token streams: distinct (layer, expert) pairs x expert bytes

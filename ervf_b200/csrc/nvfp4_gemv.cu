@@ -145,8 +145,8 @@ __global__ void __launch_bounds__(256) nvfp4_gemv_sched(GemvBatch p, int tiles_p
 // ======================================================================
 //
 // CTA = 8 consumer warps + 1 producer warp, two CTAs per SM.  Each CTA owns a
-// contiguous, balanced range of "row blocks" (rs consecutive rows of one job)
-// over the launch's active jobs and walks it in items of up to kRt rows.
+// contiguous, balanced range of row blocks over the launch's active jobs and
+// walks it in items of up to kRt rows.
 //
 // Producer warp (lane 0): per item, one bulk copy of the item's code rows and
 // one of its scale rows (cp.async.bulk, no multicast) into a ring of stages
@@ -154,27 +154,29 @@ __global__ void __launch_bounds__(256) nvfp4_gemv_sched(GemvBatch p, int tiles_p
 // mbarrier.  Weight streaming starts before the dependency wait of a
 // programmatic launch (the weights do not depend on the predecessor).
 //
-// Consumer thread (row slot ro, chain group g), gw groups per row slot (64,
-// or 32 when cols <= 1024) and rs = 256 / gw row slots: chain group g is the
-// reference's chains 4g..4g+3, whose first code unit is unit g (16 bytes =
-// 4 chains x 8 codes).  The activation of unit g lives in the thread's
-// registers for as long as the job does not change.
-//   round 1: rows ro, ro + rs, ... of the item, unit g: decode with the
-//            hardware e2m1x2 / e4m3x2 converters, w = RN(e2m1 * s) (FMUL),
-//            acc = fmaf(w, x, acc) (FFMA) in the reference's order; the four
-//            chain values go to the item's chain buffer.
-//   tail:    cols > 2048 gives chain groups c < n_u - 64 a second unit
-//            64 + c.  Those (row, c) continuations are spread evenly over all
-//            256 threads: each reads the chain values of round 1, continues
-//            them over unit 64 + c (activation from a swizzled shared copy)
-//            and writes them back.  With kRt = 24 rows and cols = 2688 every
-//            thread has 6 + 2 units per item, 98 % of an even split.
-//   tree:    thread (row tr, segment tw) reduces chains 32tw..32tw+31 of its
-//            row with the reference's shuffle tree (offsets 16..1) and eight
-//            lanes combine ((S0+S4)+(S2+S6))+((S1+S5)+(S3+S7)).
+// Consumers: a row of n_u code units (16 bytes = 4 chains x 8 codes each) has
+// 64 chain groups; group c (the reference's chains 4c..4c+3) covers unit c
+// and, when cols > 2048, unit 64 + c (its second round, which continues the
+// same four chains).  The consumer threads form T = 256 / n_u teams of n_u
+// threads; team k owns rows k + T*j, j < 2H, of every item (kRt = T * 2H),
+// interleaved so that a partial item splits evenly, and every team thread
+// runs exactly two "segments" of H rows (even j, or odd j) x one unit:
+//   thread m <  n2          : group m,    even rows: unit m, then unit 64+m
+//   thread n2 <= m < 2*n2   : group m-n2, odd rows:  unit c, then unit 64+c
+//   thread m >= 2*n2        : group m-n2, even rows, then odd rows, unit c
+// with n2 = n_u - 64 groups that have a second unit.  Every thread therefore
+// does 2H unit-rows per item (an even split of the row's n_u units).  The
+// segment's activation (32 values) is read into registers from a swizzled
+// shared copy of x (kept across items when both segments use one unit);
+// codes and block scales are decoded with the sm_100a
+// e2m1x2 / e4m3x2 converters, w = RN(e2m1 * s) (FMUL) and acc = fmaf(w, x,
+// acc) (FFMA) in the reference's order.  Chain values go to the item's chain
+// buffer; after a consumer barrier thread (row tr, segment tw) reduces chains
+// 32tw..32tw+31 of its row with the reference's shuffle tree (offsets 16..1)
+// and eight lanes combine ((S0+S4)+(S2+S6))+((S1+S5)+(S3+S7)).
 //
 // mode 1 (routed sum): the tree lane of a row writes the job's row value y_s
-// to contrib[s][row], publishes it (release fence + per-row atomic count), and
+// to contrib[s][row], publishes it (acq_rel atomic on a per-row count), and
 // the lane that completes a row's count adds the row up in ROUTE order,
 // acc = fmaf(y_s, w_s, acc) for s = 0..njobs-1 from base or 0, writes
 // resid + acc and resets the count -- the same sum as one thread walking the
@@ -189,13 +191,13 @@ struct TmaCfg {
   int stage_bytes;  // bytes per stage (128-aligned)
   int scale_off;    // scale rows inside a stage
   int part_off;     // chain buffer [kRt][kRowPitch] floats
-  int xt_off;       // tail activation [n_tail][8] float4, swizzled
+  int xs_off;       // activation [n_u][8] float4, swizzled
   int stage_base;
   int n_u;          // code units per row (cols / 32)
-  int n_tail;       // units per row beyond 64 (second-round units)
-  int gw;           // chain groups per row slot (64 or 32)
-  int rs;           // row slots (kCT / gw)
-  int kb;           // row blocks per item (kRt / rs)
+  int n2;           // chain groups with a second unit (n_u - 64, or 0)
+  int teams;        // T
+  int blk;          // rows per row block (4 or 8: 16-byte aligned scale rows)
+  int kb;           // row blocks per item (kRt / blk)
   int bpj;          // row blocks per job
 };
 
@@ -225,6 +227,69 @@ __device__ __forceinline__ float2 unit_scales(uint32_t sv, float g) {
   return make_float2(e.x * g, e.y * g);
 }
 
+// Row `row` of a stage, unit u: continue acc[0..3].
+__device__ __forceinline__ void stage_unit(const uint8_t* stage, int scale_off, int cb, int sb,
+                                           int row, int u, float g, const float (&x)[32],
+                                           float* acc) {
+  const uint4 qv = *reinterpret_cast<const uint4*>(stage + row * cb + 16 * u);
+  const uint32_t sv = *reinterpret_cast<const uint16_t*>(stage + scale_off + row * sb + 2 * u);
+  const float2 s = unit_scales(sv, g);
+  unit_fma(qv, s.x, s.y, x, acc);
+}
+
+// Activation of unit u from the swizzled shared copy (float4 i at u*8 + (i ^ (u & 7))).
+__device__ __forceinline__ void load_unit_x(const float4* xs, int u, float (&x)[32]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 v = xs[u * 8 + (i ^ (u & 7))];
+    x[4 * i] = v.x; x[4 * i + 1] = v.y; x[4 * i + 2] = v.z; x[4 * i + 3] = v.w;
+  }
+}
+
+// The two segments of one consumer thread for one item (see the schedule
+// above).  FULL: every row of the item exists, so the H rows of a segment run
+// unconditionally and interleave.
+template <int H, bool FULL>
+__device__ __forceinline__ void segments(const uint8_t* stage, int scale_off, int cb, int sb,
+                                         int team, int T, int par1, int par2, bool cont, int u1,
+                                         int u2, int grp, int nrows, float gs, const float4* xs,
+                                         float (&x)[32], bool& x_stale, float* part) {
+  float acc[H][4];
+#pragma unroll
+  for (int h = 0; h < H; ++h) acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.0f;
+  if (cont || x_stale) load_unit_x(xs, u1, x);
+  x_stale = false;
+#pragma unroll
+  for (int h = 0; h < H; ++h) {
+    const int row = team + T * (2 * h + par1);
+    if (FULL || row < nrows) stage_unit(stage, scale_off, cb, sb, row, u1, gs, x, acc[h]);
+  }
+  if (!cont) {
+#pragma unroll
+    for (int h = 0; h < H; ++h) {
+      const int row = team + T * (2 * h + par1);
+      if (FULL || row < nrows)
+        *reinterpret_cast<float4*>(part + row * kRowPitch + part_index(4 * grp)) =
+            make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+      acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.0f;
+    }
+  } else {
+    load_unit_x(xs, u2, x);
+  }
+#pragma unroll
+  for (int h = 0; h < H; ++h) {
+    const int row = team + T * (2 * h + par2);
+    if (FULL || row < nrows) stage_unit(stage, scale_off, cb, sb, row, u2, gs, x, acc[h]);
+  }
+#pragma unroll
+  for (int h = 0; h < H; ++h) {
+    const int row = team + T * (2 * h + par2);
+    if (FULL || row < nrows)
+      *reinterpret_cast<float4*>(part + row * kRowPitch + part_index(4 * grp)) =
+          make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+  }
+}
+
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -249,12 +314,13 @@ __device__ __forceinline__ bool next_item(ItemSeq& q, const TmaCfg& c, const int
   const int ji = q.blk / c.bpj, jb = q.blk - ji * c.bpj;
   const int n = min(c.kb, min(c.bpj - jb, q.blk_end - q.blk));
   job = jlist[ji];
-  r0 = jb * c.rs;
-  nrows = min(n * c.rs, rows - r0);
+  r0 = jb * c.blk;
+  nrows = min(n * c.blk, rows - r0);
   q.blk += n;
   return true;
 }
 
+template <int H>
 __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCfg c) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x;
@@ -268,7 +334,7 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
   int* jlist = reinterpret_cast<int*>(smem + 448);
   int* nact = jlist + kMaxJobs;
   float* part = reinterpret_cast<float*>(smem + c.part_off);
-  float4* xt = reinterpret_cast<float4*>(smem + c.xt_off);
+  float4* xs = reinterpret_cast<float4*>(smem + c.xs_off);
   uint8_t* stages = smem + c.stage_base;
 
   if (tid == 0) {
@@ -331,15 +397,26 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
   // ----------------------------------------------------------- consumers
   grid_dep_wait();  // activations / base / residual come from the predecessor
   grid_dep_launch();
-  for (int i = tid; i < (c.kb * c.rs) * kRowPitch; i += kCT) part[i] = 0.0f;
+  const int krt = c.teams * 2 * H;
+  for (int i = tid; i < krt * kRowPitch; i += kCT) part[i] = 0.0f;
 
-  const int g = tid % c.gw, ro = tid / c.gw;
-  const bool has_u = g < c.n_u;
+  // this thread's two segments (see the schedule above)
+  const int nu = c.n_u, n2 = c.n2;
+  const int team = tid / nu, m = tid - team * nu;
+  const bool active = team < c.teams;
+  const bool cont = m < 2 * n2;                // segment 2 continues segment 1
+  const int grp = m < n2 ? m : m - n2;         // chain group
+  const int u1 = grp, u2 = cont ? grp + 64 : grp;
+  // team rows team + T*j, j < 2H; segment rows j = 2h + parity
+  const int T = c.teams;
+  const int par1 = (m >= n2 && m < 2 * n2) ? 1 : 0;
+  const int par2 = cont ? par1 : 1;
   const int tr = tid >> 3, tw = tid & 7;
-  float xr[32];
-#pragma unroll
-  for (int m = 0; m < 32; ++m) xr[m] = 0.0f;
   const float* cur_x = nullptr;
+  // segment activation; a thread whose two segments share one unit keeps it
+  // in registers until the job's activation changes
+  float x[32];
+  bool x_stale = true;
   named_bar_sync(kBarC, kCT);
 
   int it = 0, job, r0, nrows;
@@ -348,62 +425,27 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
     const uint32_t ph = (it / S) & 1;
     ++it;
     const GemvJob& J = p.job[job];
-    if (J.x != cur_x) {
-      if (has_u) {
-        const float4* src = reinterpret_cast<const float4*>(J.x) + 8 * g;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 v = __ldg(src + i);
-          xr[4 * i] = v.x; xr[4 * i + 1] = v.y; xr[4 * i + 2] = v.z; xr[4 * i + 3] = v.w;
-        }
-      }
-      // tail activation, float4 i of tail unit t at t*8 + (i ^ (t & 7)); read
-      // after the barrier that precedes the tail phase
-      const float4* src = reinterpret_cast<const float4*>(J.x) + 8 * 64;
-      for (int f = tid; f < c.n_tail * 8; f += kCT) {
+    if (J.x != cur_x) {  // the previous item ended with a consumer barrier
+      const float4* src = reinterpret_cast<const float4*>(J.x);
+      for (int f = tid; f < nu * 8; f += kCT) {
         const int t = f >> 3, i = f & 7;
-        xt[t * 8 + (i ^ (t & 7))] = __ldg(src + f);
+        xs[t * 8 + (i ^ (t & 7))] = __ldg(src + f);
       }
+      named_bar_sync(kBarC, kCT);
       cur_x = J.x;
+      x_stale = true;
     }
     const float gs = jg[job];
     const bool to = !mbar_wait(&full[st], ph);
     const uint8_t* stage = stages + (size_t)st * c.stage_bytes;
 
-    // round 1: unit g of rows ro, ro + rs, ...
-    if (has_u) {
-#pragma unroll 2
-      for (int row = ro; row < nrows; row += c.rs) {
-        const uint4 qv = *reinterpret_cast<const uint4*>(stage + row * cb + 16 * g);
-        const uint32_t sv = *reinterpret_cast<const uint16_t*>(stage + c.scale_off + row * sb + 2 * g);
-        const float2 s = unit_scales(sv, gs);
-        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        unit_fma(qv, s.x, s.y, xr, acc);
-        *reinterpret_cast<float4*>(part + row * kRowPitch + part_index(4 * g)) =
-            make_float4(acc[0], acc[1], acc[2], acc[3]);
-      }
-    }
-    // tail: continuations (row, c) over unit 64 + c, spread over all threads
-    if (c.n_tail > 0) {
-      named_bar_sync(kBarC, kCT);
-      const int ntask = nrows * c.n_tail;
-      for (int k = tid; k < ntask; k += kCT) {
-        const int row = k / c.n_tail, t = k - row * c.n_tail;
-        const int u = 64 + t;
-        float4* pp = reinterpret_cast<float4*>(part + row * kRowPitch + part_index(4 * t));
-        const float4 a = *pp;
-        float acc[4] = {a.x, a.y, a.z, a.w};
-        float x2[32];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 v = xt[t * 8 + (i ^ (t & 7))];
-          x2[4 * i] = v.x; x2[4 * i + 1] = v.y; x2[4 * i + 2] = v.z; x2[4 * i + 3] = v.w;
-        }
-        const uint4 qv = *reinterpret_cast<const uint4*>(stage + row * cb + 16 * u);
-        const uint32_t sv = *reinterpret_cast<const uint16_t*>(stage + c.scale_off + row * sb + 2 * u);
-        const float2 s = unit_scales(sv, gs);
-        unit_fma(qv, s.x, s.y, x2, acc);
-        *pp = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    if (active) {
+      if (nrows == krt) {
+        segments<H, true>(stage, c.scale_off, cb, sb, team, T, par1, par2, cont, u1, u2, grp, nrows,
+                          gs, xs, x, x_stale, part);
+      } else {
+        segments<H, false>(stage, c.scale_off, cb, sb, team, T, par1, par2, cont, u1, u2, grp, nrows,
+                           gs, xs, x, x_stale, part);
       }
     }
     // every read of the stage is done; a timeout anywhere stops all consumers
@@ -415,15 +457,16 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
     float y = 0.0f;
     if (tr < nrows) y = group_tree(part + tr * kRowPitch + tw * kGroupPitch);
     y = combine8(legacy_fix(y, p.legacy_tree));
+    named_bar_sync(kBarC, kCT);  // the chain buffer is rewritten by the next item
     if (tw == 0 && tr < nrows) {
       const int r = r0 + tr;
       if (p.mode == 0) {
         J.out[r] = epilogue(y, p.relu2, p.out_scale);
       } else {
         p.contrib[(size_t)job * p.rows + r] = y;
-        __threadfence();
-        if (atomicAdd(&p.row_count[r], 1) == p.njobs - 1) {
-          __threadfence();
+        unsigned old_cnt;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old_cnt) : "l"(&p.row_count[r]) : "memory");
+        if ((int)old_cnt == p.njobs - 1) {
           float acc = p.base ? p.base[r] : 0.0f;
           for (int s = 0; s < p.njobs; ++s)
             acc = fmaf(__ldcg(&p.contrib[(size_t)s * p.rows + r]), p.route_w[s], acc);
@@ -432,7 +475,6 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
         }
       }
     }
-    named_bar_sync(kBarC, kCT);  // the chain buffer is rewritten by the next item
   }
 }
 
@@ -470,10 +512,7 @@ int set_smem(K kernel, int bytes) {
 }
 
 bool tma_ok(const GemvBatch& b) {
-  // Stage copies start at row blocks of rs rows: 16-byte aligned scale rows
-  // need rs * cols / 16 % 16 == 0 (rs = 4 when cols > 1024, else 8).
   if (b.cols % 32 != 0 || b.cols > 4096) return false;
-  if (b.cols > 1024 && b.cols % 64 != 0) return false;
   if (b.mode == 1 && (!b.contrib || !b.row_count)) return false;
   for (int j = 0; j < b.njobs; ++j) {
     const MatRef& m = b.job[j].mat;
@@ -501,44 +540,58 @@ int launch_ex(K kernel, dim3 grid, dim3 block, int smem, cudaStream_t stream, bo
 
 constexpr int kCtasPerSm = 2;
 
+template <int H>
+int launch_h(const GemvBatch& b, const TmaCfg& c, int smem, cudaStream_t stream) {
+  const int total = c.bpj * b.njobs;  // upper bound (inactive jobs drop out on the device)
+  int grid = dev_info().sms * kCtasPerSm;
+  if (grid > total) grid = total;
+  if (set_smem(nvfp4_gemv_tma<H>, smem)) return kErrLaunch;
+  return launch_ex(nvfp4_gemv_tma<H>, dim3(grid), dim3(kCT + 32), smem, stream, b.pdl != 0, b, c);
+}
+
 int launch_tma(const GemvBatch& b, cudaStream_t stream) {
   const DevInfo& di = dev_info();
   TmaCfg c{};
   c.n_u = b.cols / 32;
-  c.n_tail = c.n_u > 64 ? c.n_u - 64 : 0;
-  c.gw = c.n_u > 32 ? 64 : 32;
-  c.rs = kCT / c.gw;
+  c.n2 = c.n_u > 64 ? c.n_u - 64 : 0;
+  c.teams = kCT / c.n_u;
+  if (c.teams > 16) c.teams = 16;
+  // Scale rows of a block start 16-byte aligned: blk * cols / 16 % 16 == 0.
+  c.blk = (b.cols % 64 == 0) ? 4 : 8;
   const int cb = b.cols / 2, sb = b.cols / 16;
   const int budget = (di.smem_sm - kCtasPerSm * 1024) / kCtasPerSm;
-  // Largest item (<= 32 rows, a multiple of rs) whose chain buffer and two
-  // stages fit two CTAs per SM.
-  int krt = 0;
-  for (int cand = 32; cand >= c.rs; cand -= c.rs) {
+  // Largest H (rows per segment) whose chain buffer, activation and two
+  // stages fit two CTAs per SM, with kRt = teams * 2H <= 32 rows.
+  int h = 0;
+  for (int cand = 4; cand >= 1; --cand) {
+    const int krt = c.teams * 2 * cand;
+    if (krt > 32 || krt % c.blk != 0) continue;
     const int part_off = 576;  // after barriers, job tables and the active-job list
-    const int xt_off = align_up(part_off + cand * kRowPitch * 4, 16);
-    const int base = align_up(xt_off + c.n_tail * 128, 128);
-    const int stage = align_up(cand * cb + align_up(cand * sb, 16), 128);
+    const int xs_off = align_up(part_off + krt * kRowPitch * 4, 16);
+    const int base = align_up(xs_off + c.n_u * 128, 128);
+    const int stage = align_up(krt * cb + align_up(krt * sb, 16), 128);
     if (base + 2 * stage <= budget) {
-      krt = cand;
+      h = cand;
       c.part_off = part_off;
-      c.xt_off = xt_off;
+      c.xs_off = xs_off;
       c.stage_base = base;
-      c.scale_off = cand * cb;
+      c.scale_off = krt * cb;
       c.stage_bytes = stage;
+      c.kb = krt / c.blk;
       break;
     }
   }
-  if (krt == 0) return kErrShape;
-  c.kb = krt / c.rs;
+  if (h == 0) return kErrShape;
   c.stages = (budget - c.stage_base) / c.stage_bytes;
   if (c.stages > 4) c.stages = 4;
   const int smem = c.stage_base + c.stages * c.stage_bytes;
-  c.bpj = (b.rows + c.rs - 1) / c.rs;
-  const int total = c.bpj * b.njobs;  // upper bound (inactive jobs drop out on the device)
-  int grid = di.sms * kCtasPerSm;
-  if (grid > total) grid = total;
-  if (set_smem(nvfp4_gemv_tma, smem)) return kErrLaunch;
-  return launch_ex(nvfp4_gemv_tma, dim3(grid), dim3(kCT + 32), smem, stream, b.pdl != 0, b, c);
+  c.bpj = (b.rows + c.blk - 1) / c.blk;
+  switch (h) {
+    case 4: return launch_h<4>(b, c, smem, stream);
+    case 3: return launch_h<3>(b, c, smem, stream);
+    case 2: return launch_h<2>(b, c, smem, stream);
+    default: return launch_h<1>(b, c, smem, stream);
+  }
 }
 
 template <int W>
