@@ -349,7 +349,8 @@ def main():
     x_buf = torch.zeros(HIDDEN, device=device)
     r_buf = torch.zeros(L, N_EXPERTS, device=device)
 
-    use_graph = world == 1 and not args.no_graph
+    # the whole token (NCCL all-gathers included when world > 1) is one graph
+    use_graph = not args.no_graph
     graph = None
     if use_graph:
         s = torch.cuda.Stream(device)
