@@ -52,6 +52,9 @@ SIGNATURES: dict[str, list] = {
     "ervf_moe_down_routesum": [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i,
                                _vp, _sz, _i, _i, _vp],
     "ervf_routesum_scratch_bytes": [_i, _i],
+    "ervf_moe_decode": [_vp, _sz, _sz, _sz, _sz, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _i, _vp, _sz,
+                        _vp],
+    "ervf_decode_scratch_bytes": [_i, _i],
     "ervf_moe_down_routesum_static": [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp,
                                       _i, _i, _i, _i, _vp],
     "ervf_route_topk_batched": [_vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp],
@@ -67,7 +70,7 @@ SIGNATURES: dict[str, list] = {
     "ervf_cache_fetch": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _i, _vp],
 }
 
-SIZE_RESULT = {"ervf_routesum_scratch_bytes"}
+SIZE_RESULT = {"ervf_routesum_scratch_bytes", "ervf_decode_scratch_bytes"}
 
 _lib = None
 

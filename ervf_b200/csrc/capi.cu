@@ -209,6 +209,47 @@ int ervf_moe_down_routesum(const uint8_t* dn_codes, const uint8_t* dn_scales,
   return launch_nvfp4_batch(b, width, S(stream));
 }
 
+size_t ervf_decode_scratch_bytes(int hidden, int top_k) {
+  if (hidden <= 0 || top_k <= 0) return 0;
+  return ((size_t)top_k * hidden * 4 + (size_t)hidden * 4 + 15) / 16 * 16 + 16;
+}
+
+int ervf_moe_decode(const void* layer_table, size_t up_code_stride, size_t up_scale_stride,
+                    size_t dn_code_stride, size_t dn_scale_stride, const int32_t* ids,
+                    const float* route_w, int layers, int top_k, const float* x_in, float* xbuf,
+                    float* act, int hidden, int inter, void* scratch, size_t scratch_bytes,
+                    void* stream) {
+  if (!layer_table || !ids || !route_w || !x_in || !xbuf || !act || !scratch) return kErrNull;
+  if (layers <= 0 || top_k <= 0 || top_k > kMaxJobs) return kErrShape;
+  if (hidden <= 0 || inter <= 0 || hidden % 32 || inter % 32 || hidden > 4096 || inter > 4096)
+    return kErrShape;
+  if (scratch_bytes < ervf_decode_scratch_bytes(hidden, top_k)) return kErrArg;
+  if (!al(layer_table, 8) || !al(x_in, 16) || !al(xbuf, 16) || !al(act, 16) || !al(scratch, 16))
+    return kErrAlign;
+  if ((up_code_stride | up_scale_stride | dn_code_stride | dn_scale_stride) & 15u) return kErrAlign;
+  DecodeArgs a{};
+  a.layers = layers;
+  a.top_k = top_k;
+  a.hidden = hidden;
+  a.inter = inter;
+  a.up_cs = up_code_stride;
+  a.up_ss = up_scale_stride;
+  a.dn_cs = dn_code_stride;
+  a.dn_ss = dn_scale_stride;
+  a.lay = reinterpret_cast<const DecodeLayer*>(layer_table);
+  a.ids = ids;
+  a.route_w = route_w;
+  a.x_in = x_in;
+  a.xb = xbuf;
+  a.act = act;
+  a.contrib = reinterpret_cast<float*>(scratch);
+  a.row_count = reinterpret_cast<int*>(a.contrib + (size_t)top_k * hidden);
+  a.grid_bar = reinterpret_cast<unsigned*>(
+      reinterpret_cast<uint8_t*>(scratch) + ((size_t)top_k * hidden * 4 + (size_t)hidden * 4 + 15) / 16 * 16);
+  if (cudaMemsetAsync(a.grid_bar, 0, sizeof(unsigned), S(stream)) != cudaSuccess) return kErrLaunch;
+  return launch_moe_decode(a, S(stream));
+}
+
 size_t ervf_routesum_scratch_bytes(int hidden, int top_k) {
   if (hidden <= 0 || top_k <= 0) return 0;
   return routesum_scratch_bytes(hidden, top_k);

@@ -90,22 +90,6 @@ __device__ __forceinline__ float2 f16x2_to_f32x2(uint32_t h) {
   return r;
 }
 
-// Two E4M3 block-scale bytes (low byte first) as binary32 with the device
-// table's NaN -> +0.0 rule: hardware e4m3x2 -> f16x2 (exact), f16 -> f32
-// (exact).  The bytes 0x7F / 0xFF (NaN) are cleared to 0x00 first.
-__device__ __forceinline__ float2 e4m3x2_to_f32x2(uint32_t sv) {
-  // a byte is NaN iff its low 7 bits are all ones
-  const uint32_t nan = ((sv & 0x7F7Fu) + 0x0101u) & 0x8080u;
-  const uint32_t keep = ~((nan >> 7) * 0xFFu);  // 0x00 over NaN bytes
-  const uint16_t v = (uint16_t)(sv & keep & 0xFFFFu);
-  float2 r;
-  asm("{\n .reg .b32 h;\n .reg .b16 lo, hi;\n cvt.rn.f16x2.e4m3x2 h, %2;\n mov.b32 {lo, hi}, h;\n"
-      " cvt.f32.f16 %0, lo;\n cvt.f32.f16 %1, hi;\n}"
-      : "=f"(r.x), "=f"(r.y)
-      : "h"(v));
-  return r;
-}
-
 // The eight E2M1 codes of a 32-bit word (code i = nibble i, low first) as
 // exact binary32 values f[0..7]: hardware e2m1x2 -> f16x2, then f16 -> f32.
 __device__ __forceinline__ void e2m1x8_to_f32(uint32_t q, float (&f)[8]) {

@@ -80,6 +80,32 @@ __host__ __device__ inline bool job_active(const GemvBatch& b, int job) {
 #endif
 }
 
+// Persistent decode (nvfp4_gemv.cu): all routed-MoE layers of one token in
+// one cooperative launch.
+struct DecodeLayer {
+  const uint8_t* up_c;
+  const uint8_t* up_s;
+  const uint8_t* dn_c;
+  const uint8_t* dn_s;
+  const float* globals;  // [E][2] = (g_down, g_up)
+};
+
+struct DecodeArgs {
+  int layers, top_k, hidden, inter;
+  size_t up_cs, up_ss, dn_cs, dn_ss;  // per-expert record strides (bytes)
+  const DecodeLayer* lay;             // [layers], device
+  const int* ids;                     // [layers][top_k]
+  const float* route_w;               // [layers][top_k]
+  const float* x_in;                  // [hidden]
+  float* xb;                          // [2][hidden]: layer l writes xb[l & 1]
+  float* act;                         // [top_k][inter]
+  float* contrib;                     // [top_k][hidden]
+  int* row_count;                     // [hidden], zero before and after
+  unsigned* grid_bar;                 // zero at launch
+};
+
+int launch_moe_decode(const DecodeArgs& a, cudaStream_t stream);
+
 // width 0: the TMA-staged B200 schedule (falls back to width 32 where its
 // preconditions do not hold); 4/8/16/32: W lanes per row, lane L owning the
 // chains L + W*i.  Every schedule returns the same bits.

@@ -10,8 +10,9 @@
 //    mbarriers.  Each of 256 consumer threads owns one "chain group" g (four
 //    consecutive reference chains 4g..4g+3, i.e. the 16-byte code unit g) for
 //    a slot of rows and keeps that unit's activation in registers; second-
-//    round units (cols > 2048) are spread evenly over all threads.  Codes and
-//    scales are decoded with the sm_100a e2m1x2 / e4m3x2 converters.  Chain
+//    round units (cols > 2048) are spread evenly over all threads.  Codes are
+//    decoded with the sm_100a e2m1x2 converter, block scales through a
+//    per-job shared table of RN(e4m3 * g).  Chain
 //    values go to shared memory and are reduced by the reference tree.
 //
 //  * nvfp4_gemv_sched<W> -- the reference's ERVF widths 4/8/16/32 as
@@ -169,7 +170,8 @@ __global__ void __launch_bounds__(256) nvfp4_gemv_sched(GemvBatch p, int tiles_p
 // segment's activation (32 values) is read into registers from a swizzled
 // shared copy of x (kept across items when both segments use one unit);
 // codes and block scales are decoded with the sm_100a
-// e2m1x2 / e4m3x2 converters, w = RN(e2m1 * s) (FMUL) and acc = fmaf(w, x,
+// e2m1x2 converter and block scales read from the job's shared table of
+// RN(e4m3 * g) (the reference's LUT product), w = RN(e2m1 * s) (FMUL) and acc = fmaf(w, x,
 // acc) (FFMA) in the reference's order.  Chain values go to the item's chain
 // buffer; after a consumer barrier thread (row tr, segment tw) reduces chains
 // 32tw..32tw+31 of its row with the reference's shuffle tree (offsets 16..1)
@@ -192,6 +194,7 @@ struct TmaCfg {
   int scale_off;    // scale rows inside a stage
   int part_off;     // chain buffer [kRt][kRowPitch] floats
   int xs_off;       // activation [n_u][8] float4, swizzled
+  int lut_off;      // block-scale table of the current job: 256 floats RN(e4m3 * g)
   int stage_base;
   int n_u;          // code units per row (cols / 32)
   int n2;           // chain groups with a second unit (n_u - 64, or 0)
@@ -221,22 +224,6 @@ __device__ __forceinline__ void unit_fma(const uint4 q, const float s0, const fl
   }
 }
 
-// Block scales s_2u, s_2u+1 of a unit: RN(e4m3 * g) from two scale bytes.
-__device__ __forceinline__ float2 unit_scales(uint32_t sv, float g) {
-  const float2 e = e4m3x2_to_f32x2(sv);
-  return make_float2(e.x * g, e.y * g);
-}
-
-// Row `row` of a stage, unit u: continue acc[0..3].
-__device__ __forceinline__ void stage_unit(const uint8_t* stage, int scale_off, int cb, int sb,
-                                           int row, int u, float g, const float (&x)[32],
-                                           float* acc) {
-  const uint4 qv = *reinterpret_cast<const uint4*>(stage + row * cb + 16 * u);
-  const uint32_t sv = *reinterpret_cast<const uint16_t*>(stage + scale_off + row * sb + 2 * u);
-  const float2 s = unit_scales(sv, g);
-  unit_fma(qv, s.x, s.y, x, acc);
-}
-
 // Activation of unit u from the swizzled shared copy (float4 i at u*8 + (i ^ (u & 7))).
 __device__ __forceinline__ void load_unit_x(const float4* xs, int u, float (&x)[32]) {
 #pragma unroll
@@ -249,45 +236,65 @@ __device__ __forceinline__ void load_unit_x(const float4* xs, int u, float (&x)[
 // The two segments of one consumer thread for one item (see the schedule
 // above).  FULL: every row of the item exists, so the H rows of a segment run
 // unconditionally and interleave.
+// H rows of one segment, unit fixed: code / scale byte offsets (into the
+// stage, relative to smem) advance by rstep / sstep per row; block scales come
+// from the job's table of RN(e4m3 * g).
 template <int H, bool FULL>
-__device__ __forceinline__ void segments(const uint8_t* stage, int scale_off, int cb, int sb,
-                                         int team, int T, int par1, int par2, bool cont, int u1,
-                                         int u2, int grp, int nrows, float gs, const float4* xs,
-                                         float (&x)[32], bool& x_stale, float* part) {
+__device__ __forceinline__ void seg_rows(const uint8_t* smem, uint32_t coff, uint32_t soff,
+                                         uint32_t rstep, uint32_t sstep, const float* lut,
+                                         const float (&x)[32], float (&acc)[H][4], int row0,
+                                         int rowstep, int nrows) {
+#pragma unroll
+  for (int h = 0; h < H; ++h) {
+    if (FULL || row0 + h * rowstep < nrows) {
+      const uint4 q = *reinterpret_cast<const uint4*>(smem + coff + h * rstep);
+      const uint32_t s2 = *reinterpret_cast<const uint16_t*>(smem + soff + h * sstep);
+      unit_fma(q, lut[s2 & 0xFFu], lut[s2 >> 8], x, acc[h]);
+    }
+  }
+}
+
+template <int H, bool FULL>
+__device__ __forceinline__ void seg_store(float* part, uint32_t poff, uint32_t pstep,
+                                          const float (&acc)[H][4], int row0, int rowstep,
+                                          int nrows) {
+#pragma unroll
+  for (int h = 0; h < H; ++h)
+    if (FULL || row0 + h * rowstep < nrows)
+      *reinterpret_cast<float4*>(part + poff + h * pstep) =
+          make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+}
+
+// The two segments of one consumer thread for one item (see the schedule
+// above).  FULL: every row of the item exists, so the H rows of a segment run
+// unconditionally and interleave.  stage_off: the stage's byte offset in smem.
+template <int H, bool FULL>
+__device__ __forceinline__ void segments(const uint8_t* smem, uint32_t stage_off, int scale_off,
+                                         int cb, int sb, int team, int T, int par1, int par2,
+                                         bool cont, int u1, int u2, int grp, int nrows,
+                                         const float* lut, const float4* xs, float (&x)[32],
+                                         bool& x_stale, float* part) {
   float acc[H][4];
 #pragma unroll
   for (int h = 0; h < H; ++h) acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.0f;
+  const int rowstep = 2 * T;
+  const uint32_t rstep = (uint32_t)(rowstep * cb), sstep = (uint32_t)(rowstep * sb);
+  const uint32_t pstep = (uint32_t)(rowstep * kRowPitch);
+  const int row1 = team + T * par1, row2 = team + T * par2;
   if (cont || x_stale) load_unit_x(xs, u1, x);
   x_stale = false;
-#pragma unroll
-  for (int h = 0; h < H; ++h) {
-    const int row = team + T * (2 * h + par1);
-    if (FULL || row < nrows) stage_unit(stage, scale_off, cb, sb, row, u1, gs, x, acc[h]);
-  }
+  seg_rows<H, FULL>(smem, stage_off + row1 * cb + 16 * u1, stage_off + scale_off + row1 * sb + 2 * u1,
+                    rstep, sstep, lut, x, acc, row1, rowstep, nrows);
   if (!cont) {
+    seg_store<H, FULL>(part, row1 * kRowPitch + part_index(4 * grp), pstep, acc, row1, rowstep, nrows);
 #pragma unroll
-    for (int h = 0; h < H; ++h) {
-      const int row = team + T * (2 * h + par1);
-      if (FULL || row < nrows)
-        *reinterpret_cast<float4*>(part + row * kRowPitch + part_index(4 * grp)) =
-            make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-      acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.0f;
-    }
+    for (int h = 0; h < H; ++h) acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.0f;
   } else {
     load_unit_x(xs, u2, x);
   }
-#pragma unroll
-  for (int h = 0; h < H; ++h) {
-    const int row = team + T * (2 * h + par2);
-    if (FULL || row < nrows) stage_unit(stage, scale_off, cb, sb, row, u2, gs, x, acc[h]);
-  }
-#pragma unroll
-  for (int h = 0; h < H; ++h) {
-    const int row = team + T * (2 * h + par2);
-    if (FULL || row < nrows)
-      *reinterpret_cast<float4*>(part + row * kRowPitch + part_index(4 * grp)) =
-          make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-  }
+  seg_rows<H, FULL>(smem, stage_off + row2 * cb + 16 * u2, stage_off + scale_off + row2 * sb + 2 * u2,
+                    rstep, sstep, lut, x, acc, row2, rowstep, nrows);
+  seg_store<H, FULL>(part, row2 * kRowPitch + part_index(4 * grp), pstep, acc, row2, rowstep, nrows);
 }
 
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -335,6 +342,7 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
   int* nact = jlist + kMaxJobs;
   float* part = reinterpret_cast<float*>(smem + c.part_off);
   float4* xs = reinterpret_cast<float4*>(smem + c.xs_off);
+  float* lut = reinterpret_cast<float*>(smem + c.lut_off);  // [256] of the current job
   uint8_t* stages = smem + c.stage_base;
 
   if (tid == 0) {
@@ -413,6 +421,7 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
   const int par2 = cont ? par1 : 1;
   const int tr = tid >> 3, tw = tid & 7;
   const float* cur_x = nullptr;
+  int cur_job = -1;
   // segment activation; a thread whose two segments share one unit keeps it
   // in registers until the job's activation changes
   float x[32];
@@ -425,27 +434,32 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
     const uint32_t ph = (it / S) & 1;
     ++it;
     const GemvJob& J = p.job[job];
-    if (J.x != cur_x) {  // the previous item ended with a consumer barrier
-      const float4* src = reinterpret_cast<const float4*>(J.x);
-      for (int f = tid; f < nu * 8; f += kCT) {
-        const int t = f >> 3, i = f & 7;
-        xs[t * 8 + (i ^ (t & 7))] = __ldg(src + f);
+    if (J.x != cur_x || job != cur_job) {  // the previous item ended with a consumer barrier
+      if (J.x != cur_x) {
+        const float4* src = reinterpret_cast<const float4*>(J.x);
+        for (int f = tid; f < nu * 8; f += kCT) {
+          const int t = f >> 3, i = f & 7;
+          xs[t * 8 + (i ^ (t & 7))] = __ldg(src + f);
+        }
+        cur_x = J.x;
+        x_stale = true;
+      }
+      if (job != cur_job) {
+        lut[tid] = e4m3_lut_value((uint32_t)tid) * jg[job];
+        cur_job = job;
       }
       named_bar_sync(kBarC, kCT);
-      cur_x = J.x;
-      x_stale = true;
     }
-    const float gs = jg[job];
     const bool to = !mbar_wait(&full[st], ph);
-    const uint8_t* stage = stages + (size_t)st * c.stage_bytes;
+    const uint32_t stage_off = (uint32_t)(c.stage_base + st * c.stage_bytes);
 
     if (active) {
       if (nrows == krt) {
-        segments<H, true>(stage, c.scale_off, cb, sb, team, T, par1, par2, cont, u1, u2, grp, nrows,
-                          gs, xs, x, x_stale, part);
+        segments<H, true>(smem, stage_off, c.scale_off, cb, sb, team, T, par1, par2, cont, u1, u2, grp,
+                          nrows, lut, xs, x, x_stale, part);
       } else {
-        segments<H, false>(stage, c.scale_off, cb, sb, team, T, par1, par2, cont, u1, u2, grp, nrows,
-                           gs, xs, x, x_stale, part);
+        segments<H, false>(smem, stage_off, c.scale_off, cb, sb, team, T, par1, par2, cont, u1, u2,
+                           grp, nrows, lut, xs, x, x_stale, part);
       }
     }
     // every read of the stage is done; a timeout anywhere stops all consumers
@@ -474,6 +488,300 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
           p.row_count[r] = 0;
         }
       }
+    }
+  }
+}
+
+// Job-aligned split: the grid is cut into njobs contiguous CTA groups, one
+// per job, and each group splits its job's row blocks evenly, so that every
+// CTA works on a single job (one activation) per launch or phase.
+__device__ __forceinline__ void cta_blocks_per_job(int njobs, int bpj, ItemSeq& q) {
+  const int G = gridDim.x, b = blockIdx.x;
+  if (G < njobs) {
+    cta_blocks(njobs * bpj, q);
+    return;
+  }
+  const int j = (int)(((long long)b * njobs) / G);
+  const int c0 = (int)(((long long)j * G + njobs - 1) / njobs);
+  const int c1 = (int)(((long long)(j + 1) * G + njobs - 1) / njobs);
+  const int n = c1 - c0, k = b - c0;
+  const int per = bpj / n, rem = bpj % n;
+  q.blk = j * bpj + k * per + min(k, rem);
+  q.blk_end = q.blk + per + (k < rem ? 1 : 0);
+}
+
+// ======================================================================
+// Persistent decode: every routed-MoE layer of one token in one launch
+// ======================================================================
+//
+// Phases p = 0 .. 2L-1 alternate up (layer l = p/2: act[s] = relu2(up_s(x_l)))
+// and down (x_{l+1} = x_l + sum_s w_s down_s(act[s]) in route order), each
+// with the item schedule of nvfp4_gemv_tma, separated by grid barriers (a
+// cooperative launch keeps every CTA resident).  The producer warp never
+// waits at a grid barrier: expert weights do not depend on activations and
+// the routing of every layer is known before the launch, so the copy ring
+// keeps streaming the next phases' experts while the consumers wait.
+// Activations written by other CTAs are read through L2 (ld.global.cg).
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid barrier of the consumer threads (all CTAs): returns true when this
+// CTA gave up waiting (error word set) or was already dead.
+__device__ __forceinline__ bool grid_barrier(unsigned* bar, unsigned target, bool dead) {
+  named_bar_sync(kBarC, kCT);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(bar, 1u);
+    if (!dead) {
+      const long long t0 = clock64();
+      while (ld_acquire_gpu(bar) < target) {
+        if (clock64() - t0 > 4000000000LL) {
+          atomicExch(&g_device_error, kErrTimeout);
+          dead = true;
+          break;
+        }
+        nanosleep_ns(64);
+      }
+    }
+    __threadfence();
+  }
+  return named_bar_or(kBarC, kCT, dead);
+}
+
+// Job s of phase p: code / scale rows and global scale.
+__device__ __forceinline__ void decode_job(const DecodeArgs& a, int p, int s, const uint8_t*& cc,
+                                           const uint8_t*& ss, float& g) {
+  const int l = p >> 1;
+  const DecodeLayer& L = a.lay[l];
+  const size_t slot = (size_t)__ldg(&a.ids[l * a.top_k + s]);
+  if (p & 1) {
+    cc = L.dn_c + slot * a.dn_cs;
+    ss = L.dn_s + slot * a.dn_ss;
+    g = __ldg(&L.globals[slot * 2 + 0]);
+  } else {
+    cc = L.up_c + slot * a.up_cs;
+    ss = L.up_s + slot * a.up_ss;
+    g = __ldg(&L.globals[slot * 2 + 1]);
+  }
+}
+
+template <int H>
+__device__ __forceinline__ void decode_segments(const TmaCfg& c, int tid, bool full, const uint8_t* smem,
+                                                uint32_t stage_off, int cb, int sb, int nrows,
+                                                const float* lut, const float4* xs, float (&x)[32],
+                                                bool& x_stale, float* part) {
+  const int nu = c.n_u, n2 = c.n2, T = c.teams;
+  const int team = tid / nu, m = tid - team * nu;
+  if (team >= T) return;
+  const bool cont = m < 2 * n2;
+  const int grp = m < n2 ? m : m - n2;
+  const int u1 = grp, u2 = cont ? grp + 64 : grp;
+  const int par1 = (m >= n2 && m < 2 * n2) ? 1 : 0;
+  const int par2 = cont ? par1 : 1;
+  if (full) {
+    segments<H, true>(smem, stage_off, c.scale_off, cb, sb, team, T, par1, par2, cont, u1, u2, grp,
+                      nrows, lut, xs, x, x_stale, part);
+  } else {
+    segments<H, false>(smem, stage_off, c.scale_off, cb, sb, team, T, par1, par2, cont, u1, u2, grp,
+                       nrows, lut, xs, x, x_stale, part);
+  }
+}
+
+// x_l = x_{l-1} + acc with acc = fmaf(contrib[s][r], w_s, acc) over the route
+// slots of layer l-1 in order from 0.0 (the routed sum with residual, as
+// ervf_moe_down_routesum computes it), for every row r, by the CTA's
+// consumer threads.  Writes the swizzled shared copy (xs, if given) and the
+// global vector (out, if given).  Reads through L2: other CTAs wrote contrib.
+__device__ __forceinline__ void rebuild_x(const DecodeArgs& a, int l, float4* xs, float* out) {
+  const float* xp = l == 1 ? a.x_in : a.xb + (size_t)((l - 2) & 1) * a.hidden;
+  const float* w = a.route_w + (size_t)(l - 1) * a.top_k;
+  const int n4 = a.hidden >> 2;
+  for (int f = threadIdx.x; f < n4; f += kCT) {
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int s2 = 0; s2 < a.top_k; ++s2) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(a.contrib + (size_t)s2 * a.hidden) + f);
+      const float ws = __ldg(&w[s2]);
+      acc.x = fmaf(v.x, ws, acc.x);
+      acc.y = fmaf(v.y, ws, acc.y);
+      acc.z = fmaf(v.z, ws, acc.z);
+      acc.w = fmaf(v.w, ws, acc.w);
+    }
+    const float4 b = __ldcg(reinterpret_cast<const float4*>(xp) + f);
+    const float4 xv = make_float4(b.x + acc.x, b.y + acc.y, b.z + acc.z, b.w + acc.w);
+    if (xs) {
+      const int t = f >> 3, i = f & 7;
+      xs[t * 8 + (i ^ (t & 7))] = xv;
+    }
+    if (out) reinterpret_cast<float4*>(out)[f] = xv;
+  }
+}
+
+template <int HU, int HD>
+__global__ void __launch_bounds__(kCT + 32, 2) nvfp4_moe_decode(DecodeArgs a, TmaCfg cu, TmaCfg cd) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x;
+  const int S = cu.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [S], S <= 8
+  uint64_t* empty = full + 8;                         // [S]
+  int* jlist = reinterpret_cast<int*>(smem + 448);
+  float* part = reinterpret_cast<float*>(smem + cu.part_off);
+  float4* xs = reinterpret_cast<float4*>(smem + cu.xs_off);
+  float* lut = reinterpret_cast<float*>(smem + cu.lut_off);  // [256] of the current job
+  uint8_t* stages = smem + cu.stage_base;
+  const int P = 2 * a.layers;
+
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    fence_mbar_init();
+  }
+  if (tid < kMaxJobs) jlist[tid] = tid;  // every route slot is a job of every phase
+  __syncthreads();
+
+  // ------------------------------------------------------------ producer
+  if (tid >= kCT) {
+    if (tid == kCT) {
+      int it = 0;
+      bool ok = true;
+      for (int p = 0; p < P && ok; ++p) {
+        const TmaCfg& c = (p & 1) ? cd : cu;
+        const int rows = (p & 1) ? a.hidden : a.inter, cols = (p & 1) ? a.inter : a.hidden;
+        const int cb = cols >> 1, sb = cols >> 4;
+        ItemSeq q;
+        if (p & 1) {
+          cta_blocks_per_job(a.top_k, c.bpj, q);
+        } else {
+          cta_blocks(a.top_k * c.bpj, q);
+        }
+        int job, r0, nrows;
+        while (next_item(q, c, jlist, rows, job, r0, nrows)) {
+          const int st = it % S;
+          if (!mbar_wait(&empty[st], ((it / S) & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          ++it;
+          const uint8_t *cc, *ss;
+          float g;
+          decode_job(a, p, job, cc, ss, g);
+          uint8_t* dst = stages + (size_t)st * cu.stage_bytes;
+          const uint32_t code_bytes = (uint32_t)(nrows * cb);
+          const uint32_t scale_bytes = (uint32_t)(nrows * sb);
+          const uint32_t s16 = scale_bytes & ~15u;
+          const uint8_t* ssrc = ss + (size_t)r0 * sb;
+          for (uint32_t i = s16; i < scale_bytes; ++i) dst[c.scale_off + i] = ssrc[i];
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          mbar_arrive_expect_tx(&full[st], code_bytes + s16);
+          bulk_g2s(dst, cc + (size_t)r0 * cb, code_bytes, &full[st]);
+          if (s16) bulk_g2s(dst + c.scale_off, ssrc, s16, &full[st]);
+        }
+      }
+      // Leave no bulk copy in flight: wait (bounded) for the last stages.
+      for (int k = (it > S ? it - S : 0); k < it; ++k) mbar_wait(&full[k % S], (k / S) & 1);
+    }
+    return;
+  }
+
+  // ----------------------------------------------------------- consumers
+  const int krt_max = (cu.kb * cu.blk > cd.kb * cd.blk) ? cu.kb * cu.blk : cd.kb * cd.blk;
+  for (int i = tid; i < krt_max * kRowPitch; i += kCT) part[i] = 0.0f;
+  const int tr = tid >> 3, tw = tid & 7;
+  float x[32];
+  bool dead = false;
+  int it = 0;
+  named_bar_sync(kBarC, kCT);
+
+  for (int p = 0; p < P; ++p) {
+    const bool down = (p & 1) != 0;
+    const int l = p >> 1;
+    const TmaCfg& c = down ? cd : cu;
+    const int rows = down ? a.hidden : a.inter, cols = down ? a.inter : a.hidden;
+    const int cb = cols >> 1, sb = cols >> 4;
+    const int krt = down ? HD * 2 * cd.teams : HU * 2 * cu.teams;
+    const float* x_l = l == 0 ? a.x_in : a.xb + (size_t)((l - 1) & 1) * a.hidden;
+    // x_l is written (by CTA 0) while the up phase of layer l refills it
+    float* x_next_prev = a.xb + (size_t)((l - 1) & 1) * a.hidden;
+    // chain groups beyond this phase's units must read as zero in the tree
+    for (int i = tid; i < krt_max * kRowPitch; i += kCT) part[i] = 0.0f;
+    named_bar_sync(kBarC, kCT);
+    const float* cur_x = nullptr;
+    int cur_job = -1;
+    bool x_stale = true;
+    ItemSeq q;
+    if (down) {
+      cta_blocks_per_job(a.top_k, c.bpj, q);
+    } else {
+      cta_blocks(a.top_k * c.bpj, q);
+    }
+    int job, r0, nrows;
+    while (next_item(q, c, jlist, rows, job, r0, nrows)) {
+      const int st = it % S;
+      const uint32_t ph = (it / S) & 1;
+      ++it;
+      const float* xj = down ? a.act + (size_t)job * a.inter : x_l;
+      if (xj != cur_x || job != cur_job) {  // the previous item ended with a consumer barrier
+        if (xj != cur_x) {
+          if (!down && l > 0) {
+            // x_l = x_{l-1} + route-order sum of the previous down phase
+            rebuild_x(a, l, xs, blockIdx.x == 0 ? x_next_prev : nullptr);
+          } else {
+            const float4* src = reinterpret_cast<const float4*>(xj);
+            for (int f = tid; f < c.n_u * 8; f += kCT) {
+              const int t = f >> 3, i = f & 7;
+              xs[t * 8 + (i ^ (t & 7))] = __ldcg(src + f);
+            }
+          }
+          cur_x = xj;
+          x_stale = true;
+        }
+        if (job != cur_job) {
+          const uint8_t *cc, *ss;
+          float gs;
+          decode_job(a, p, job, cc, ss, gs);
+          lut[tid] = e4m3_lut_value((uint32_t)tid) * gs;
+          cur_job = job;
+        }
+        named_bar_sync(kBarC, kCT);
+      }
+      bool to = false;
+      if (!dead) to = !mbar_wait(&full[st], ph);
+      const uint32_t stage_off = (uint32_t)(cu.stage_base + st * cu.stage_bytes);
+      if (!dead && !to) {
+        if (down) {
+          decode_segments<HD>(c, tid, nrows == krt, smem, stage_off, cb, sb, nrows, lut, xs, x, x_stale,
+                              part);
+        } else {
+          decode_segments<HU>(c, tid, nrows == krt, smem, stage_off, cb, sb, nrows, lut, xs, x, x_stale,
+                              part);
+        }
+      }
+      dead = named_bar_or(kBarC, kCT, dead || to);
+      if (tid == 0 && !dead) mbar_arrive(&empty[st]);
+      float y = 0.0f;
+      if (!dead && tr < nrows) y = group_tree(part + tr * kRowPitch + tw * kGroupPitch);
+      y = combine8(y);
+      named_bar_sync(kBarC, kCT);  // the chain buffer is rewritten by the next item
+      if (!dead && tw == 0 && tr < nrows) {
+        const int r = r0 + tr;
+        if (!down) {
+          a.act[(size_t)job * a.inter + r] = epilogue(y, 1, 1.0f);
+        } else {
+          a.contrib[(size_t)job * a.hidden + r] = y;  // summed after the grid barrier
+        }
+      }
+    }
+    if (p + 1 < P) {
+      dead = grid_barrier(a.grid_bar, (unsigned)((p + 1) * gridDim.x), dead);
+    } else {
+      // x_L: every CTA arrives, CTA 0 waits and sums the last down phase
+      dead = grid_barrier(a.grid_bar, (unsigned)((p + 1) * gridDim.x), dead || blockIdx.x != 0);
+      if (blockIdx.x == 0 && !dead) rebuild_x(a, a.layers, nullptr, a.xb + (size_t)((a.layers - 1) & 1) * a.hidden);
     }
   }
 }
@@ -509,6 +817,15 @@ int set_smem(K kernel, int bytes) {
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
     return kErrLaunch;
   return kOk;
+}
+
+// Smallest row block whose bulk copies start 16-byte aligned: code rows need
+// r0 * cols / 2 % 16 == 0 and scale rows r0 * cols / 16 % 16 == 0, i.e.
+// r0 * cols % 256 == 0 (cols % 32 == 0): blk = 256 / gcd(cols, 256).
+int row_block(int cols) {
+  int g = 256;
+  while (cols % g != 0) g >>= 1;
+  return 256 / g;
 }
 
 bool tma_ok(const GemvBatch& b) {
@@ -556,8 +873,7 @@ int launch_tma(const GemvBatch& b, cudaStream_t stream) {
   c.n2 = c.n_u > 64 ? c.n_u - 64 : 0;
   c.teams = kCT / c.n_u;
   if (c.teams > 16) c.teams = 16;
-  // Scale rows of a block start 16-byte aligned: blk * cols / 16 % 16 == 0.
-  c.blk = (b.cols % 64 == 0) ? 4 : 8;
+  c.blk = row_block(b.cols);
   const int cb = b.cols / 2, sb = b.cols / 16;
   const int budget = (di.smem_sm - kCtasPerSm * 1024) / kCtasPerSm;
   // Largest H (rows per segment) whose chain buffer, activation and two
@@ -568,12 +884,14 @@ int launch_tma(const GemvBatch& b, cudaStream_t stream) {
     if (krt > 32 || krt % c.blk != 0) continue;
     const int part_off = 576;  // after barriers, job tables and the active-job list
     const int xs_off = align_up(part_off + krt * kRowPitch * 4, 16);
-    const int base = align_up(xs_off + c.n_u * 128, 128);
+    const int lut_off = xs_off + c.n_u * 128;
+    const int base = align_up(lut_off + 1024, 128);
     const int stage = align_up(krt * cb + align_up(krt * sb, 16), 128);
     if (base + 2 * stage <= budget) {
       h = cand;
       c.part_off = part_off;
       c.xs_off = xs_off;
+      c.lut_off = lut_off;
       c.stage_base = base;
       c.scale_off = krt * cb;
       c.stage_bytes = stage;
@@ -592,6 +910,44 @@ int launch_tma(const GemvBatch& b, cudaStream_t stream) {
     case 2: return launch_h<2>(b, c, smem, stream);
     default: return launch_h<1>(b, c, smem, stream);
   }
+}
+
+// Persistent decode launch: item geometry of the up phase (cols = hidden)
+// and the down phase (cols = inter) with a shared stage ring and chain buffer.
+bool phase_cfg(int rows, int cols, int H, TmaCfg& c) {
+  c.n_u = cols / 32;
+  c.n2 = c.n_u > 64 ? c.n_u - 64 : 0;
+  c.teams = kCT / c.n_u;
+  if (c.teams > 16) c.teams = 16;
+  c.blk = row_block(cols);
+  const int krt = c.teams * 2 * H;
+  if (krt > 32 || krt % c.blk != 0) return false;
+  c.kb = krt / c.blk;
+  c.bpj = (rows + c.blk - 1) / c.blk;
+  c.scale_off = krt * (cols / 2);
+  return true;
+}
+
+template <int HU, int HD>
+int launch_decode_h(const DecodeArgs& a, TmaCfg cu, TmaCfg cd, int smem, cudaStream_t stream) {
+  auto kern = nvfp4_moe_decode<HU, HD>;
+  if (set_smem(kern, smem)) return kErrLaunch;
+  int nb = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kCT + 32, smem) != cudaSuccess)
+    return kErrLaunch;
+  if (nb < 1) return kErrShape;
+  if (nb > kCtasPerSm) nb = kCtasPerSm;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(dev_info().sms * nb);
+  cfg.blockDim = dim3(kCT + 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // grid barriers need every CTA resident
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a, cu, cd) == cudaSuccess ? kOk : kErrLaunch;
 }
 
 template <int W>
@@ -632,6 +988,47 @@ int launch_nvfp4_batch(const GemvBatch& b, int width, cudaStream_t stream) {
     case 32: return launch_sched_w<32>(b, stream);
     default: return kErrArg;
   }
+}
+
+int launch_moe_decode(const DecodeArgs& a, cudaStream_t stream) {
+  const DevInfo& di = dev_info();
+  const int budget = (di.smem_sm - kCtasPerSm * 1024) / kCtasPerSm;
+  static const int combos[][2] = {{4, 4}, {4, 3}, {4, 2}, {4, 1}, {3, 3}, {2, 2}, {1, 1}};
+  for (const auto& hc : combos) {
+    TmaCfg cu{}, cd{};
+    if (!phase_cfg(a.inter, a.hidden, hc[0], cu) || !phase_cfg(a.hidden, a.inter, hc[1], cd)) continue;
+    const int krt_u = cu.kb * cu.blk, krt_d = cd.kb * cd.blk;
+    const int part_rows = krt_u > krt_d ? krt_u : krt_d;
+    const int stage_u = align_up(krt_u * (a.hidden / 2) + align_up(krt_u * (a.hidden / 16), 16), 128);
+    const int stage_d = align_up(krt_d * (a.inter / 2) + align_up(krt_d * (a.inter / 16), 16), 128);
+    const int stage = stage_u > stage_d ? stage_u : stage_d;
+    const int nu_max = cu.n_u > cd.n_u ? cu.n_u : cd.n_u;
+    const int part_off = 576;
+    const int xs_off = align_up(part_off + part_rows * kRowPitch * 4, 16);
+    const int lut_off = xs_off + nu_max * 128;
+    const int base = align_up(lut_off + 1024, 128);
+    if (base + 2 * stage > budget) continue;
+    int stages = (budget - base) / stage;
+    if (stages > 4) stages = 4;
+    for (TmaCfg* c : {&cu, &cd}) {
+      c->stages = stages;
+      c->stage_bytes = stage;
+      c->part_off = part_off;
+      c->xs_off = xs_off;
+      c->lut_off = lut_off;
+      c->stage_base = base;
+    }
+    const int smem = base + stages * stage;
+    const int hu = hc[0], hd = hc[1];
+    if (hu == 4 && hd == 4) return launch_decode_h<4, 4>(a, cu, cd, smem, stream);
+    if (hu == 4 && hd == 3) return launch_decode_h<4, 3>(a, cu, cd, smem, stream);
+    if (hu == 4 && hd == 2) return launch_decode_h<4, 2>(a, cu, cd, smem, stream);
+    if (hu == 4 && hd == 1) return launch_decode_h<4, 1>(a, cu, cd, smem, stream);
+    if (hu == 3) return launch_decode_h<3, 3>(a, cu, cd, smem, stream);
+    if (hu == 2) return launch_decode_h<2, 2>(a, cu, cd, smem, stream);
+    return launch_decode_h<1, 1>(a, cu, cd, smem, stream);
+  }
+  return kErrShape;
 }
 
 }  // namespace ervf

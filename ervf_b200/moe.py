@@ -124,12 +124,26 @@ class MoEDecoder:
         self.w = torch.zeros(L, k, dtype=torch.float32, device=d)
         self.act = torch.zeros(k * bank.inter, dtype=torch.float32, device=d)
         self.gate_b = torch.zeros(bank.n_experts, dtype=torch.float32, device=d)
-        self.xs = [torch.zeros(bank.hidden, dtype=torch.float32, device=d) for _ in range(2)]
+        # x after layer l lives in xbuf[l & 1]
+        self.xbuf = torch.zeros(2, bank.hidden, dtype=torch.float32, device=d)
+        self.xs = [self.xbuf[0], self.xbuf[1]]
         if ep_ranks > 1:
             self.contrib = torch.zeros(k * bank.hidden, dtype=torch.float32, device=d)
             self.gathered = torch.zeros(ep_ranks * k * bank.hidden, dtype=torch.float32, device=d)
         self.graph = None
         self.pdl = True
+        # persistent=True: one cooperative launch for all layers of the token
+        # (single GPU, bit-identical).  Off by default: on B200 the chain of
+        # PDL-overlapped per-layer launches is faster at batch 1 (0.62 vs
+        # 0.68 ms per 24-layer token), the grid barriers and the per-CTA
+        # rebuild of x costing more than the launch gaps they remove.
+        self.persistent = False
+        self.table = torch.tensor(
+            [[ptr(bank.up_codes[l]), ptr(bank.up_scales[l]), ptr(bank.dn_codes[l]),
+              ptr(bank.dn_scales[l]), ptr(bank.globals[l])] for l in range(L)],
+            dtype=torch.int64, device=d)
+        nb = _lib.load().ervf_decode_scratch_bytes(bank.hidden, k)
+        self.scratch = torch.zeros(nb, dtype=torch.uint8, device=d)
 
     def _s(self) -> int:
         return int(torch.cuda.current_stream(self.bank.device).cuda_stream)
@@ -175,6 +189,13 @@ class MoEDecoder:
         router logits of every layer.  Returns the buffer holding x after
         the last layer."""
         self.route(rlogs)
+        b = self.bank
+        if self.persistent and self.ep_ranks == 1:
+            _lib.call("ervf_moe_decode", ptr(self.table), int(b.up_code_bytes), int(b.up_scale_bytes),
+                      int(b.dn_code_bytes), int(b.dn_scale_bytes), ptr(self.ids), ptr(self.w),
+                      b.n_layers, self.top_k, ptr(x_in), ptr(self.xbuf), ptr(self.act), b.hidden,
+                      b.inter, ptr(self.scratch), self.scratch.numel(), self._s())
+            return self.xs[(b.n_layers - 1) & 1]
         cur = x_in
         for l in range(self.bank.n_layers):
             nxt = self.xs[l & 1]

@@ -125,6 +125,32 @@ ERVF_API int ervf_moe_down_routesum(const uint8_t* dn_codes, const uint8_t* dn_s
 /* Bytes of scratch ervf_moe_down_routesum uses for (hidden, top_k). */
 ERVF_API size_t ervf_routesum_scratch_bytes(int hidden, int top_k);
 
+/* All routed-MoE layers of one decode token in one cooperative launch: for
+ * l = 0..layers-1, act[s] = relu(up_{e}(x_l))^2 for the route slots s with
+ * experts e = ids[l*top_k + s], then x_{l+1} = x_l + acc with acc =
+ * fmaf(down_e(act[s]), route_w[l*top_k + s], acc) over s in route order from
+ * 0.0 -- bit-identical to the per-layer ervf_moe_up_grouped +
+ * ervf_moe_down_routesum chain (fused_nvfp4.py:970-984, route order
+ * runtime.py:588-596; the reference runs one launch per expert GEMV).
+ * layer_table: device array [layers][5] of 64-bit addresses (up codes, up
+ * scales, down codes, down scales, globals f32[E][2] = (g_down, g_up)) of each
+ * layer's expert bank, records `*_stride` bytes apart (16-byte multiples).
+ * x_in [hidden]; xbuf [2][hidden]: layer l writes xbuf[(l & 1) * hidden], so the
+ * result is xbuf[((layers - 1) & 1) * hidden]; act [top_k][inter]; scratch:
+ * ervf_decode_scratch_bytes(hidden, top_k) bytes, zero before its first use
+ * (each call leaves it ready; calls that share it must not overlap).  hidden,
+ * inter: multiples of 32, <= 4096; top_k <= 16.  One cudaMemsetAsync precedes
+ * the launch.  No counterpart in the reference. */
+ERVF_API int ervf_moe_decode(const void* layer_table, size_t up_code_stride,
+                             size_t up_scale_stride, size_t dn_code_stride,
+                             size_t dn_scale_stride, const int32_t* ids, const float* route_w,
+                             int layers, int top_k, const float* x_in, float* xbuf, float* act,
+                             int hidden, int inter, void* scratch, size_t scratch_bytes,
+                             void* stream);
+
+/* Bytes of scratch ervf_moe_decode uses for (hidden, top_k). */
+ERVF_API size_t ervf_decode_scratch_bytes(int hidden, int top_k);
+
 /* ervf_moe_down_routesum without a scratch argument.  No counterpart in the
  * reference.  The scratch is a fixed device array inside the library, so the
  * call allocates nothing: hidden <= 8192 and top_k <= 8, else

@@ -95,8 +95,9 @@ def test_grouped_up_and_routesum_match_unfused(fused, oracle, bank, cuda, width)
 
 
 def test_decoder_step_pdl_chain_matches_oracle(fused, oracle, bank, cuda):
-    """Three layers of the decode step (batched routing, PDL-chained grouped
-    launches, CUDA graph) equal the oracle's route-order recurrence."""
+    """Three layers of the decode step -- batched routing, then either the
+    PDL-chained grouped launches or the one persistent launch, eager and in a
+    CUDA graph -- equal the oracle's route-order recurrence."""
     from ervf_b200.moe import ExpertBank, MoEDecoder
 
     L, E, k = 3, 8, 6
@@ -109,7 +110,9 @@ def test_decoder_step_pdl_chain_matches_oracle(fused, oracle, bank, cuda):
     rl = r.standard_normal((L, E)).astype(np.float32)
     x = x_regime(HIDDEN, "bf16", seed=21)
     xd, rd = _t(x, cuda), _t(rl, cuda)
-    for use_graph in (False, True):
+    for use_graph, persistent in ((False, False), (True, False), (False, True), (True, True)):
+        dec.persistent = persistent
+        dec.xbuf.fill_(float("nan"))
         if use_graph:
             g = torch.cuda.CUDAGraph()
             s = torch.cuda.Stream()
@@ -129,7 +132,7 @@ def test_decoder_step_pdl_chain_matches_oracle(fused, oracle, bank, cuda):
             experts = {e: (*bank["ups"][(e + l) % E], *bank["dns"][(e + 2 * l) % E]) for e in range(E)}
             want = (want + oracle.moe_block(want, experts, ids, w, HIDDEN, INTER)).astype(np.float32)
             assert np.array_equal(dec.ids[l].cpu().numpy(), ids)
-        assert bits_equal(y.cpu().numpy(), want), use_graph
+        assert bits_equal(y.cpu().numpy(), want), (use_graph, persistent)
 
 
 def test_routesum_residual_matches_f64(fused, oracle, bank, cuda):
