@@ -143,9 +143,35 @@ def time_region(fn, steps, device):
     return a.elapsed_time(b)
 
 
+def time_graph(fn, steps, device):
+    """Device time per call (ms) of `steps` calls of fn captured in one CUDA
+    graph, so that host launch cost does not hide short kernels; replayed
+    once untimed, then timed with CUDA events."""
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        fn(0)
+    torch.cuda.current_stream(device).wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(steps):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize(device)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    g.replay()
+    b.record()
+    b.synchronize()
+    del g
+    return a.elapsed_time(b) / steps
+
+
 def kernel_roofline(dec, bank, device, hbm, iters=192):
-    """Average device time of the two grouped expert kernels, each launch on
-    a different (layer, token) routing so that weights come from HBM."""
+    """Average device time of the two grouped expert kernels (a CUDA graph of
+    `iters` launches each, timed with CUDA events), each launch on a
+    different (layer, token) routing so that weights come from HBM."""
     from ervf_b200.fused_nvfp4 import FusedNVFP4
 
     f = dec.fused
@@ -173,8 +199,8 @@ def kernel_roofline(dec, bank, device, hbm, iters=192):
     for fn in (up, down):
         for i in range(8):
             fn(i)
-    t_up = time_region(up, iters, device) / iters
-    t_dn = time_region(down, iters, device) / iters
+    t_up = time_graph(up, iters, device)
+    t_dn = time_graph(down, iters, device)
     rec = INTER * HIDDEN // 2 + INTER * HIDDEN // 16
     up_bytes = TOP_K * rec + HIDDEN * 4 + TOP_K * INTER * 4
     dn_bytes = TOP_K * rec + TOP_K * INTER * 4 + 2 * HIDDEN * 4
@@ -189,8 +215,9 @@ def kernel_roofline(dec, bank, device, hbm, iters=192):
 
 def gemv_shape(device, hbm, rows=INTER, cols=HIDDEN, min_iters=64):
     """One NVFP4 GEMV [rows x cols] (config 0 by default) cycling over a
-    replica pool of >= 8 x L2 (L2-cold weights; one copy when a single matrix
-    already exceeds that), B200 schedule, CUDA-event time per call.
+    replica pool of >= 8 x L2 (L2-cold weights; two copies when a single
+    matrix already exceeds 2 x L2), B200 schedule, device time per call from
+    a CUDA graph of the calls.
     Algorithmic bytes per call: codes + scales + global scale + x + out."""
     from ervf_b200 import FusedNVFP4
     from ervf_b200.formats import quantize_nvfp4_torch
@@ -217,10 +244,44 @@ def gemv_shape(device, hbm, rows=INTER, cols=HIDDEN, min_iters=64):
     for i in range(10):
         call(i)
     iters = max(min_iters, 4 * n)
-    ms = time_region(call, iters, device) / iters
+    ms = time_graph(call, iters, device)
     algo = rec + 4 + cols * 4 + rows * 4
     return {"rows": rows, "cols": cols, "us": ms * 1e3, "gbs": algo / ms / 1e6,
             "frac": algo / ms / 1e6 / hbm, "pool_replicas": n, "bytes_per_call": algo}
+
+
+def bf16_gemvs(device, hbm):
+    """Config 3: BF16 dense GEMVs [4096x2688], [2688x4096] and the output head
+    [131072x2688] at batch 1 and 8, cycling an L2-cold replica pool (>= 8 x
+    L2; the head alone exceeds L2), device time per call from a CUDA graph.  Algorithmic
+    bytes: 2*rows*cols + 4*cols*B + 4*rows*B."""
+    from ervf_b200 import GPUKernels
+
+    k = GPUKernels(device=device)
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    res = {}
+    for rows, cols in ((4096, 2688), (2688, 4096), (131072, 2688)):
+        nbytes = 2 * rows * cols
+        n = max(1, (8 * l2) // nbytes + 1) if nbytes < 2 * l2 else 2
+        w1 = (torch.randn(rows * cols, device=device) * 0.02).to(torch.bfloat16).view(torch.int16)
+        W = w1.reshape(1, -1).repeat(n, 1)
+        del w1
+        for batch in (1, 8):
+            x = torch.randn(batch * cols, device=device)
+            out = torch.zeros(batch * rows, device=device)
+
+            def call(i):
+                k.mv_bf16_batched(out, W[i % n], x, rows, cols, batch)
+
+            for i in range(3):
+                call(i)
+            iters = max(16, 4 * n)
+            ms = time_graph(call, iters, device)
+            algo = nbytes + 4 * cols * batch + 4 * rows * batch
+            res[f"{rows}x{cols}_b{batch}"] = {"us": round(ms * 1e3, 2), "gbs": round(algo / ms / 1e6, 1),
+                                              "frac": round(algo / ms / 1e6 / hbm, 4)}
+        del W
+    return res
 
 
 def cpu_sample(bank, layers_sampled=2, tokens=2):
@@ -423,6 +484,12 @@ def main():
 
     kern = kernel_roofline(dec, bank, device, hbm) if world == 1 else None
     gemv0 = gemv_shape(device, hbm) if (world == 1 and rank == 0) else None
+    extra = None
+    if world == 1 and rank == 0:
+        # config 2 (Qwen shapes) GEMVs and config 3 BF16 GEMVs, L2-cold
+        extra = {"gemv_config2": {f"{r}x{c}": gemv_shape(device, hbm, r, c) for r, c in
+                                  ((1536, 2048), (2048, 768))},
+                 "bf16_gemv_config3": bf16_gemvs(device, hbm)}
 
     if rank == 0:
         # bytes one token streams: distinct (layer, expert) pairs x expert bytes
@@ -458,6 +525,8 @@ def main():
             line["kernels"] = kern
         if gemv0 is not None:
             line["gemv_config0"] = gemv0
+        if extra is not None:
+            line.update(extra)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_sample(bank)
         print(json.dumps(line), flush=True)

@@ -23,6 +23,7 @@ ERR_SCRATCH_LIMIT = -8
 
 LAUNCH_PDL = 1
 LAUNCH_IDS_READY = 2
+UP_SWIGLU = 4
 
 _NAMES = {
     ERR_NULL: "null pointer",
@@ -57,6 +58,7 @@ SIGNATURES: dict[str, list] = {
     "ervf_decode_scratch_bytes": [_i, _i],
     "ervf_moe_down_routesum_static": [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp,
                                       _i, _i, _i, _i, _vp],
+    "ervf_route_topk_softmax": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "ervf_route_topk_batched": [_vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp],
     "ervf_ep_expert_slots": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _i, _vp, _vp, _vp,
                              _i, _i, _i, _i, _i, _vp],

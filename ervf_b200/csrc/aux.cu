@@ -402,6 +402,79 @@ int launch_route_topk(const float* rlog, const float* gate_b, int* ids, float* w
   return launch_route_topk_batched(rlog, gate_b, ids, w, 1, n, top_k, scaling, bad_pick, 0, stream);
 }
 
+// Softmax top-k routing (config 2, Qwen shape), one warp per layer: the k
+// largest logits in descending order, ties to the lowest index (the order of
+// the reference router's strict `>` scan), then w_i = e_i / sum with
+// e_i = expf(logit_i - logit_max) over the selected experts and sum added in
+// selection order from 0 -- the renormalised softmax of the selected experts
+// (the full softmax denominator cancels).  n <= 32 * NPL, top_k <= 32.
+template <int NPL>
+__global__ void route_topk_softmax_kernel(const float* __restrict__ rlog, int* __restrict__ ids,
+                                          float* __restrict__ w, int layers, int n, int top_k) {
+  const int lane = threadIdx.x & 31;
+  const int layer = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (layer >= layers) return;
+  const float* lg = rlog + (size_t)layer * n;
+  float v[NPL];
+  bool taken[NPL];
+#pragma unroll
+  for (int j = 0; j < NPL; ++j) {
+    const int e = lane + 32 * j;
+    v[j] = e < n ? lg[e] : 0.0f;
+    taken[j] = e >= n;
+  }
+  float top = 0.0f, mine = 0.0f, sum = 0.0f;
+  int my_id = 0;
+  for (int s = 0; s < top_k; ++s) {
+    float bv = 0.0f;
+    int bi = -1;
+#pragma unroll
+    for (int j = 0; j < NPL; ++j)
+      if (!taken[j] && (bi < 0 || v[j] > bv)) {
+        bv = v[j];
+        bi = lane + 32 * j;
+      }
+    // warp arg-max: larger value wins, equal values go to the lower index
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (s == 0) top = bv;
+    const float e = expf(bv - top);
+    sum += e;
+    if (lane == s) {
+      my_id = bi;
+      mine = e;
+    }
+#pragma unroll
+    for (int j = 0; j < NPL; ++j)
+      if (bi == lane + 32 * j) taken[j] = true;
+  }
+  if (lane < top_k) {
+    ids[(size_t)layer * top_k + lane] = my_id;
+    w[(size_t)layer * top_k + lane] = mine / sum;
+  }
+}
+
+int launch_route_topk_softmax(const float* rlog, int* ids, float* w, int layers, int n, int top_k,
+                              cudaStream_t stream) {
+  const int warps = 4;
+  const int grid = (layers + warps - 1) / warps;
+  if (n <= 128) {
+    route_topk_softmax_kernel<4><<<grid, 32 * warps, 0, stream>>>(rlog, ids, w, layers, n, top_k);
+  } else if (n <= 256) {
+    route_topk_softmax_kernel<8><<<grid, 32 * warps, 0, stream>>>(rlog, ids, w, layers, n, top_k);
+  } else {
+    route_topk_softmax_kernel<32><<<grid, 32 * warps, 0, stream>>>(rlog, ids, w, layers, n, top_k);
+  }
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
 int launch_route_topk_batched(const float* rlog, const float* gate_b, int* ids, float* w, int layers,
                               int n, int top_k, float scaling, int bad_pick, int bias_stride,
                               cudaStream_t stream) {

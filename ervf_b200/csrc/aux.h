@@ -9,6 +9,8 @@ namespace ervf {
 
 int launch_route_topk(const float* rlog, const float* gate_b, int* ids, float* w, int n, int top_k,
                       float scaling, int bad_pick, cudaStream_t stream);
+int launch_route_topk_softmax(const float* rlog, int* ids, float* w, int layers, int n, int top_k,
+                              cudaStream_t stream);
 int launch_route_topk_batched(const float* rlog, const float* gate_b, int* ids, float* w, int layers,
                               int n, int top_k, float scaling, int bad_pick, int bias_stride,
                               cudaStream_t stream);

@@ -138,13 +138,16 @@ int ervf_moe_up_grouped(const uint8_t* up_codes, const uint8_t* up_scales, size_
                         void* stream) {
   if (!up_codes || !up_scales || !ids || !globals || !x || !act) return kErrNull;
   if (top_k <= 0 || top_k > kMaxJobs) return kErrShape;
-  if (int e = check_nvfp4_shape(inter, hidden, width)) return e;
+  const bool swiglu = (flags & ERVF_UP_SWIGLU) != 0;
+  const int rows = swiglu ? 2 * inter : inter;
+  if (int e = check_nvfp4_shape(rows, hidden, width)) return e;
   if (!al(up_codes, 4) || (up_code_stride & 3) || !al(x, 4) || !al(act, 4)) return kErrAlign;
   GemvBatch b{};
-  b.rows = inter;
+  b.rows = rows;
   b.cols = hidden;
   b.njobs = top_k;
-  b.relu2 = 1;
+  b.relu2 = swiglu ? 0 : 1;
+  b.swiglu = swiglu ? 1 : 0;
   b.out_scale = 1.0f;
   b.pdl = (flags & ERVF_LAUNCH_PDL) ? 1 : 0;
   b.ids_ready = (flags & ERVF_LAUNCH_IDS_READY) ? 1 : 0;
@@ -162,6 +165,7 @@ int ervf_moe_up_grouped(const uint8_t* up_codes, const uint8_t* up_scales, size_
     b.job[s].x = x;
     b.job[s].out = act + (size_t)s * inter;
   }
+  if (swiglu && (width != 0 || !nvfp4_tma_ok(b))) return kErrArg;  // B200 schedule only
   return launch_nvfp4_batch(b, width, S(stream));
 }
 
@@ -371,6 +375,13 @@ int ervf_route_topk_batched(const float* rlog, const float* gate_b, int32_t* ids
   if (n > 256 && !gate_b) return kErrNull;
   return launch_route_topk_batched(rlog, gate_b, ids, w, layers, n, top_k, scaling, bad_pick,
                                    bias_stride, S(stream));
+}
+
+int ervf_route_topk_softmax(const float* rlog, int32_t* ids, float* w, int layers, int n,
+                            int top_k, void* stream) {
+  if (!rlog || !ids || !w) return kErrNull;
+  if (layers <= 0 || n <= 0 || n > 1024 || top_k <= 0 || top_k > 32 || top_k > n) return kErrShape;
+  return launch_route_topk_softmax(rlog, ids, w, layers, n, top_k, S(stream));
 }
 
 int ervf_cache_assign(int32_t* slot_of, int32_t* expert_of, int32_t* last_used, int32_t* state2,

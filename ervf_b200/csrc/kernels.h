@@ -39,6 +39,7 @@ struct GemvJob {
 struct GemvBatch {
   int rows, cols, njobs, mode;
   int relu2;
+  int swiglu;  // mode 0, TMA schedule: rows 2i / 2i+1 are gate / up, out[i] = silu(gate) * up
   float out_scale;
   int legacy_tree;  // 1: the 256-thread kernel's combine (S + 0.0 per group sum)
   GemvJob job[kMaxJobs];
@@ -110,6 +111,10 @@ int launch_moe_decode(const DecodeArgs& a, cudaStream_t stream);
 // preconditions do not hold); 4/8/16/32: W lanes per row, lane L owning the
 // chains L + W*i.  Every schedule returns the same bits.
 int launch_nvfp4_batch(const GemvBatch& b, int width, cudaStream_t stream);
+
+// True when the batch meets the B200 schedule's preconditions (cols % 32,
+// cols <= 4096, 16-byte aligned bases and strides, routed-sum scratch).
+bool nvfp4_tma_ok(const GemvBatch& b);
 
 // BF16 GEMV (gpu_kernels.py:21-49 semantics), out[b*rows + r].
 int launch_bf16_gemv(const uint16_t* W, const float* x, float* out, int rows, int cols,

@@ -224,6 +224,9 @@ __device__ __forceinline__ void unit_fma(const uint4 q, const float s0, const fl
   }
 }
 
+// SiLU of the gate row, v / (1 + e^-v) in binary32 (CUDA expf).
+__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+
 // Activation of unit u from the swizzled shared copy (float4 i at u*8 + (i ^ (u & 7))).
 __device__ __forceinline__ void load_unit_x(const float4* xs, int u, float (&x)[32]) {
 #pragma unroll
@@ -471,8 +474,13 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
     float y = 0.0f;
     if (tr < nrows) y = group_tree(part + tr * kRowPitch + tw * kGroupPitch);
     y = combine8(legacy_fix(y, p.legacy_tree));
+    // SwiGLU: rows 2i (gate) and 2i+1 (up) sit 8 lanes apart in one warp
+    const float y_up = __shfl_down_sync(0xffffffffu, y, 8);
     named_bar_sync(kBarC, kCT);  // the chain buffer is rewritten by the next item
-    if (tw == 0 && tr < nrows) {
+    if (p.swiglu) {
+      if (tw == 0 && (tr & 1) == 0 && tr + 1 < nrows)
+        J.out[(r0 + tr) >> 1] = silu(y) * y_up;
+    } else if (tw == 0 && tr < nrows) {
       const int r = r0 + tr;
       if (p.mode == 0) {
         J.out[r] = epilogue(y, p.relu2, p.out_scale);
@@ -874,6 +882,7 @@ int launch_tma(const GemvBatch& b, cudaStream_t stream) {
   c.teams = kCT / c.n_u;
   if (c.teams > 16) c.teams = 16;
   c.blk = row_block(b.cols);
+  if (b.swiglu && c.blk < 2) c.blk = 2;  // gate / up row pairs stay in one item
   const int cb = b.cols / 2, sb = b.cols / 16;
   const int budget = (di.smem_sm - kCtasPerSm * 1024) / kCtasPerSm;
   // Largest H (rows per segment) whose chain buffer, activation and two
@@ -963,6 +972,8 @@ int launch_sched_w(const GemvBatch& b, cudaStream_t stream) {
 }
 
 }  // namespace
+
+bool nvfp4_tma_ok(const GemvBatch& b) { return tma_ok(b); }
 
 int device_sm_count() { return dev_info().sms; }
 int device_smem_optin() { return dev_info().smem_optin; }

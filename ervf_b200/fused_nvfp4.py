@@ -253,6 +253,12 @@ class FusedNVFP4:
                                      device=self.device)
         return cache[key]
 
+    def route_topk_softmax(self, rlogs, ids, w, layers: int, n: int, top_k: int) -> None:
+        """Softmax top-k routing (Qwen-shaped experts) of `layers` logit rows:
+        ids[l][s], w[l][s] = renormalised softmax of the selected experts."""
+        _lib.call("ervf_route_topk_softmax", ptr(rlogs), ptr(ids), ptr(w), int(layers), int(n),
+                  int(top_k), self._s())
+
     def route_topk_batched(self, rlogs, gate_b, ids, w, layers: int, n: int, top_k: int,
                            scaling: float, bad_pick: int = 0, bias_stride: int = 0) -> None:
         """route_topk for `layers` independent logit rows in one launch."""

@@ -50,6 +50,11 @@ extern "C" {
  *   be read -- and the routed experts' weights streamed -- before the wait. */
 #define ERVF_LAUNCH_PDL 1
 #define ERVF_LAUNCH_IDS_READY 2
+/* ervf_moe_up_grouped only: SwiGLU experts (Qwen shape).  The up record has
+ * 2*inter rows, gate and up interleaved (row 2i = gate i, row 2i+1 = up i),
+ * and act[s*inter + i] = silu(gate_i) * up_i, silu(v) = v / (1 + expf(-v)).
+ * B200 schedule (width 0) only.  The reference has no SwiGLU NVFP4 kernel. */
+#define ERVF_UP_SWIGLU 4
 
 /* Library version, e.g. 100 for 0.1.0. */
 ERVF_API int ervf_version(void);
@@ -233,6 +238,15 @@ ERVF_API int ervf_route_topk(const float* rlog, const float* gate_b, int32_t* id
 ERVF_API int ervf_route_topk_batched(const float* rlog, const float* gate_b, int32_t* ids, float* w,
                                      int layers, int n, int top_k, float scaling, int bad_pick,
                                      int bias_stride, void* stream);
+
+/* Softmax top-k routing of `layers` logit rows f32[layers][n] (config 2,
+ * Qwen shape; the reference's router is sigmoid only): per layer the top_k
+ * largest logits in descending order (ties to the lowest index), ids[l][s]
+ * and w[l][s] = e_s / sum, e_s = expf(logit_s - logit_max), sum added in
+ * selection order -- the renormalised softmax of the selected experts.
+ * n <= 1024, top_k <= 32.  No counterpart in the reference. */
+ERVF_API int ervf_route_topk_softmax(const float* rlog, int32_t* ids, float* w, int layers, int n,
+                                     int top_k, void* stream);
 
 /* Device LRU slot assignment: replaces cache_assign / FusedNVFP4.cache_assign
  * (fused_nvfp4.py:470-511, :803-808). */
