@@ -384,6 +384,14 @@ int ervf_route_topk_softmax(const float* rlog, int32_t* ids, float* w, int layer
   return launch_route_topk_softmax(rlog, ids, w, layers, n, top_k, S(stream));
 }
 
+int ervf_nvfp4_gemm_tc(const uint8_t* codes, const uint8_t* scales, float global_scale,
+                       const float* x, float* out, int rows, int cols, int n, void* stream) {
+  if (!codes || !scales || !x || !out) return kErrNull;
+  if (rows <= 0 || cols <= 0 || cols % 32 || n < 1 || n > 16) return kErrShape;
+  if (!al(codes, 16) || !al(scales, 2) || !al(x, 16) || !al(out, 4)) return kErrAlign;
+  return launch_nvfp4_gemm_tc(codes, scales, global_scale, x, out, rows, cols, n, S(stream));
+}
+
 int ervf_cache_assign(int32_t* slot_of, int32_t* expert_of, int32_t* last_used, int32_t* state2,
                       const int32_t* ids, int32_t* slots, int32_t* need, int32_t* stats2, int cap,
                       int top_k, void* stream) {

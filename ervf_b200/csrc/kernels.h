@@ -116,6 +116,11 @@ int launch_nvfp4_batch(const GemvBatch& b, int width, cudaStream_t stream);
 // cols <= 4096, 16-byte aligned bases and strides, routed-sum scratch).
 bool nvfp4_tma_ok(const GemvBatch& b);
 
+// Batched NVFP4 GEMM on the tensor cores (nvfp4_gemm_tc.cu):
+// out[n][r] = g * (W @ X[n])[r] for n < N <= 16, fp32 accumulate.
+int launch_nvfp4_gemm_tc(const uint8_t* codes, const uint8_t* scales, float g, const float* x,
+                         float* out, int rows, int cols, int n, cudaStream_t stream);
+
 // BF16 GEMV (gpu_kernels.py:21-49 semantics), out[b*rows + r].
 int launch_bf16_gemv(const uint16_t* W, const float* x, float* out, int rows, int cols,
                      int batch, cudaStream_t stream);

@@ -253,6 +253,13 @@ class FusedNVFP4:
                                      device=self.device)
         return cache[key]
 
+    def gemm_tc(self, out, codes, scales, x, global_scale: float, rows: int, cols: int,
+                n: int) -> None:
+        """Batched NVFP4 GEMM on the tensor cores for n <= 16 activation rows:
+        out[j*rows + r] = g * (W @ x[j])[r] (tolerance path, fp32 accumulate)."""
+        _lib.call("ervf_nvfp4_gemm_tc", ptr(codes), ptr(scales), float(np.float32(global_scale)),
+                  ptr(x), ptr(out), int(rows), int(cols), int(n), self._s())
+
     def route_topk_softmax(self, rlogs, ids, w, layers: int, n: int, top_k: int) -> None:
         """Softmax top-k routing (Qwen-shaped experts) of `layers` logit rows:
         ids[l][s], w[l][s] = renormalised softmax of the selected experts."""

@@ -239,6 +239,18 @@ ERVF_API int ervf_route_topk_batched(const float* rlog, const float* gate_b, int
                                      int layers, int n, int top_k, float scaling, int bad_pick,
                                      int bias_stride, void* stream);
 
+/* Batched NVFP4 GEMM on the sm_100a tensor cores (tcgen05.mma, fp32
+ * accumulator in tensor memory): out[j*rows + r] = g * sum_k W[r][k] *
+ * x[j*cols + k] for the j < n <= 16 activation rows of a decode batch.  W is
+ * decoded exactly to f16 (e2m1 x E4M3), x is rounded to f16, g is applied to
+ * the fp32 result: held to rel-L2 <= 1e-3 against the FP32 dequantise-then-
+ * matmul, not to the batch-1 chain order.  cols % 32 == 0; codes 16-byte,
+ * x 16-byte aligned.  Replaces the batched SIMT gemm_nvfp4_rows_b
+ * (sweepspec.py:28-240) for one matrix. */
+ERVF_API int ervf_nvfp4_gemm_tc(const uint8_t* codes, const uint8_t* scales, float global_scale,
+                                const float* x, float* out, int rows, int cols, int n,
+                                void* stream);
+
 /* Softmax top-k routing of `layers` logit rows f32[layers][n] (config 2,
  * Qwen shape; the reference's router is sigmoid only): per layer the top_k
  * largest logits in descending order (ties to the lowest index), ids[l][s]
