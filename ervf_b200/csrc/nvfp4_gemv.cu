@@ -599,32 +599,22 @@ __device__ __forceinline__ void decode_segments(const TmaCfg& c, int tid, bool f
   }
 }
 
-// x_l = x_{l-1} + acc with acc = fmaf(contrib[s][r], w_s, acc) over the route
-// slots of layer l-1 in order from 0.0 (the routed sum with residual, as
-// ervf_moe_down_routesum computes it), for every row r, by the CTA's
-// consumer threads.  Writes the swizzled shared copy (xs, if given) and the
-// global vector (out, if given).  Reads through L2: other CTAs wrote contrib.
-__device__ __forceinline__ void rebuild_x(const DecodeArgs& a, int l, float4* xs, float* out) {
-  const float* xp = l == 1 ? a.x_in : a.xb + (size_t)((l - 2) & 1) * a.hidden;
-  const float* w = a.route_w + (size_t)(l - 1) * a.top_k;
-  const int n4 = a.hidden >> 2;
-  for (int f = threadIdx.x; f < n4; f += kCT) {
-    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (int s2 = 0; s2 < a.top_k; ++s2) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(a.contrib + (size_t)s2 * a.hidden) + f);
-      const float ws = __ldg(&w[s2]);
-      acc.x = fmaf(v.x, ws, acc.x);
-      acc.y = fmaf(v.y, ws, acc.y);
-      acc.z = fmaf(v.z, ws, acc.z);
-      acc.w = fmaf(v.w, ws, acc.w);
-    }
-    const float4 b = __ldcg(reinterpret_cast<const float4*>(xp) + f);
-    const float4 xv = make_float4(b.x + acc.x, b.y + acc.y, b.z + acc.z, b.w + acc.w);
-    if (xs) {
-      const int t = f >> 3, i = f & 7;
-      xs[t * 8 + (i ^ (t & 7))] = xv;
-    }
-    if (out) reinterpret_cast<float4*>(out)[f] = xv;
+// Route-order sum of layer l for this CTA's slice of rows (the grid splits
+// the hidden rows evenly): x_{l+1}[r] = x_l[r] + acc, acc = fmaf(contrib[s][r],
+// w_s, acc) over the route slots in order from 0.0 -- the routed sum with
+// residual as ervf_moe_down_routesum computes it.  Reads through L2: other
+// CTAs wrote contrib.
+__device__ __forceinline__ void sum_rows(const DecodeArgs& a, int l) {
+  const float* xl = l == 0 ? a.x_in : a.xb + (size_t)((l - 1) & 1) * a.hidden;
+  float* xn = a.xb + (size_t)(l & 1) * a.hidden;
+  const float* w = a.route_w + (size_t)l * a.top_k;
+  const int G = gridDim.x, b = blockIdx.x;
+  const int lo = (int)((long long)b * a.hidden / G), hi = (int)((long long)(b + 1) * a.hidden / G);
+  for (int r = lo + (int)threadIdx.x; r < hi; r += kCT) {
+    float acc = 0.0f;
+    for (int s2 = 0; s2 < a.top_k; ++s2)
+      acc = fmaf(__ldcg(&a.contrib[(size_t)s2 * a.hidden + r]), __ldg(&w[s2]), acc);
+    xn[r] = __ldcg(&xl[r]) + acc;
   }
 }
 
@@ -703,6 +693,7 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_moe_decode(DecodeArgs a, Tm
   float x[32];
   bool dead = false;
   int it = 0;
+  unsigned nbar = 0;  // grid barriers passed
   named_bar_sync(kBarC, kCT);
 
   for (int p = 0; p < P; ++p) {
@@ -713,8 +704,6 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_moe_decode(DecodeArgs a, Tm
     const int cb = cols >> 1, sb = cols >> 4;
     const int krt = down ? HD * 2 * cd.teams : HU * 2 * cu.teams;
     const float* x_l = l == 0 ? a.x_in : a.xb + (size_t)((l - 1) & 1) * a.hidden;
-    // x_l is written (by CTA 0) while the up phase of layer l refills it
-    float* x_next_prev = a.xb + (size_t)((l - 1) & 1) * a.hidden;
     // chain groups beyond this phase's units must read as zero in the tree
     for (int i = tid; i < krt_max * kRowPitch; i += kCT) part[i] = 0.0f;
     named_bar_sync(kBarC, kCT);
@@ -735,15 +724,10 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_moe_decode(DecodeArgs a, Tm
       const float* xj = down ? a.act + (size_t)job * a.inter : x_l;
       if (xj != cur_x || job != cur_job) {  // the previous item ended with a consumer barrier
         if (xj != cur_x) {
-          if (!down && l > 0) {
-            // x_l = x_{l-1} + route-order sum of the previous down phase
-            rebuild_x(a, l, xs, blockIdx.x == 0 ? x_next_prev : nullptr);
-          } else {
-            const float4* src = reinterpret_cast<const float4*>(xj);
-            for (int f = tid; f < c.n_u * 8; f += kCT) {
-              const int t = f >> 3, i = f & 7;
-              xs[t * 8 + (i ^ (t & 7))] = __ldcg(src + f);
-            }
+          const float4* src = reinterpret_cast<const float4*>(xj);
+          for (int f = tid; f < c.n_u * 8; f += kCT) {
+            const int t = f >> 3, i = f & 7;
+            xs[t * 8 + (i ^ (t & 7))] = __ldcg(src + f);
           }
           cur_x = xj;
           x_stale = true;
@@ -784,12 +768,13 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_moe_decode(DecodeArgs a, Tm
         }
       }
     }
-    if (p + 1 < P) {
-      dead = grid_barrier(a.grid_bar, (unsigned)((p + 1) * gridDim.x), dead);
-    } else {
-      // x_L: every CTA arrives, CTA 0 waits and sums the last down phase
-      dead = grid_barrier(a.grid_bar, (unsigned)((p + 1) * gridDim.x), dead || blockIdx.x != 0);
-      if (blockIdx.x == 0 && !dead) rebuild_x(a, a.layers, nullptr, a.xb + (size_t)((a.layers - 1) & 1) * a.hidden);
+    // every phase ends at a grid barrier; a down phase is followed by the
+    // slice-parallel route-order sum and (unless it was the last layer)
+    // another barrier before the next layer reads x_{l+1}
+    dead = grid_barrier(a.grid_bar, (unsigned)(++nbar * gridDim.x), dead);
+    if (down) {
+      if (!dead) sum_rows(a, l);
+      if (p + 1 < P) dead = grid_barrier(a.grid_bar, (unsigned)(++nbar * gridDim.x), dead);
     }
   }
 }

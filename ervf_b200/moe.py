@@ -134,9 +134,9 @@ class MoEDecoder:
         self.pdl = True
         # persistent=True: one cooperative launch for all layers of the token
         # (single GPU, bit-identical).  Off by default: on B200 the chain of
-        # PDL-overlapped per-layer launches is faster at batch 1 (0.62 vs
-        # 0.68 ms per 24-layer token), the grid barriers and the per-CTA
-        # rebuild of x costing more than the launch gaps they remove.
+        # PDL-overlapped per-layer launches is faster at batch 1 (0.61 vs
+        # 0.67 ms per 24-layer token); the three grid barriers per layer
+        # cost ~2.5-3 us each, mostly waiting for the slowest CTA.
         self.persistent = False
         self.table = torch.tensor(
             [[ptr(bank.up_codes[l]), ptr(bank.up_scales[l]), ptr(bank.dn_codes[l]),

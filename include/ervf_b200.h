@@ -142,8 +142,8 @@ ERVF_API size_t ervf_routesum_scratch_bytes(int hidden, int top_k);
  * layer's expert bank, records `*_stride` bytes apart (16-byte multiples).
  * x_in [hidden]; xbuf [2][hidden]: layer l writes xbuf[(l & 1) * hidden], so the
  * result is xbuf[((layers - 1) & 1) * hidden]; act [top_k][inter]; scratch:
- * ervf_decode_scratch_bytes(hidden, top_k) bytes, zero before its first use
- * (each call leaves it ready; calls that share it must not overlap).  hidden,
+ * ervf_decode_scratch_bytes(hidden, top_k) bytes (route-slot outputs and the
+ * grid-barrier counter; calls that share it must not overlap).  hidden,
  * inter: multiples of 32, <= 4096; top_k <= 16.  One cudaMemsetAsync precedes
  * the launch.  No counterpart in the reference. */
 ERVF_API int ervf_moe_decode(const void* layer_table, size_t up_code_stride,
