@@ -47,6 +47,8 @@ def parse():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--gemv", type=int, nargs=2, metavar=("ROWS", "COLS"),
                     help="time one NVFP4 GEMV shape instead of the decode step")
+    ap.add_argument("--gemm-tc", type=int, nargs=3, metavar=("ROWS", "COLS", "N"),
+                    help="time the tensor-core batched NVFP4 GEMM (N <= 16 tokens)")
     return ap.parse_args()
 
 
@@ -250,6 +252,41 @@ def gemv_shape(device, hbm, rows=INTER, cols=HIDDEN, min_iters=64):
             "frac": algo / ms / 1e6 / hbm, "pool_replicas": n, "bytes_per_call": algo}
 
 
+def gemm_tc_shape(device, hbm, rows, cols, n):
+    """Batched NVFP4 GEMM on the tensor cores: one matrix [rows x cols] times
+    n <= 16 activation rows, L2-cold replica pool, device time per call from a
+    CUDA graph.  Algorithmic bytes: codes + scales + n*cols*4 + n*rows*4; the
+    same weights through n batch-1 GEMVs are reported beside it."""
+    from ervf_b200 import FusedNVFP4
+    from ervf_b200.formats import quantize_nvfp4_torch
+
+    f = FusedNVFP4(device=device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    codes, scales, gsc = quantize_nvfp4_torch(torch.randn(rows, cols, generator=gen,
+                                                          device=device) * 0.02)
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    rec = codes.numel() + scales.numel()
+    m = max(1, (8 * l2) // rec + 1) if rec < 2 * l2 else 2
+    pc = codes.reshape(1, -1).repeat(m, 1)
+    ps = scales.reshape(1, -1).repeat(m, 1)
+    del codes, scales
+    x = torch.randn(n * cols, device=device)
+    out = torch.zeros(n * rows, device=device)
+    g = float(gsc)
+    iters = max(16, 4 * m)
+    ms = time_graph(lambda i: f.gemm_tc(out, pc[i % m], ps[i % m], x, g, rows, cols, n), iters, device)
+    o1 = torch.zeros(rows, device=device)
+    ms1 = time_graph(lambda i: f.gemv_into(o1, pc[i % m], ps[i % m], x[:cols], g, rows, cols),
+                     iters, device)
+    algo = rec + n * cols * 4 + n * rows * 4
+    return {"rows": rows, "cols": cols, "n": n, "us": round(ms * 1e3, 2),
+            "gbs": round(algo / ms / 1e6, 1), "frac": round(algo / ms / 1e6 / hbm, 4),
+            "tokens_per_s": round(n / (ms * 1e-3), 1),
+            "batch1_gemv_us": round(ms1 * 1e3, 2),
+            "speedup_vs_n_batch1_gemvs": round(n * ms1 / ms, 2)}
+
+
 def bf16_gemvs(device, hbm):
     """Config 3: BF16 dense GEMVs [4096x2688], [2688x4096] and the output head
     [131072x2688] at batch 1 and 8, cycling an L2-cold replica pool (>= 8 x
@@ -376,6 +413,11 @@ def main():
         r.update({"peak_gbs": hbm, "peak_kind": peak_kind})
         print(json.dumps({"gemv": r}))
         return
+    if args.gemm_tc:
+        r = gemm_tc_shape(device, hbm, *args.gemm_tc)
+        r.update({"peak_gbs": hbm, "peak_kind": peak_kind})
+        print(json.dumps({"gemm_tc": r}))
+        return
     L = args.layers
     t0 = time.time()
     bank = ExpertBank(L, N_EXPERTS, HIDDEN, INTER, device)
@@ -489,7 +531,10 @@ def main():
         # config 2 (Qwen shapes) GEMVs and config 3 BF16 GEMVs, L2-cold
         extra = {"gemv_config2": {f"{r}x{c}": gemv_shape(device, hbm, r, c) for r, c in
                                   ((1536, 2048), (2048, 768))},
-                 "bf16_gemv_config3": bf16_gemvs(device, hbm)}
+                 "bf16_gemv_config3": bf16_gemvs(device, hbm),
+                 # config 2 batch-16 variant on the tensor cores
+                 "gemm_tc_config2_b16": {f"{r}x{c}": gemm_tc_shape(device, hbm, r, c, 16) for r, c in
+                                         ((1536, 2048), (2048, 768))}}
 
     if rank == 0:
         # bytes one token streams: distinct (layer, expert) pairs x expert bytes
