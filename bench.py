@@ -317,6 +317,15 @@ def bf16_gemvs(device, hbm):
             algo = nbytes + 4 * cols * batch + 4 * rows * batch
             res[f"{rows}x{cols}_b{batch}"] = {"us": round(ms * 1e3, 2), "gbs": round(algo / ms / 1e6, 1),
                                               "frac": round(algo / ms / 1e6 / hbm, 4)}
+            if batch > 1:  # the tensor-core path (tolerance) beside the SIMT one
+
+                def call_tc(i):
+                    k.mm_bf16_tc(out, W[i % n], x, rows, cols, batch)
+
+                ms = time_graph(call_tc, iters, device)
+                res[f"{rows}x{cols}_b{batch}_tc"] = {"us": round(ms * 1e3, 2),
+                                                     "gbs": round(algo / ms / 1e6, 1),
+                                                     "frac": round(algo / ms / 1e6 / hbm, 4)}
         del W
     return res
 

@@ -58,6 +58,7 @@ SIGNATURES: dict[str, list] = {
     "ervf_decode_scratch_bytes": [_i, _i],
     "ervf_moe_down_routesum_static": [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp,
                                       _i, _i, _i, _i, _vp],
+    "ervf_bf16_gemm_tc": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "ervf_nvfp4_gemm_tc": [_vp, _vp, _f, _vp, _vp, _i, _i, _i, _vp],
     "ervf_route_topk_softmax": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "ervf_route_topk_batched": [_vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp],

@@ -392,6 +392,14 @@ int ervf_nvfp4_gemm_tc(const uint8_t* codes, const uint8_t* scales, float global
   return launch_nvfp4_gemm_tc(codes, scales, global_scale, x, out, rows, cols, n, S(stream));
 }
 
+int ervf_bf16_gemm_tc(const uint16_t* W, const float* x, float* out, int rows, int cols, int batch,
+                      void* stream) {
+  if (!W || !x || !out) return kErrNull;
+  if (rows <= 0 || cols <= 0 || cols % 32 || batch < 1 || batch > 8) return kErrShape;
+  if (!al(W, 16) || !al(x, 16) || !al(out, 4)) return kErrAlign;
+  return launch_bf16_gemm_tc(W, x, out, rows, cols, batch, S(stream));
+}
+
 int ervf_cache_assign(int32_t* slot_of, int32_t* expert_of, int32_t* last_used, int32_t* state2,
                       const int32_t* ids, int32_t* slots, int32_t* need, int32_t* stats2, int cap,
                       int top_k, void* stream) {

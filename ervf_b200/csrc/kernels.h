@@ -121,6 +121,11 @@ bool nvfp4_tma_ok(const GemvBatch& b);
 int launch_nvfp4_gemm_tc(const uint8_t* codes, const uint8_t* scales, float g, const float* x,
                          float* out, int rows, int cols, int n, cudaStream_t stream);
 
+// Batched BF16 GEMM on the tensor cores: out[n][r] = (W @ X[n])[r] for
+// n < N <= 8 (X split into bf16 high / low halves), fp32 accumulate.
+int launch_bf16_gemm_tc(const uint16_t* W, const float* x, float* out, int rows, int cols, int n,
+                        cudaStream_t stream);
+
 // BF16 GEMV (gpu_kernels.py:21-49 semantics), out[b*rows + r].
 int launch_bf16_gemv(const uint16_t* W, const float* x, float* out, int rows, int cols,
                      int batch, cudaStream_t stream);

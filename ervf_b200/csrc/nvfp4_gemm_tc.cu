@@ -46,12 +46,18 @@ constexpr int kTcBStage = kTcN * kTcKB * 2;             // 2 KB
 constexpr int kTcRawDepth = 8;                          // k-blocks of codes in flight
 constexpr int kTcRawStage = kTcM * (kTcKB / 2);         // 4 KB of code bytes
 constexpr int kTcSmem = 1024 + 2 * kTcBStage + kTcRawDepth * kTcRawStage;
+// BF16 weights (dense projections): 64 B of one row per thread and k-block
+constexpr int kTcRawDepthBf = 4;
+constexpr int kTcRawStageBf = kTcM * kTcKB * 2;         // 16 KB
+constexpr int kTcSmemBf = 1024 + 2 * kTcBStage + kTcRawDepthBf * kTcRawStageBf;
+
+enum TcMode { kTcNvfp4 = 0, kTcBf16 = 1 };
 constexpr int kTcTmemCols = 128;     // D: columns 0..15; A stages: 32..63, 64..95
 constexpr int kTcACol = 32;
 constexpr int kTcAStageCols = kTcKB / 2;  // two f16 per 32-bit column
 
 struct TcArgs {
-  const uint8_t* codes;   // [rows][cols/2]
+  const uint8_t* codes;   // [rows][cols/2]; kTcBf16: bf16 weights [rows][cols]
   const uint8_t* scales;  // [rows][cols/16]
   float g;
   const float* x;         // [n][cols]
@@ -67,8 +73,17 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46);
 }
 
-// kind::f16 instruction descriptor: D f32, A f16, B f16, K-major, N, M.
+// kind::f16 instruction descriptor: D f32, A / B f16 (or bf16), K-major, N, M.
 constexpr uint32_t kTcIdesc = (1u << 4) | ((uint32_t)(kTcN >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
+constexpr uint32_t kTcIdescBf = kTcIdesc | (1u << 7) | (1u << 10);
+
+__device__ __forceinline__ uint32_t f32x2_to_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
   uint32_t d;
@@ -129,12 +144,16 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity) {
   return mbar_wait(bar, parity, 2000000000LL);
 }
 
+template <int MODE>
 __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
+  constexpr int kDepth = MODE == kTcBf16 ? kTcRawDepthBf : kTcRawDepth;
+  constexpr int kRawStage = MODE == kTcBf16 ? kTcRawStageBf : kTcRawStage;
+  constexpr int kUnitBytes = MODE == kTcBf16 ? 64 : 16;  // per thread and k-block
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* mb = reinterpret_cast<uint64_t*>(smem);  // [0,1]: stage done, [2]: accumulator done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 64);
   uint8_t* bst0 = smem + 1024;                       // two B stages
-  uint8_t* raw0 = bst0 + 2 * kTcBStage;              // [depth][128 rows][32 code bytes]
+  uint8_t* raw0 = bst0 + 2 * kTcBStage;              // [depth][128 rows][2 x unit bytes]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int cb = a.cols >> 1, sb = a.cols >> 4, n_u = a.cols >> 5;
   const int nkb = (a.cols + kTcKB - 1) / kTcKB;
@@ -177,19 +196,28 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
     // This thread's code unit of k-block kb goes, by cp.async, to raw ring
     // slot kb % depth (the thread that copies a unit decodes it: no barrier);
     // its two scale bytes go to a register ring of the same depth.
-    uint8_t* my_raw = raw0 + rr * (kTcKB / 2) + 16 * half;
+    uint8_t* my_raw = raw0 + rr * (2 * kUnitBytes) + kUnitBytes * half;
+    const uint8_t* wrow = a.codes + (size_t)row * a.cols * 2;  // kTcBf16
     auto copy_unit = [&](int kb) {
       const int u = 2 * kb + half;
       const bool ok = row_ok && u < n_u;
-      cp_async16(my_raw + (kb % kTcRawDepth) * kTcRawStage, ok ? crow + 16 * u : a.codes, ok ? 16u : 0u);
+      uint8_t* dst = my_raw + (kb % kDepth) * kRawStage;
+      if constexpr (MODE == kTcBf16) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          cp_async16(dst + 16 * i, ok ? wrow + 64 * u + 16 * i : a.codes, ok ? 16u : 0u);
+      } else {
+        cp_async16(dst, ok ? crow + 16 * u : a.codes, ok ? 16u : 0u);
+      }
     };
     auto scale_of = [&](int kb) -> uint32_t {
+      if constexpr (MODE == kTcBf16) return 0u;
       const int u = 2 * kb + half;
       return (row_ok && u < n_u) ? (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(srow + 2 * u)) : 0u;
     };
-    uint32_t svr[kTcRawDepth];
+    uint32_t svr[kDepth];
 #pragma unroll
-    for (int d = 0; d < kTcRawDepth - 1; ++d) {
+    for (int d = 0; d < kDepth - 1; ++d) {
       if (kb0 + d < kb1) {
         copy_unit(kb0 + d);
         svr[d] = scale_of(kb0 + d);
@@ -198,9 +226,10 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
     }
     auto load_x = [&](int kb, float4 (&v)[2]) {
       const int k = kb * kTcKB + bc * 8;
-      if (tid < 128 && bn < a.n && k < a.cols) {
-        v[0] = __ldg(reinterpret_cast<const float4*>(a.x + (size_t)bn * a.cols + k));
-        v[1] = __ldg(reinterpret_cast<const float4*>(a.x + (size_t)bn * a.cols + k + 4));
+      const int xn = MODE == kTcBf16 ? (bn & 7) : bn;  // kTcBf16: rows n and n + 8 share X[n]
+      if (tid < 128 && xn < a.n && k < a.cols) {
+        v[0] = __ldg(reinterpret_cast<const float4*>(a.x + (size_t)xn * a.cols + k));
+        v[1] = __ldg(reinterpret_cast<const float4*>(a.x + (size_t)xn * a.cols + k + 4));
       } else {
         v[0] = v[1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
@@ -212,34 +241,56 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
       const int s = (int)(gkb & 1u);
       // the MMAs that last read this stage (two k-blocks ago) are complete
       if (gkb >= 2 && !dead) dead = !tc_wait(&mb[s], ((gkb >> 1) - 1) & 1u);
-      const int slot = (kb - kb0) % kTcRawDepth;
+      const int slot = (kb - kb0) % kDepth;
       {
-        const int ahead = kb + kTcRawDepth - 1;
+        const int ahead = kb + kDepth - 1;
         if (ahead < kb1) {
           copy_unit(ahead);
-          const int idx = (ahead - kb0) % kTcRawDepth;
+          const int idx = (ahead - kb0) % kDepth;
 #pragma unroll
-          for (int d = 0; d < kTcRawDepth; ++d)  // static slots keep the ring in registers
+          for (int d = 0; d < kDepth; ++d)  // static slots keep the ring in registers
             if (d == idx) svr[d] = scale_of(ahead);
         }
         cp_async_commit();
       }
-      cp_async_wait<kTcRawDepth - 1>();  // this k-block's unit has landed
-      uint32_t sv = 0;
-#pragma unroll
-      for (int d = 0; d < kTcRawDepth; ++d)
-        if (d == slot) sv = svr[d];
-      const uint4 q = *reinterpret_cast<const uint4*>(my_raw + (kb % kTcRawDepth) * kTcRawStage);
+      cp_async_wait<kDepth - 1>();  // this k-block's unit has landed
+      const uint8_t* mine = my_raw + (kb % kDepth) * kRawStage;
       uint32_t w[16];
-      decode_unit(q, sv, w);
+      if constexpr (MODE == kTcBf16) {
+        // bf16 pairs are already the 32-bit column layout (K order, low first)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint4 v = *reinterpret_cast<const uint4*>(mine + 16 * i);
+          w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+        }
+      } else {
+        uint32_t sv = 0;
+#pragma unroll
+        for (int d = 0; d < kDepth; ++d)
+          if (d == slot) sv = svr[d];
+        decode_unit(*reinterpret_cast<const uint4*>(mine), sv, w);
+      }
       // A: this row's 32 columns of the k-block into tensor memory
       tmem_st16(lane_base + kTcACol + s * kTcAStageCols + 16 * half, w);
-      // B: X rows as f16 (loaded one k-block ahead), zero beyond batch / cols
+      // B: X rows as f16 (loaded one k-block ahead), zero beyond batch / cols;
+      // kTcBf16: rows 0..7 the bf16 rounding of X, rows 8..15 its remainder
       if (tid < 128) {
         uint8_t* sbuf = bst0 + s * kTcBStage;
-        *reinterpret_cast<uint4*>(sbuf + (bn >> 3) * kTcBSBO + bc * 128 + (bn & 7) * 16) =
-            make_uint4(f32x2_to_f16x2(xv[0].x, xv[0].y), f32x2_to_f16x2(xv[0].z, xv[0].w),
-                       f32x2_to_f16x2(xv[1].x, xv[1].y), f32x2_to_f16x2(xv[1].z, xv[1].w));
+        uint4 v;
+        if constexpr (MODE == kTcBf16) {
+          const float e[8] = {xv[0].x, xv[0].y, xv[0].z, xv[0].w, xv[1].x, xv[1].y, xv[1].z, xv[1].w};
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            hw[i] = f32x2_to_bf16x2(e[2 * i], e[2 * i + 1]);
+            lw[i] = f32x2_to_bf16x2(e[2 * i] - bf16_lo(hw[i]), e[2 * i + 1] - bf16_hi(hw[i]));
+          }
+          v = bn < 8 ? make_uint4(hw[0], hw[1], hw[2], hw[3]) : make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        } else {
+          v = make_uint4(f32x2_to_f16x2(xv[0].x, xv[0].y), f32x2_to_f16x2(xv[0].z, xv[0].w),
+                         f32x2_to_f16x2(xv[1].x, xv[1].y), f32x2_to_f16x2(xv[1].z, xv[1].w));
+        }
+        *reinterpret_cast<uint4*>(sbuf + (bn >> 3) * kTcBSBO + bc * 128 + (bn & 7) * 16) = v;
       }
       if (kb + 1 < kb1) load_x(kb + 1, xv);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -256,8 +307,8 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
           asm volatile(
               "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
               " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
-              ::"r"(tmem), "r"(tmem + kTcACol + s * kTcAStageCols + 8 * j), "l"(db), "r"(kTcIdesc),
-                "r"(accum) : "memory");
+              ::"r"(tmem), "r"(tmem + kTcACol + s * kTcAStageCols + 8 * j), "l"(db),
+                "r"(MODE == kTcBf16 ? kTcIdescBf : kTcIdesc), "r"(accum) : "memory");
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                      ::"r"(smem_u32(&mb[s])) : "memory");
@@ -285,7 +336,8 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
 #pragma unroll
         for (int j = 0; j < kTcN; ++j) {
           if (j < a.n) {
-            const float y = __uint_as_float(v[j]) * a.g;
+            const float y = MODE == kTcBf16 ? (j < 8 ? __uint_as_float(v[j]) + __uint_as_float(v[j + 8]) : 0.0f)
+                                            : __uint_as_float(v[j]) * a.g;
             float* o = a.out + (size_t)j * a.rows + orow;
             if (a.splits > 1) {
               atomicAdd(o, y);
@@ -308,22 +360,25 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
 
 }  // namespace
 
-int launch_nvfp4_gemm_tc(const uint8_t* codes, const uint8_t* scales, float g, const float* x,
-                         float* out, int rows, int cols, int n, cudaStream_t stream) {
-  if (n < 1 || n > kTcN) return kErrShape;
+namespace {
+
+template <int MODE>
+int launch_tc(const uint8_t* w, const uint8_t* scales, float g, const float* x, float* out, int rows,
+              int cols, int n, cudaStream_t stream) {
+  constexpr int smem = MODE == kTcBf16 ? kTcSmemBf : kTcSmem;
+  auto kern = nvfp4_gemm_tc_kernel<MODE>;
   const int sms = device_sm_count();
-  if (cudaFuncSetAttribute(nvfp4_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kTcSmem) != cudaSuccess)
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return kErrLaunch;
   // CTAs per SM from the shared-memory footprint and the 512 tensor-memory
   // columns of an SM
   int smem_sm = 0;
   cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, 0);
-  int per_sm = smem_sm / (kTcSmem + 1024);
+  int per_sm = smem_sm / (smem + 1024);
   if (per_sm > 512 / kTcTmemCols) per_sm = 512 / kTcTmemCols;
   if (per_sm < 1) return kErrShape;
   TcArgs a{};
-  a.codes = codes;
+  a.codes = w;
   a.scales = scales;
   a.g = g;
   a.x = x;
@@ -342,8 +397,23 @@ int launch_nvfp4_gemm_tc(const uint8_t* codes, const uint8_t* scales, float g, c
   if (splits > 1 && cudaMemsetAsync(out, 0, (size_t)n * rows * sizeof(float), stream) != cudaSuccess)
     return kErrLaunch;
   const int grid = a.units < slots ? a.units : slots;
-  nvfp4_gemm_tc_kernel<<<grid, kTcThreads, kTcSmem, stream>>>(a);
+  kern<<<grid, kTcThreads, smem, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+}  // namespace
+
+int launch_nvfp4_gemm_tc(const uint8_t* codes, const uint8_t* scales, float g, const float* x,
+                         float* out, int rows, int cols, int n, cudaStream_t stream) {
+  if (n < 1 || n > kTcN) return kErrShape;
+  return launch_tc<kTcNvfp4>(codes, scales, g, x, out, rows, cols, n, stream);
+}
+
+int launch_bf16_gemm_tc(const uint16_t* W, const float* x, float* out, int rows, int cols, int n,
+                        cudaStream_t stream) {
+  if (n < 1 || n > 8) return kErrShape;
+  return launch_tc<kTcBf16>(reinterpret_cast<const uint8_t*>(W), nullptr, 1.0f, x, out, rows, cols, n,
+                            stream);
 }
 
 }  // namespace ervf

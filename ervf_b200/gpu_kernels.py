@@ -32,6 +32,15 @@ class GPUKernels:
         reference's gemv_bf16."""
         self.mv_bf16_batched(out, W, x, rows, cols, 1)
 
+    def mm_bf16_tc(self, out, W, x, rows: int, cols: int, batch: int) -> None:
+        """out[b*rows + r] for x[b*cols + k], b < batch <= 8, on the tensor
+        cores (tolerance path: rel-L2 <= 1e-3, not gemv_bf16's chain order)."""
+        _need(out, batch * rows, "out")
+        _need(W, rows * cols, "W")
+        _need(x, batch * cols, "x")
+        _lib.call("ervf_bf16_gemm_tc", ptr(W), ptr(x), ptr(out), int(rows), int(cols), int(batch),
+                  self._s())
+
     def mv_bf16_batched(self, out, W, x, rows: int, cols: int, batch: int) -> None:
         """out[b*rows + r] for x[b*cols + k], b < batch <= 8."""
         _need(out, batch * rows, "out")

@@ -251,6 +251,15 @@ ERVF_API int ervf_nvfp4_gemm_tc(const uint8_t* codes, const uint8_t* scales, flo
                                 const float* x, float* out, int rows, int cols, int n,
                                 void* stream);
 
+/* Batched BF16 GEMM on the tensor cores for the dense projections:
+ * out[b*rows + r] = sum_k W[r][k] * x[b*cols + k] for b < batch <= 8, fp32
+ * accumulate; x is split into bf16 high and low halves (16 MMA columns), so
+ * the result is held to rel-L2 <= 1e-3, not to gemv_bf16's chain order (the
+ * reference has no batched BF16 kernel; ervf_bf16_gemv keeps that order).
+ * cols % 32 == 0; W and x 16-byte aligned. */
+ERVF_API int ervf_bf16_gemm_tc(const uint16_t* W, const float* x, float* out, int rows, int cols,
+                               int batch, void* stream);
+
 /* Softmax top-k routing of `layers` logit rows f32[layers][n] (config 2,
  * Qwen shape; the reference's router is sigmoid only): per layer the top_k
  * largest logits in descending order (ties to the lowest index), ids[l][s]

@@ -62,3 +62,23 @@ def test_gemm_tc_rejects_bad_batch(fused, cuda):
     with pytest.raises(ValueError):
         fused.gemm_tc(torch.zeros(17 * 128, device=cuda), _t(codes, cuda), _t(scales, cuda),
                       torch.zeros(17 * 256, device=cuda), g, 128, 256, 17)
+
+
+@pytest.mark.parametrize("rows,cols,batch", [(4096, 2688, 8), (2688, 4096, 8), (300, 1856, 3),
+                                             (4096, 2688, 1)])
+def test_bf16_gemm_tc_matches_fp32(cuda, rows, cols, batch):
+    """Config 3 at batch 8 on the tensor cores: rel-L2 against the fp32 matmul."""
+    from ervf_b200 import GPUKernels
+
+    r = np.random.default_rng(rows + batch)
+    Wf = r.standard_normal((rows, cols)).astype(np.float32) * 0.02
+    W = (Wf.view(np.uint32) >> 16).astype(np.uint16)
+    x = r.standard_normal(batch * cols).astype(np.float32)
+    out = torch.full((batch * rows,), float("nan"), device=cuda)
+    GPUKernels().mm_bf16_tc(out, _t(W, cuda), _t(x, cuda), rows, cols, batch)
+    torch.cuda.synchronize()
+    Wb = (W.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    ref = x.reshape(batch, cols).astype(np.float64) @ Wb.T
+    got = out.cpu().numpy().reshape(batch, rows)
+    assert rel_l2(got, ref) <= 1e-3
+    assert rel_l2(got, ref) <= 2e-5  # bf16 weights exact, x to ~16 bits, fp32 accumulation
