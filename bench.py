@@ -330,6 +330,31 @@ def bf16_gemvs(device, hbm):
     return res
 
 
+def batched_decode(dec, device, hbm, tokens=32, steps=20):
+    """Config 4 at batch 32: a decode batch through all layers, expert-major on
+    the tensor cores (each routed expert read once per layer for all its
+    tokens), CUDA graph of the whole step, device time.  Bytes per step: the
+    distinct (layer, expert) records the routing touches plus activations."""
+    L, E = dec.bank.n_layers, dec.bank.n_experts
+    g = torch.Generator(device=device)
+    g.manual_seed(7)
+    xb = torch.randn(tokens, HIDDEN, generator=g, device=device)
+    rb = torch.randn(L, tokens, E, generator=g, device=device)
+    dec.step_batch(xb, rb)
+    torch.cuda.synchronize(device)
+    ids = dec.bids.view(L, tokens, TOP_K)
+    distinct = sum(int(torch.unique(ids[l]).numel()) for l in range(L))
+    rec = 2 * (INTER * HIDDEN // 2 + INTER * HIDDEN // 16)
+    step_bytes = distinct * rec + L * tokens * TOP_K * (HIDDEN + INTER) * 4
+    ms = time_graph(lambda i: dec.step_batch(xb, rb), steps, device)
+    return {"tokens_per_step": tokens, "ms_per_step": round(ms, 4),
+            "tok_s": round(tokens / (ms * 1e-3), 1),
+            "distinct_experts_per_layer": round(distinct / L, 1),
+            "step_bytes": step_bytes, "gbs": round(step_bytes / ms / 1e6, 1),
+            "frac": round(step_bytes / ms / 1e6 / hbm, 4),
+            "path": "expert-major tcgen05 (tolerance), route-order sum"}
+
+
 def cpu_sample(bank, layers_sampled=2, tokens=2):
     """Reference-path CPU baseline on a bounded sample: `tokens` tokens x
     `layers_sampled` layers of the same workload, torch FP32 dequant + matmul
@@ -535,6 +560,7 @@ def main():
 
     kern = kernel_roofline(dec, bank, device, hbm) if world == 1 else None
     gemv0 = gemv_shape(device, hbm) if (world == 1 and rank == 0) else None
+    batch32 = batched_decode(dec, device, hbm) if (world == 1 and rank == 0) else None
     extra = None
     if world == 1 and rank == 0:
         # config 2 (Qwen shapes) GEMVs and config 3 BF16 GEMVs, L2-cold
@@ -581,6 +607,8 @@ def main():
             line["gemv_config0"] = gemv0
         if extra is not None:
             line.update(extra)
+        if batch32 is not None:
+            line["batched_decode_b32"] = batch32
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_sample(bank)
         print(json.dumps(line), flush=True)

@@ -58,6 +58,9 @@ SIGNATURES: dict[str, list] = {
     "ervf_decode_scratch_bytes": [_i, _i],
     "ervf_moe_down_routesum_static": [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp,
                                       _i, _i, _i, _i, _vp],
+    "ervf_moe_batched": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _i, _i, _vp, _vp,
+                         _i, _i, _vp, _sz, _vp],
+    "ervf_moe_batched_scratch_bytes": [_i, _i, _i, _i],
     "ervf_bf16_gemm_tc": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "ervf_nvfp4_gemm_tc": [_vp, _vp, _f, _vp, _vp, _i, _i, _i, _vp],
     "ervf_route_topk_softmax": [_vp, _vp, _vp, _i, _i, _i, _vp],
@@ -74,7 +77,8 @@ SIGNATURES: dict[str, list] = {
     "ervf_cache_fetch": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _i, _vp],
 }
 
-SIZE_RESULT = {"ervf_routesum_scratch_bytes", "ervf_decode_scratch_bytes"}
+SIZE_RESULT = {"ervf_routesum_scratch_bytes", "ervf_decode_scratch_bytes",
+               "ervf_moe_batched_scratch_bytes"}
 
 _lib = None
 

@@ -475,6 +475,92 @@ int launch_route_topk_softmax(const float* rlog, int* ids, float* w, int layers,
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
+// Expert-major lists of a decode batch (one CTA): the P = T * k route pairs
+// (token t, slot s) at p = t*k + s, sorted by expert and, inside an expert,
+// by p (deterministic).  pos[p] = sorted position, tok_sorted[q] = token of
+// the pair at sorted position q; chunks of <= 16 pairs of one expert:
+// chunk_expert / chunk_off / chunk_n, n_chunks.  An id outside [0, E) is
+// recorded in the device error word and counted as expert 0.
+__global__ void moe_batch_lists_kernel(const int* __restrict__ ids, int P, int k, int E,
+                                       int* chunk_expert, int* chunk_off, int* chunk_n,
+                                       int* n_chunks, int* tok_sorted, int* pos) {
+  __shared__ int cnt[kMaxBatchExperts];
+  __shared__ int off[kMaxBatchExperts];
+  __shared__ int choff[kMaxBatchExperts];
+  const int tid = threadIdx.x;
+  for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int q = tid; q < P; q += blockDim.x) {
+    int e = ids[q];
+    if (e < 0 || e >= E) {
+      atomicExch(&g_device_error, kErrArg);
+      e = 0;
+    }
+    atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int o = 0, c = 0;
+    for (int e = 0; e < E; ++e) {
+      off[e] = o;
+      choff[e] = c;
+      o += cnt[e];
+      c += (cnt[e] + 15) / 16;
+    }
+    *n_chunks = c;
+  }
+  __syncthreads();
+  for (int q = tid; q < P; q += blockDim.x) {
+    int e = ids[q];
+    if (e < 0 || e >= E) e = 0;
+    int rank = 0;
+    for (int r = 0; r < q; ++r) {
+      int f = ids[r];
+      if (f < 0 || f >= E) f = 0;
+      rank += f == e;
+    }
+    const int sp = off[e] + rank;
+    pos[q] = sp;
+    tok_sorted[sp] = q / k;
+  }
+  for (int e = tid; e < E; e += blockDim.x) {
+    const int nc = (cnt[e] + 15) / 16;
+    for (int c = 0; c < nc; ++c) {
+      chunk_expert[choff[e] + c] = e;
+      chunk_off[choff[e] + c] = off[e] + 16 * c;
+      chunk_n[choff[e] + c] = min(16, cnt[e] - 16 * c);
+    }
+  }
+}
+
+// out[t][r] = x[t][r] + acc, acc = fmaf(contrib[pos[t*k+s]][r], w[t*k+s], acc)
+// over the route slots s = 0..k-1 in order from 0.0 (route-order contract).
+__global__ void moe_batch_routesum_kernel(const float* __restrict__ contrib, const int* __restrict__ pos,
+                                          const float* __restrict__ w, const float* __restrict__ x,
+                                          float* __restrict__ out, int hidden, int k) {
+  const int t = blockIdx.y;
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= hidden) return;
+  float acc = 0.0f;
+  for (int s = 0; s < k; ++s)
+    acc = fmaf(__ldcg(&contrib[(size_t)pos[t * k + s] * hidden + r]), w[t * k + s], acc);
+  out[(size_t)t * hidden + r] = (x ? x[(size_t)t * hidden + r] : 0.0f) + acc;
+}
+
+int launch_moe_batch_lists(const int* ids, int P, int k, int E, int* chunk_expert, int* chunk_off,
+                           int* chunk_n, int* n_chunks, int* tok_sorted, int* pos, cudaStream_t stream) {
+  moe_batch_lists_kernel<<<1, 512, 0, stream>>>(ids, P, k, E, chunk_expert, chunk_off, chunk_n, n_chunks,
+                                               tok_sorted, pos);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int launch_moe_batch_routesum(const float* contrib, const int* pos, const float* w, const float* x,
+                              float* out, int T, int hidden, int k, cudaStream_t stream) {
+  moe_batch_routesum_kernel<<<dim3((hidden + 255) / 256, T), 256, 0, stream>>>(contrib, pos, w, x, out,
+                                                                               hidden, k);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
 int launch_route_topk_batched(const float* rlog, const float* gate_b, int* ids, float* w, int layers,
                               int n, int top_k, float scaling, int bad_pick, int bias_stride,
                               cudaStream_t stream) {

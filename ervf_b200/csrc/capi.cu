@@ -400,6 +400,94 @@ int ervf_bf16_gemm_tc(const uint16_t* W, const float* x, float* out, int rows, i
   return launch_bf16_gemm_tc(W, x, out, rows, cols, batch, S(stream));
 }
 
+namespace {
+struct BatchScratch {
+  int *chunk_expert, *chunk_off, *chunk_n, *n_chunks, *tok_sorted, *pos;
+  float *act, *contrib;
+  size_t bytes;
+};
+BatchScratch batch_scratch(void* base, int pairs, int hidden, int inter) {
+  BatchScratch b{};
+  uint8_t* p = reinterpret_cast<uint8_t*>(base);
+  const size_t ints = ((size_t)5 * pairs + 4 + 3) / 4 * 4;
+  int* ip = reinterpret_cast<int*>(p);
+  b.chunk_expert = ip;
+  b.chunk_off = ip + pairs;
+  b.chunk_n = ip + 2 * (size_t)pairs;
+  b.tok_sorted = ip + 3 * (size_t)pairs;
+  b.pos = ip + 4 * (size_t)pairs;
+  b.n_chunks = ip + 5 * (size_t)pairs;
+  b.act = reinterpret_cast<float*>(p + ints * 4);
+  b.contrib = b.act + (size_t)pairs * inter;
+  b.bytes = ints * 4 + (size_t)pairs * (inter + hidden) * 4;
+  return b;
+}
+}  // namespace
+
+size_t ervf_moe_batched_scratch_bytes(int tokens, int top_k, int hidden, int inter) {
+  if (tokens <= 0 || top_k <= 0 || hidden <= 0 || inter <= 0) return 0;
+  return batch_scratch(nullptr, tokens * top_k, hidden, inter).bytes;
+}
+
+int ervf_moe_batched(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
+                     size_t up_scale_stride, const uint8_t* dn_codes, const uint8_t* dn_scales,
+                     size_t dn_code_stride, size_t dn_scale_stride, const float* globals,
+                     const int32_t* ids, const float* route_w, int tokens, int top_k, int n_experts,
+                     const float* x, float* out, int hidden, int inter, void* scratch,
+                     size_t scratch_bytes, void* stream) {
+  if (!up_codes || !up_scales || !dn_codes || !dn_scales || !globals || !ids || !route_w || !x ||
+      !out || !scratch)
+    return kErrNull;
+  const int pairs = tokens * top_k;
+  if (tokens <= 0 || top_k <= 0 || top_k > kMaxJobs || pairs > 4096 || n_experts <= 0 ||
+      n_experts > kMaxBatchExperts)
+    return kErrShape;
+  if (hidden <= 0 || inter <= 0 || hidden % 32 || inter % 32) return kErrShape;
+  const BatchScratch b = batch_scratch(scratch, pairs, hidden, inter);
+  if (scratch_bytes < b.bytes) return kErrArg;
+  if (!al(up_codes, 16) || !al(dn_codes, 16) || !al(up_scales, 2) || !al(dn_scales, 2) || !al(x, 16) ||
+      !al(scratch, 16) || ((up_code_stride | dn_code_stride) & 15u) || ((up_scale_stride | dn_scale_stride) & 1u))
+    return kErrAlign;
+  cudaStream_t st = S(stream);
+  if (int e = launch_moe_batch_lists(ids, pairs, top_k, n_experts, b.chunk_expert, b.chunk_off, b.chunk_n,
+                                     b.n_chunks, b.tok_sorted, b.pos, st))
+    return e;
+  GroupedTc g{};
+  g.chunk_expert = b.chunk_expert;
+  g.chunk_off = b.chunk_off;
+  g.chunk_n = b.chunk_n;
+  g.n_chunks = b.n_chunks;
+  g.max_chunks = pairs;
+  g.globals = globals;
+  // up: act[q] = relu(g_up * W_up x_token(q))^2 for sorted pair q
+  g.codes = up_codes;
+  g.scales = up_scales;
+  g.code_stride = up_code_stride;
+  g.scale_stride = up_scale_stride;
+  g.gsel = 1;
+  g.x = x;
+  g.b_idx = b.tok_sorted;
+  g.out = b.act;
+  g.rows = inter;
+  g.cols = hidden;
+  g.relu2 = 1;
+  if (int e = launch_grouped_tc(g, st)) return e;
+  // down: contrib[q] = g_down * W_down act[q]
+  g.codes = dn_codes;
+  g.scales = dn_scales;
+  g.code_stride = dn_code_stride;
+  g.scale_stride = dn_scale_stride;
+  g.gsel = 0;
+  g.x = b.act;
+  g.b_idx = nullptr;
+  g.out = b.contrib;
+  g.rows = hidden;
+  g.cols = inter;
+  g.relu2 = 0;
+  if (int e = launch_grouped_tc(g, st)) return e;
+  return launch_moe_batch_routesum(b.contrib, b.pos, route_w, x, out, tokens, hidden, top_k, st);
+}
+
 int ervf_cache_assign(int32_t* slot_of, int32_t* expert_of, int32_t* last_used, int32_t* state2,
                       const int32_t* ids, int32_t* slots, int32_t* need, int32_t* stats2, int cap,
                       int top_k, void* stream) {

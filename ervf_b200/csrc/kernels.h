@@ -121,6 +121,27 @@ bool nvfp4_tma_ok(const GemvBatch& b);
 int launch_nvfp4_gemm_tc(const uint8_t* codes, const uint8_t* scales, float g, const float* x,
                          float* out, int rows, int cols, int n, cudaStream_t stream);
 
+// Expert-major grouped NVFP4 GEMM on the tensor cores (batched MoE block):
+// see TcArgs in nvfp4_gemm_tc.cu.
+struct GroupedTc {
+  const uint8_t* codes;   // expert bank base (expert e at e * code_stride)
+  const uint8_t* scales;
+  size_t code_stride, scale_stride;
+  const float* globals;   // [E][2]
+  int gsel;               // 1: up (g_up), 0: down (g_down)
+  const float* x;         // source rows
+  const int* b_idx;       // gather index per sorted pair (NULL: identity)
+  float* out;             // [pairs][rows]
+  int rows, cols;
+  const int* chunk_expert;
+  const int* chunk_off;
+  const int* chunk_n;
+  const int* n_chunks;
+  int max_chunks;
+  int relu2;
+};
+int launch_grouped_tc(const GroupedTc& g, cudaStream_t stream);
+
 // Batched BF16 GEMM on the tensor cores: out[n][r] = (W @ X[n])[r] for
 // n < N <= 8 (X split into bf16 high / low halves), fp32 accumulate.
 int launch_bf16_gemm_tc(const uint16_t* W, const float* x, float* out, int rows, int cols, int n,

@@ -51,7 +51,7 @@ constexpr int kTcRawDepthBf = 4;
 constexpr int kTcRawStageBf = kTcM * kTcKB * 2;         // 16 KB
 constexpr int kTcSmemBf = 1024 + 2 * kTcBStage + kTcRawDepthBf * kTcRawStageBf;
 
-enum TcMode { kTcNvfp4 = 0, kTcBf16 = 1 };
+enum TcMode { kTcNvfp4 = 0, kTcBf16 = 1, kTcGrouped = 2 };
 constexpr int kTcTmemCols = 128;     // D: columns 0..15; A stages: 32..63, 64..95
 constexpr int kTcACol = 32;
 constexpr int kTcAStageCols = kTcKB / 2;  // two f16 per 32-bit column
@@ -65,6 +65,20 @@ struct TcArgs {
   int rows, cols, n;
   int splits;             // K-splits per row tile (atomic accumulation when > 1)
   int units;              // row tiles * splits
+  // kTcGrouped (expert-major batched MoE): unit = (chunk, row tile); chunk c
+  // is expert chunk_expert[c] with the n = chunk_n[c] <= 16 route pairs
+  // chunk_off[c] .. +n of the expert-sorted pair list.  B column j gathers X
+  // row b_idx[chunk_off + j] (b_idx NULL: row chunk_off + j); output row of
+  // pair p is out[p * rows + r].  Weights: codes + e*code_stride, global scale
+  // globals[e*2 + gsel]; relu2 squares the positive part.
+  const int* chunk_expert;
+  const int* chunk_off;
+  const int* chunk_n;
+  const int* n_chunks;
+  const int* b_idx;
+  size_t code_stride, scale_stride;
+  const float* globals;
+  int gsel, relu2, tiles;
 };
 
 // UMMA shared-memory descriptor, K-major, no swizzle (sm100 version 1).
@@ -185,13 +199,32 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
   uint32_t nacc = 0;  // accumulator commits waited for
 
   for (int unit = blockIdx.x; unit < a.units; unit += gridDim.x) {
-    const int tile = unit / a.splits, split = unit - tile * a.splits;
+    int tile, split, un, uoff = 0;
+    const uint8_t* ucodes = a.codes;
+    const uint8_t* uscales = a.scales;
+    float ug = a.g;
+    if constexpr (MODE == kTcGrouped) {
+      const int chunk = unit / a.tiles;
+      if (chunk >= __ldg(a.n_chunks)) continue;  // uniform over the CTA
+      tile = unit - chunk * a.tiles;
+      split = 0;
+      const int e = __ldg(&a.chunk_expert[chunk]);
+      un = __ldg(&a.chunk_n[chunk]);
+      uoff = __ldg(&a.chunk_off[chunk]);
+      ucodes = a.codes + (size_t)e * a.code_stride;
+      uscales = a.scales + (size_t)e * a.scale_stride;
+      ug = __ldg(&a.globals[e * 2 + a.gsel]);
+    } else {
+      tile = unit / a.splits;
+      split = unit - tile * a.splits;
+      un = a.n;
+    }
     const int kb0 = (int)((long long)split * nkb / a.splits);
     const int kb1 = (int)((long long)(split + 1) * nkb / a.splits);
     const int row = tile * kTcM + rr;
     const bool row_ok = row < a.rows;
-    const uint8_t* crow = a.codes + (size_t)row * cb;
-    const uint8_t* srow = a.scales + (size_t)row * sb;
+    const uint8_t* crow = ucodes + (size_t)row * cb;
+    const uint8_t* srow = uscales + (size_t)row * sb;
 
     // This thread's code unit of k-block kb goes, by cp.async, to raw ring
     // slot kb % depth (the thread that copies a unit decodes it: no barrier);
@@ -227,9 +260,13 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
     auto load_x = [&](int kb, float4 (&v)[2]) {
       const int k = kb * kTcKB + bc * 8;
       const int xn = MODE == kTcBf16 ? (bn & 7) : bn;  // kTcBf16: rows n and n + 8 share X[n]
-      if (tid < 128 && xn < a.n && k < a.cols) {
-        v[0] = __ldg(reinterpret_cast<const float4*>(a.x + (size_t)xn * a.cols + k));
-        v[1] = __ldg(reinterpret_cast<const float4*>(a.x + (size_t)xn * a.cols + k + 4));
+      if (tid < 128 && xn < un && k < a.cols) {
+        size_t src = (size_t)xn;
+        if constexpr (MODE == kTcGrouped)
+          src = a.b_idx ? (size_t)__ldg(&a.b_idx[uoff + xn]) : (size_t)(uoff + xn);
+        // activations may come from the previous launch: read through L2
+        v[0] = __ldcg(reinterpret_cast<const float4*>(a.x + src * a.cols + k));
+        v[1] = __ldcg(reinterpret_cast<const float4*>(a.x + src * a.cols + k + 4));
       } else {
         v[0] = v[1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
@@ -335,10 +372,14 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
       if (!dead && orow < a.rows) {
 #pragma unroll
         for (int j = 0; j < kTcN; ++j) {
-          if (j < a.n) {
-            const float y = MODE == kTcBf16 ? (j < 8 ? __uint_as_float(v[j]) + __uint_as_float(v[j + 8]) : 0.0f)
-                                            : __uint_as_float(v[j]) * a.g;
-            float* o = a.out + (size_t)j * a.rows + orow;
+          if (j < un) {
+            float y = MODE == kTcBf16 ? (j < 8 ? __uint_as_float(v[j]) + __uint_as_float(v[j + 8]) : 0.0f)
+                                      : __uint_as_float(v[j]) * ug;
+            if (MODE == kTcGrouped && a.relu2) {
+              const float r = fmaxf(y, 0.0f);
+              y = r * r;
+            }
+            float* o = a.out + (size_t)(uoff + j) * a.rows + orow;
             if (a.splits > 1) {
               atomicAdd(o, y);
             } else {
@@ -407,6 +448,43 @@ int launch_nvfp4_gemm_tc(const uint8_t* codes, const uint8_t* scales, float g, c
                          float* out, int rows, int cols, int n, cudaStream_t stream) {
   if (n < 1 || n > kTcN) return kErrShape;
   return launch_tc<kTcNvfp4>(codes, scales, g, x, out, rows, cols, n, stream);
+}
+
+int launch_grouped_tc(const GroupedTc& g, cudaStream_t stream) {
+  constexpr int smem = kTcSmem;
+  auto kern = nvfp4_gemm_tc_kernel<kTcGrouped>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return kErrLaunch;
+  int smem_sm = 0;
+  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, 0);
+  int per_sm = smem_sm / (smem + 1024);
+  if (per_sm > 512 / kTcTmemCols) per_sm = 512 / kTcTmemCols;
+  if (per_sm < 1) return kErrShape;
+  TcArgs a{};
+  a.codes = g.codes;
+  a.scales = g.scales;
+  a.x = g.x;
+  a.out = g.out;
+  a.rows = g.rows;
+  a.cols = g.cols;
+  a.n = 16;
+  a.splits = 1;
+  a.tiles = (g.rows + kTcM - 1) / kTcM;
+  a.units = g.max_chunks * a.tiles;
+  a.chunk_expert = g.chunk_expert;
+  a.chunk_off = g.chunk_off;
+  a.chunk_n = g.chunk_n;
+  a.n_chunks = g.n_chunks;
+  a.b_idx = g.b_idx;
+  a.code_stride = g.code_stride;
+  a.scale_stride = g.scale_stride;
+  a.globals = g.globals;
+  a.gsel = g.gsel;
+  a.relu2 = g.relu2;
+  const int slots = device_sm_count() * per_sm;
+  const int grid = a.units < slots ? a.units : slots;
+  kern<<<grid, kTcThreads, smem, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
 int launch_bf16_gemm_tc(const uint16_t* W, const float* x, float* out, int rows, int cols, int n,

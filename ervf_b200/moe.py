@@ -184,6 +184,30 @@ class MoEDecoder:
         _lib.call("ervf_ep_route_sum", ptr(self.gathered), ptr(ids), ptr(w), k, ptr(x), ptr(out),
                   b.hidden, self.ep_ranks, self._s())
 
+    def step_batch(self, x_in: torch.Tensor, rlogs: torch.Tensor) -> torch.Tensor:
+        """A decode batch of T tokens through every layer, expert-major on the
+        tensor cores (tolerance path).  x_in f32[T][hidden], rlogs
+        f32[L][T][E].  Returns the buffer holding x after the last layer."""
+        b, k = self.bank, self.top_k
+        L, T = b.n_layers, x_in.shape[0]
+        d = b.device
+        if getattr(self, "_bt", None) != T:
+            self._bt = T
+            self.bids = torch.zeros(L * T, k, dtype=torch.int32, device=d)
+            self.bw = torch.zeros(L * T, k, dtype=torch.float32, device=d)
+            self.bx = torch.zeros(2, T, b.hidden, dtype=torch.float32, device=d)
+        self.fused.route_topk_batched(rlogs, None, self.bids, self.bw, L * T, b.n_experts, k,
+                                      self.scaling)
+        cur = x_in
+        for l in range(L):
+            nxt = self.bx[l & 1]
+            self.fused.moe_batched(b.up_codes[l], b.up_scales[l], b.up_code_bytes, b.up_scale_bytes,
+                                   b.dn_codes[l], b.dn_scales[l], b.dn_code_bytes, b.dn_scale_bytes,
+                                   b.globals[l], self.bids[l * T:(l + 1) * T], self.bw[l * T:(l + 1) * T],
+                                   T, k, b.n_experts, cur, nxt, b.hidden, b.inter)
+            cur = nxt
+        return cur
+
     def step(self, x_in: torch.Tensor, rlogs: torch.Tensor) -> torch.Tensor:
         """One decode token through all layers; rlogs f32[L][E] are the
         router logits of every layer.  Returns the buffer holding x after

@@ -260,6 +260,27 @@ ERVF_API int ervf_nvfp4_gemm_tc(const uint8_t* codes, const uint8_t* scales, flo
 ERVF_API int ervf_bf16_gemm_tc(const uint16_t* W, const float* x, float* out, int rows, int cols,
                                int batch, void* stream);
 
+/* Expert-major batched routed-MoE block of a decode batch on the tensor cores
+ * (the reference's SweepMoE block, sweepspec.py:244-375): tokens x[t] (f32
+ * [tokens][hidden]) routed to ids[t*top_k + s] with weights route_w[...]:
+ * every expert is read once for all the tokens routed to it (chunks of <= 16
+ * tokens as the MMA's N columns), act = relu(up(x))^2, contrib = down(act),
+ * then out[t] = x[t] + acc, acc = fmaf(contrib[t,s], w[t,s], acc) over s in
+ * route order.  Four launches (lists, up, down, route sum).  Tolerance path
+ * (rel-L2 <= 1e-3; weights exact in f16, x and act rounded to f16).  Bank as
+ * in ervf_moe_up_grouped / ervf_moe_down_routesum; tokens*top_k <= 4096,
+ * n_experts <= 1024; scratch: ervf_moe_batched_scratch_bytes(...) bytes. */
+ERVF_API int ervf_moe_batched(const uint8_t* up_codes, const uint8_t* up_scales,
+                              size_t up_code_stride, size_t up_scale_stride,
+                              const uint8_t* dn_codes, const uint8_t* dn_scales,
+                              size_t dn_code_stride, size_t dn_scale_stride, const float* globals,
+                              const int32_t* ids, const float* route_w, int tokens, int top_k,
+                              int n_experts, const float* x, float* out, int hidden, int inter,
+                              void* scratch, size_t scratch_bytes, void* stream);
+
+/* Bytes of scratch ervf_moe_batched uses. */
+ERVF_API size_t ervf_moe_batched_scratch_bytes(int tokens, int top_k, int hidden, int inter);
+
 /* Softmax top-k routing of `layers` logit rows f32[layers][n] (config 2,
  * Qwen shape; the reference's router is sigmoid only): per layer the top_k
  * largest logits in descending order (ties to the lowest index), ids[l][s]
