@@ -7,8 +7,10 @@ relu^2, down 2688x1856), all HBM-resident (17.24 GB), sigmoid top-6 routing
 from random logits per layer and token, x_{L+1} = x_L + moe_L(x_L) in fp32.
 A "step" is one token through all 24 layers.  Weights are seeded synthetic
 (N(0, 0.02) quantised to NVFP4 on the device): the real checkpoint is not
-available.  With --gpus N the experts are sharded by id (e % N) and the
-per-slot outputs are all-gathered over NCCL before the route-order sum.
+available.  With --gpus N the experts are sharded by id (e % N); per layer
+one exchange kernel reads every route slot's output from its owner's memory
+over NVLink and adds the slots in route order (--exchange nccl: an NCCL
+all-gather and a route-sum launch instead).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -45,6 +47,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="expert-parallel exchange of the slot outputs (N > 1)")
     ap.add_argument("--gemv", type=int, nargs=2, metavar=("ROWS", "COLS"),
                     help="time one NVFP4 GEMV shape instead of the decode step")
     ap.add_argument("--gemm-tc", type=int, nargs=3, metavar=("ROWS", "COLS", "N"),
@@ -475,7 +479,8 @@ def main():
         import torch.distributed as dist
 
         group = dist.group.WORLD
-    dec = MoEDecoder(bank, TOP_K, ep_ranks=world, ep_rank=rank, group=group)
+    dec = MoEDecoder(bank, TOP_K, ep_ranks=world, ep_rank=rank, group=group,
+                     exchange=args.exchange)
 
     T = args.warmup + args.steps
     g = torch.Generator(device=device)
@@ -486,7 +491,7 @@ def main():
     x_buf = torch.zeros(HIDDEN, device=device)
     r_buf = torch.zeros(L, N_EXPERTS, device=device)
 
-    # the whole token (NCCL all-gathers included when world > 1) is one graph
+    # the whole token (the exchanges included when world > 1) is one graph
     use_graph = not args.no_graph
     graph = None
     if use_graph:
@@ -582,9 +587,12 @@ def main():
             "config": {"workload": f"config4: {L} MoE layers x {N_EXPERTS} NVFP4 experts "
                                    f"(hidden {HIDDEN}, inter {INTER}), top-{TOP_K} sigmoid, batch 1",
                        "global_batch": 1, "parallelism": f"ep{world}",
+                       "exchange": args.exchange if world > 1 else None,
                        "l2": "inputs larger than L2 (17.2 GB bank, 808 MB streamed per token)",
                        "cuda_graph": graph is not None},
-            "gpu_launches": 3 * L * args.steps if world == 1 else 4 * L * args.steps,
+            # router + per layer: up, down(+route sum) on one GPU; up, down,
+            # exchange(+route sum) or route sum after the all-gather with N > 1
+            "gpu_launches": (2 * L + 1 if world == 1 else 3 * L + 1) * args.steps,
             "token_bytes": token_bytes,
             "token_roofline_frac": (token_bytes / (ms / args.steps / 1e3) / 1e9) / (hbm * world),
             "clocks": clocks,
@@ -617,6 +625,8 @@ def main():
     if world > 1:
         import torch.distributed as dist
 
+        torch.cuda.synchronize(device)
+        dec.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -19,6 +19,7 @@ ERR_ALIGN = -3
 ERR_LAUNCH = -4
 ERR_TIMEOUT = -5
 ERR_ARG = -6
+ERR_DEVICE = -7
 ERR_SCRATCH_LIMIT = -8
 
 LAUNCH_PDL = 1
@@ -32,6 +33,7 @@ _NAMES = {
     ERR_LAUNCH: "CUDA launch failed",
     ERR_TIMEOUT: "device wait timed out",
     ERR_ARG: "invalid argument",
+    ERR_DEVICE: "CUDA set-up call failed",
     ERR_SCRATCH_LIMIT: "larger than the fixed scratch array (hidden <= 8192, top_k <= 8)",
 }
 
@@ -68,6 +70,14 @@ SIGNATURES: dict[str, list] = {
     "ervf_ep_expert_slots": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _i, _vp, _vp, _vp,
                              _i, _i, _i, _i, _i, _vp],
     "ervf_ep_route_sum": [_vp, _vp, _vp, _i, _vp, _vp, _i, _i, _vp],
+    "ervf_ep_expert_slots_ex": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _i, _vp, _vp,
+                                _vp, _i, _i, _i, _i, _i, _i, _vp],
+    "ervf_ep_region_bytes": [_i, _i],
+    "ervf_ep_region_alloc": [_sz, _vp, _vp],
+    "ervf_ep_region_open": [_vp, _vp],
+    "ervf_ep_region_close": [_vp],
+    "ervf_ep_region_free": [_vp],
+    "ervf_ep_exchange_route_sum": [_vp, _i, _i, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _vp],
     "ervf_down_masked": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _vp],
     "ervf_down_masked_ind": [_vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp],
     "ervf_panel_major": [_vp, _vp, _vp, _i, _i, _vp],
@@ -78,7 +88,7 @@ SIGNATURES: dict[str, list] = {
 }
 
 SIZE_RESULT = {"ervf_routesum_scratch_bytes", "ervf_decode_scratch_bytes",
-               "ervf_moe_batched_scratch_bytes"}
+               "ervf_moe_batched_scratch_bytes", "ervf_ep_region_bytes"}
 
 _lib = None
 

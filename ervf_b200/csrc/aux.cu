@@ -621,4 +621,6 @@ int launch_panel_major(const uint8_t* codes, const uint8_t* scales, uint8_t* blo
   return launched();
 }
 
+int read_aux_device_error(bool clear) { return read_unit_error(clear); }
+
 }  // namespace ervf

@@ -4,6 +4,7 @@
 #include "../../include/ervf_b200.h"
 
 #include <atomic>
+#include <cstring>
 
 #include "aux.h"
 #include "common.cuh"
@@ -42,7 +43,14 @@ extern "C" {
 
 int ervf_version(void) { return 100; }
 
-int ervf_device_status(void) { return read_device_error(true); }
+int ervf_device_status(void) {
+  // read and clear every unit's word; report the first error found
+  const int v[4] = {read_gemv_device_error(true), read_aux_device_error(true),
+                    read_tc_device_error(true), read_ep_device_error(true)};
+  for (int e : v)
+    if (e) return e;
+  return kOk;
+}
 
 int ervf_nvfp4_gemv(const uint8_t* codes, const uint8_t* scales, const float* x, float* out,
                     float global_scale, int rows, int cols, int apply_relu2, float out_scale,
@@ -265,6 +273,18 @@ int ervf_ep_expert_slots(const uint8_t* up_codes, const uint8_t* up_scales, size
                          const float* globals, int top_k, const float* x, float* act,
                          float* contrib, int hidden, int inter, int ep_ranks, int ep_rank,
                          int width, void* stream) {
+  return ervf_ep_expert_slots_ex(up_codes, up_scales, up_code_stride, up_scale_stride, dn_codes,
+                                 dn_scales, dn_code_stride, dn_scale_stride, ids, globals, top_k, x,
+                                 act, contrib, hidden, inter, ep_ranks, ep_rank, width, 0, stream);
+}
+
+int ervf_ep_expert_slots_ex(const uint8_t* up_codes, const uint8_t* up_scales,
+                            size_t up_code_stride, size_t up_scale_stride,
+                            const uint8_t* dn_codes, const uint8_t* dn_scales,
+                            size_t dn_code_stride, size_t dn_scale_stride, const int32_t* ids,
+                            const float* globals, int top_k, const float* x, float* act,
+                            float* contrib, int hidden, int inter, int ep_ranks, int ep_rank,
+                            int width, int flags, void* stream) {
   if (!up_codes || !up_scales || !dn_codes || !dn_scales || !ids || !globals || !x || !act || !contrib)
     return kErrNull;
   if (top_k <= 0 || top_k > kMaxJobs || ep_ranks < 1 || ep_rank < 0 || ep_rank >= ep_ranks)
@@ -274,9 +294,12 @@ int ervf_ep_expert_slots(const uint8_t* up_codes, const uint8_t* up_scales, size
   if (!al(up_codes, 4) || !al(dn_codes, 4) || (up_code_stride & 3) || (dn_code_stride & 3) ||
       !al(x, 4) || !al(act, 4) || !al(contrib, 4))
     return kErrAlign;
+  if (flags & ~(ERVF_LAUNCH_PDL | ERVF_LAUNCH_IDS_READY)) return kErrArg;
   GemvBatch b{};
   b.njobs = top_k;
   b.out_scale = 1.0f;
+  b.pdl = (flags & ERVF_LAUNCH_PDL) ? 1 : 0;
+  b.ids_ready = (flags & ERVF_LAUNCH_IDS_READY) ? 1 : 0;
   b.ep_ids = ids;
   b.ep_ranks = ep_ranks;
   b.ep_rank = ep_rank;
@@ -301,6 +324,7 @@ int ervf_ep_expert_slots(const uint8_t* up_codes, const uint8_t* up_scales, size
   b.rows = hidden;
   b.cols = inter;
   b.relu2 = 0;
+  if (b.pdl) b.ids_ready = 1;  // ids were complete before the up launch began
   for (int s = 0; s < top_k; ++s) {
     MatRef& m = b.job[s].mat;
     m.codes = dn_codes;
@@ -486,6 +510,86 @@ int ervf_moe_batched(const uint8_t* up_codes, const uint8_t* up_scales, size_t u
   g.relu2 = 0;
   if (int e = launch_grouped_tc(g, st)) return e;
   return launch_moe_batch_routesum(b.contrib, b.pos, route_w, x, out, tokens, hidden, top_k, st);
+}
+
+size_t ervf_ep_region_bytes(int hidden, int top_k) {
+  if (hidden <= 0 || top_k <= 0 || top_k > kMaxJobs) return 0;
+  return ep_region_bytes(hidden, top_k);
+}
+
+int ervf_ep_region_alloc(size_t bytes, void** region, void* ipc_handle) {
+  if (!region || !ipc_handle) return kErrNull;
+  if (bytes <= kEpSlotsOffset) return kErrShape;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return kErrDevice;
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+      cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    cudaFree(p);
+    return kErrDevice;
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *region = p;
+  return kOk;
+}
+
+int ervf_ep_region_open(const void* ipc_handle, void** region) {
+  if (!ipc_handle || !region) return kErrNull;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return kErrDevice;
+  }
+  *region = p;
+  return kOk;
+}
+
+int ervf_ep_region_close(void* region) {
+  if (!region) return kErrNull;
+  if (cudaIpcCloseMemHandle(region) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return kErrDevice;
+  }
+  return kOk;
+}
+
+int ervf_ep_region_free(void* region) {
+  if (!region) return kErrNull;
+  if (cudaFree(region) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return kErrDevice;
+  }
+  return kOk;
+}
+
+int ervf_ep_exchange_route_sum(const uint64_t* peers, int nranks, int rank, int buf,
+                               const int32_t* ids, const float* route_w, int top_k, const float* x,
+                               float* out, int hidden, int timeout_ms, int flags, void* stream) {
+  if (!peers || !ids || !route_w || !out) return kErrNull;
+  if (nranks < 1 || nranks > kEpMaxRanks || rank < 0 || rank >= nranks) return kErrShape;
+  if (top_k <= 0 || top_k > kMaxJobs || hidden <= 0 || hidden % 4) return kErrShape;
+  if (buf < 0 || buf >= kEpBufs || timeout_ms <= 0 || timeout_ms > 600000) return kErrArg;
+  if (flags & ~ERVF_LAUNCH_PDL) return kErrArg;
+  if (!al(peers, 8) || !al(out, 16) || (x && !al(x, 16))) return kErrAlign;
+  EpExchange a{};
+  a.peers = peers;
+  a.nranks = nranks;
+  a.rank = rank;
+  a.buf = buf;
+  a.top_k = top_k;
+  a.hidden = hidden;
+  a.ids = ids;
+  a.route_w = route_w;
+  a.x = x;
+  a.out = out;
+  a.timeout_ns = (uint64_t)timeout_ms * 1000000ull;
+  return launch_ep_exchange_sum(a, (flags & ERVF_LAUNCH_PDL) != 0, S(stream));
 }
 
 int ervf_cache_assign(int32_t* slot_of, int32_t* expert_of, int32_t* last_used, int32_t* state2,

@@ -36,8 +36,20 @@ enum : int {
 
 // Device-side error word: set by a kernel whose bounded wait ran out.  One
 // copy per translation unit; each unit that waits exports a host reader
-// (read_device_error in kernels.h), and ervf_device_status() reads them all.
+// (read_*_device_error in kernels.h), and ervf_device_status() reads them all.
 static __device__ int g_device_error;
+
+// Host reader of this unit's error word (each unit wraps it in a named
+// function declared in kernels.h).
+static inline int read_unit_error(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return kErrLaunch;
+  if (clear && v) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)) != cudaSuccess) return kErrLaunch;
+  }
+  return v;
+}
 
 // ------------------------------------------------------------- decoding
 

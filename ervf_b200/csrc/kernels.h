@@ -157,7 +157,36 @@ int launch_weighted_accumulate(float* dst, const float* src, float weight, const
 int device_sm_count();
 int device_smem_optin();
 
-// Reads (and optionally clears) the device error word set by bounded waits.
-int read_device_error(bool clear);
+// Device error words (one per translation unit: bounded waits that ran out,
+// ids out of range).  Each reader returns the unit's word and, with clear,
+// resets it.
+int read_gemv_device_error(bool clear);
+int read_aux_device_error(bool clear);
+int read_tc_device_error(bool clear);
+int read_ep_device_error(bool clear);
+
+// Expert-parallel exchange over NVLink peer memory (ep_p2p.cu).  Region
+// layout of every rank: u64 flag[kEpMaxRanks] at 0, u64 seq at 512, f32
+// slots[kEpBufs][top_k][hidden] at kEpSlotsOffset.
+constexpr int kEpMaxRanks = 64;
+constexpr int kEpBufs = 3;
+constexpr size_t kEpSlotsOffset = 1024;
+constexpr int kEpThreads = 1024;
+
+inline size_t ep_region_bytes(int hidden, int top_k) {
+  return kEpSlotsOffset + (size_t)kEpBufs * top_k * hidden * sizeof(float);
+}
+
+struct EpExchange {
+  const uint64_t* peers;  // [nranks] device: every rank's region as mapped here
+  int nranks, rank, buf, top_k, hidden;
+  const int* ids;         // [top_k]
+  const float* route_w;   // [top_k]
+  const float* x;         // [hidden] or NULL
+  float* out;             // [hidden]
+  uint64_t timeout_ns;
+};
+
+int launch_ep_exchange_sum(const EpExchange& a, bool pdl, cudaStream_t stream);
 
 }  // namespace ervf

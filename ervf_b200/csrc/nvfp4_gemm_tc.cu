@@ -494,4 +494,6 @@ int launch_bf16_gemm_tc(const uint16_t* W, const float* x, float* out, int rows,
                             stream);
 }
 
+int read_tc_device_error(bool clear) { return read_unit_error(clear); }
+
 }  // namespace ervf

@@ -963,15 +963,7 @@ bool nvfp4_tma_ok(const GemvBatch& b) { return tma_ok(b); }
 int device_sm_count() { return dev_info().sms; }
 int device_smem_optin() { return dev_info().smem_optin; }
 
-int read_device_error(bool clear) {
-  int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return kErrLaunch;
-  if (clear) {
-    const int zero = 0;
-    if (cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)) != cudaSuccess) return kErrLaunch;
-  }
-  return v;
-}
+int read_gemv_device_error(bool clear) { return read_unit_error(clear); }
 
 int launch_nvfp4_batch(const GemvBatch& b, int width, cudaStream_t stream) {
   switch (width) {

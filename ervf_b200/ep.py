@@ -28,3 +28,81 @@ def gathered_index(ids, slot: int, world: int, top_k: int, hidden: int) -> int:
 
 def experts_of_rank(n_experts: int, world: int, rank: int) -> list[int]:
     return list(range(rank, n_experts, world))
+
+
+class PeerExchange:
+    """Exchange regions of every rank, mapped over NVLink (CUDA IPC).
+
+    Each rank allocates one region (``ervf_ep_region_alloc``), the 64-byte
+    IPC handles are all-gathered over ``group``, and every peer's region is
+    mapped here (``ervf_ep_region_open``).  ``peers`` is the device table
+    u64[world] the exchange kernel reads; ``slots(buf)`` the address where
+    this rank's down launch writes the slots it owns.  Set-up only: the
+    per-layer exchange (``ervf_ep_exchange_route_sum``) is one kernel with no
+    collective call.  ``close()`` unmaps the peers, waits for every rank and
+    frees the own region.
+    """
+
+    def __init__(self, group, world: int, rank: int, hidden: int, top_k: int, device):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self.world, self.rank, self.hidden, self.top_k = world, rank, hidden, top_k
+        self.group, self.device = group, device
+        lib = _lib.load()
+        self.nbytes = int(lib.ervf_ep_region_bytes(hidden, top_k))
+        if self.nbytes == 0:
+            raise ValueError("unsupported exchange shape")
+        own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        with torch.cuda.device(device):
+            _lib.call("ervf_ep_region_alloc", self.nbytes, ctypes.byref(own), handle)
+        self.own = int(own.value)
+        mine = torch.frombuffer(bytearray(handle.raw), dtype=torch.uint8).to(device)
+        allh = torch.empty(world * 64, dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(allh, mine, group=group)
+        allh = allh.cpu().numpy().tobytes()
+        self.mapped = []
+        ptrs = []
+        with torch.cuda.device(device):
+            for q in range(world):
+                if q == rank:
+                    ptrs.append(self.own)
+                    continue
+                p = ctypes.c_void_p()
+                _lib.call("ervf_ep_region_open", allh[q * 64:(q + 1) * 64], ctypes.byref(p))
+                self.mapped.append(int(p.value))
+                ptrs.append(int(p.value))
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        # every rank has zeroed its region before anyone's first exchange
+        dist.barrier(group=group)
+
+    def slots(self, buf: int) -> int:
+        return self.own + 1024 + buf * self.top_k * self.hidden * 4
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        from . import _lib
+
+        if self.own is None:
+            return
+        for p in self.mapped:
+            _lib.call("ervf_ep_region_close", p)
+        self.mapped = []
+        dist.barrier(group=self.group)
+        _lib.call("ervf_ep_region_free", self.own)
+        self.own = None
+
+
+def exchange_buffer(layer: int, n_layers: int) -> int:
+    """Slot buffer of a layer: consecutive exchanges (the wrap from the last
+    layer of one step to layer 0 of the next included) use different
+    buffers -- alternate 0 / 1, and the last layer of an odd count takes 2."""
+    if n_layers % 2 == 1 and layer == n_layers - 1:
+        return 2
+    return layer & 1

@@ -20,9 +20,11 @@ with 1-D bulk copies.
 (route_topk), one launch for the top-k up projections with relu^2, one
 launch for the top-k down projections fused with the route-order weighted
 sum and the residual add x + moe(x).  With expert parallelism (``ep_ranks``
-> 1) each rank owns experts e with e % ep_ranks == rank, computes only its
-slots' down outputs, and the per-slot outputs are all-gathered before the
-same route-order sum -- so every rank's result is bit-identical to one GPU.
+> 1) each rank owns experts e with e % ep_ranks == rank and computes only
+its slots' down outputs; one exchange kernel per layer then reads every
+slot from its owner's memory over NVLink (or, with ``exchange="nccl"``, an
+all-gather collects them) before the same route-order sum -- so every
+rank's result is bit-identical to one GPU.
 """
 
 from __future__ import annotations
@@ -115,7 +117,8 @@ class MoEDecoder:
     """Routed MoE layers of one token on a resident ``ExpertBank``."""
 
     def __init__(self, bank: ExpertBank, top_k: int, scaling: float = 1.0, fused=None,
-                 ep_ranks: int = 1, ep_rank: int = 0, group=None):
+                 ep_ranks: int = 1, ep_rank: int = 0, group=None, exchange: str = "p2p",
+                 exchange_timeout_ms: int = 5000):
         self.bank, self.top_k, self.scaling = bank, top_k, scaling
         self.fused = fused or FusedNVFP4(device=bank.device)
         self.ep_ranks, self.ep_rank, self.group = ep_ranks, ep_rank, group
@@ -127,9 +130,20 @@ class MoEDecoder:
         # x after layer l lives in xbuf[l & 1]
         self.xbuf = torch.zeros(2, bank.hidden, dtype=torch.float32, device=d)
         self.xs = [self.xbuf[0], self.xbuf[1]]
-        if ep_ranks > 1:
+        # exchange of the slot outputs between ranks: "p2p" = peer-memory
+        # exchange kernel fused with the route-order sum (one launch, no
+        # collective); "nccl" = NCCL all-gather + route-sum launch
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError(f"exchange must be 'p2p' or 'nccl', not {exchange!r}")
+        self.exchange, self.exchange_timeout_ms = exchange, int(exchange_timeout_ms)
+        self.xchg = None
+        if ep_ranks > 1 and exchange == "nccl":
             self.contrib = torch.zeros(k * bank.hidden, dtype=torch.float32, device=d)
             self.gathered = torch.zeros(ep_ranks * k * bank.hidden, dtype=torch.float32, device=d)
+        elif ep_ranks > 1:
+            from .ep import PeerExchange
+
+            self.xchg = PeerExchange(group, ep_ranks, ep_rank, bank.hidden, k, d)
         self.graph = None
         self.pdl = True
         # persistent=True: one cooperative launch for all layers of the token
@@ -173,6 +187,20 @@ class MoEDecoder:
                                 ids, b.globals[l], w, k, self.act, out, b.hidden, b.inter, resid=x,
                                 flags=dn_flags)
             return
+        if self.xchg is not None:
+            from .ep import exchange_buffer
+
+            buf = exchange_buffer(l, b.n_layers)
+            up_flags = (_lib.LAUNCH_PDL | (0 if first else _lib.LAUNCH_IDS_READY)) if self.pdl else 0
+            _lib.call("ervf_ep_expert_slots_ex", ptr(b.up_codes[l]), ptr(b.up_scales[l]),
+                      int(b.up_code_bytes), int(b.up_scale_bytes), ptr(b.dn_codes[l]),
+                      ptr(b.dn_scales[l]), int(b.dn_code_bytes), int(b.dn_scale_bytes), ptr(ids),
+                      ptr(b.globals[l]), k, ptr(x), ptr(self.act), self.xchg.slots(buf), b.hidden,
+                      b.inter, self.ep_ranks, self.ep_rank, f._width(), up_flags, self._s())
+            _lib.call("ervf_ep_exchange_route_sum", ptr(self.xchg.peers), self.ep_ranks,
+                      self.ep_rank, buf, ptr(ids), ptr(w), k, ptr(x), ptr(out), b.hidden,
+                      self.exchange_timeout_ms, _lib.LAUNCH_PDL if self.pdl else 0, self._s())
+            return
         import torch.distributed as dist
 
         _lib.call("ervf_ep_expert_slots", ptr(b.up_codes[l]), ptr(b.up_scales[l]),
@@ -183,6 +211,12 @@ class MoEDecoder:
         dist.all_gather_into_tensor(self.gathered, self.contrib, group=self.group)
         _lib.call("ervf_ep_route_sum", ptr(self.gathered), ptr(ids), ptr(w), k, ptr(x), ptr(out),
                   b.hidden, self.ep_ranks, self._s())
+
+    def close(self) -> None:
+        """Releases the peer-exchange regions (collective over the ranks)."""
+        if self.xchg is not None:
+            self.xchg.close()
+            self.xchg = None
 
     def step_batch(self, x_in: torch.Tensor, rlogs: torch.Tensor) -> torch.Tensor:
         """A decode batch of T tokens through every layer, expert-major on the

@@ -38,6 +38,7 @@ extern "C" {
 #define ERVF_ERR_LAUNCH -4   /* the CUDA launch failed */
 #define ERVF_ERR_TIMEOUT -5  /* a bounded device wait ran out (ervf_device_status) */
 #define ERVF_ERR_ARG -6      /* an argument value is invalid (width, batch, ...) */
+#define ERVF_ERR_DEVICE -7    /* a set-up CUDA call failed (allocation, IPC mapping) */
 #define ERVF_ERR_SCRATCH_LIMIT -8 /* larger than the library's fixed scratch array */
 
 /* Launch flags of the grouped MoE entry points.
@@ -196,6 +197,59 @@ ERVF_API int ervf_ep_expert_slots(const uint8_t* up_codes, const uint8_t* up_sca
 ERVF_API int ervf_ep_route_sum(const float* gathered, const int32_t* ids, const float* route_w,
                                int top_k, const float* x, float* out, int hidden, int ep_ranks,
                                void* stream);
+
+/* ervf_ep_expert_slots with launch flags (ERVF_LAUNCH_PDL, ERVF_LAUNCH_IDS_READY,
+ * as for ervf_moe_up_grouped; the down launch always follows the up launch
+ * with the ids already complete). */
+ERVF_API int ervf_ep_expert_slots_ex(const uint8_t* up_codes, const uint8_t* up_scales,
+                                     size_t up_code_stride, size_t up_scale_stride,
+                                     const uint8_t* dn_codes, const uint8_t* dn_scales,
+                                     size_t dn_code_stride, size_t dn_scale_stride,
+                                     const int32_t* ids, const float* globals, int top_k,
+                                     const float* x, float* act, float* contrib, int hidden,
+                                     int inter, int ep_ranks, int ep_rank, int width, int flags,
+                                     void* stream);
+
+/* Expert-parallel exchange over NVLink peer memory (no counterpart in the
+ * reference, which is single-GPU; it replaces the all-gather +
+ * ervf_ep_route_sum pair).  Each rank owns one exchange region:
+ *   [0, 512)  u64 flag[64]   flag[src] = last epoch rank src published
+ *   [512]     u64 seq        epochs this rank has published
+ *   [ERVF_EP_SLOTS_OFFSET]   f32 slots[ERVF_EP_BUFS][top_k][hidden]
+ * Set-up (once, not per token; these calls allocate / map and synchronise):
+ *   ervf_ep_region_alloc  cudaMalloc + zero + 64-byte CUDA IPC handle;
+ *   exchange the handles between the ranks (e.g. an all-gather);
+ *   ervf_ep_region_open   map a peer's region (peer access enabled);
+ *   a device table u64 peers[nranks] of every rank's region as mapped on
+ *   this rank (its own region at [rank]).
+ * Every rank must have finished ervf_ep_region_alloc before any rank runs an
+ * exchange.  Tear-down: ervf_ep_region_close on peers' regions, a barrier
+ * between the ranks, then ervf_ep_region_free on the own region. */
+#define ERVF_EP_SLOTS_OFFSET 1024
+#define ERVF_EP_BUFS 3
+#define ERVF_EP_MAX_RANKS 64
+ERVF_API size_t ervf_ep_region_bytes(int hidden, int top_k);
+ERVF_API int ervf_ep_region_alloc(size_t bytes, void** region, void* ipc_handle);
+ERVF_API int ervf_ep_region_open(const void* ipc_handle, void** region);
+ERVF_API int ervf_ep_region_close(void* region);
+ERVF_API int ervf_ep_region_free(void* region);
+
+/* One layer's exchange + route-order sum, one CTA: the slots this rank owns
+ * must already be in slots[buf] of its own region (ervf_ep_expert_slots_ex
+ * with contrib = region + ERVF_EP_SLOTS_OFFSET + buf*top_k*hidden*4).  The
+ * kernel publishes epoch seq+1 into every rank's flag[rank]
+ * (st.release.sys), waits until all ranks published it (bounded by
+ * timeout_ms; on time-out out is left unwritten and ervf_device_status
+ * reports ERVF_ERR_TIMEOUT), reads slot s from the region of rank
+ * ids[s] % nranks over NVLink and writes out[r] = x[r] + acc, acc =
+ * fmaf(slot_s[r], route_w[s], acc) in route order from 0.0 (x may be NULL):
+ * bit-identical to ervf_moe_down_routesum on one GPU.  Two consecutive
+ * exchanges must use different bufs.  hidden % 4 == 0, x/out 16-byte
+ * aligned; flags: ERVF_LAUNCH_PDL or 0. */
+ERVF_API int ervf_ep_exchange_route_sum(const uint64_t* peers, int nranks, int rank, int buf,
+                                        const int32_t* ids, const float* route_w, int top_k,
+                                        const float* x, float* out, int hidden, int timeout_ms,
+                                        int flags, void* stream);
 
 /* The runtime's masked down path over one panel-major down record
  * (runtime.py:34-52): panel_scan + gemv_down_masked_partial +
