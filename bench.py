@@ -334,11 +334,15 @@ def bf16_gemvs(device, hbm):
     return res
 
 
-def batched_decode(dec, device, hbm, tokens=32, steps=20):
+def batched_decode(dec, device, hbm, world=1, tokens=32, steps=20):
     """Config 4 at batch 32: a decode batch through all layers, expert-major on
     the tensor cores (each routed expert read once per layer for all its
-    tokens), CUDA graph of the whole step, device time.  Bytes per step: the
-    distinct (layer, expert) records the routing touches plus activations."""
+    tokens), CUDA graph of the whole step, device time (max over ranks).  With
+    N GPUs every rank streams only its experts (e % N) and one peer-memory
+    exchange per layer feeds the route-order sum.  Bytes per step: the
+    distinct (layer, expert) records the routing touches plus activations;
+    frac is against the aggregate HBM roofline (N x measured), frac_busiest
+    against the busiest rank's bytes per layer."""
     L, E = dec.bank.n_layers, dec.bank.n_experts
     g = torch.Generator(device=device)
     g.manual_seed(7)
@@ -347,16 +351,30 @@ def batched_decode(dec, device, hbm, tokens=32, steps=20):
     dec.step_batch(xb, rb)
     torch.cuda.synchronize(device)
     ids = dec.bids.view(L, tokens, TOP_K)
-    distinct = sum(int(torch.unique(ids[l]).numel()) for l in range(L))
     rec = 2 * (INTER * HIDDEN // 2 + INTER * HIDDEN // 16)
-    step_bytes = distinct * rec + L * tokens * TOP_K * (HIDDEN + INTER) * 4
+    act_bytes = tokens * TOP_K * (HIDDEN + INTER) * 4
+    distinct, busiest = 0, 0
+    for l in range(L):
+        u = torch.unique(ids[l]).cpu()
+        distinct += int(u.numel())
+        busiest += max(int((u % world == r).sum()) for r in range(world))
+    step_bytes = distinct * rec + L * act_bytes
+    busiest_bytes = busiest * rec + L * act_bytes
     ms = time_graph(lambda i: dec.step_batch(xb, rb), steps, device)
-    return {"tokens_per_step": tokens, "ms_per_step": round(ms, 4),
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"tokens_per_step": tokens, "n_gpus": world, "ms_per_step": round(ms, 4),
             "tok_s": round(tokens / (ms * 1e-3), 1),
             "distinct_experts_per_layer": round(distinct / L, 1),
             "step_bytes": step_bytes, "gbs": round(step_bytes / ms / 1e6, 1),
-            "frac": round(step_bytes / ms / 1e6 / hbm, 4),
-            "path": "expert-major tcgen05 (tolerance), route-order sum"}
+            "frac": round(step_bytes / ms / 1e6 / (hbm * world), 4),
+            "frac_busiest": round(busiest_bytes / ms / 1e6 / hbm, 4),
+            "path": "expert-major tcgen05 (tolerance), route-order sum"
+                    + (", peer-memory exchange" if world > 1 else "")}
 
 
 def cpu_sample(bank, layers_sampled=2, tokens=2):
@@ -565,7 +583,7 @@ def main():
 
     kern = kernel_roofline(dec, bank, device, hbm) if world == 1 else None
     gemv0 = gemv_shape(device, hbm) if (world == 1 and rank == 0) else None
-    batch32 = batched_decode(dec, device, hbm) if (world == 1 and rank == 0) else None
+    batch32 = batched_decode(dec, device, hbm, world)
     extra = None
     if world == 1 and rank == 0:
         # config 2 (Qwen shapes) GEMVs and config 3 BF16 GEMVs, L2-cold

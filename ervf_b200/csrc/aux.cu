@@ -480,10 +480,13 @@ int launch_route_topk_softmax(const float* rlog, int* ids, float* w, int layers,
 // by p (deterministic).  pos[p] = sorted position, tok_sorted[q] = token of
 // the pair at sorted position q; chunks of <= 16 pairs of one expert:
 // chunk_expert / chunk_off / chunk_n, n_chunks.  An id outside [0, E) is
-// recorded in the device error word and counted as expert 0.
+// recorded in the device error word and counted as expert 0.  With expert
+// parallelism every rank sorts all pairs (so pos is the same on every rank)
+// but makes chunks only of the experts it owns (e % ep_ranks == ep_rank).
 __global__ void moe_batch_lists_kernel(const int* __restrict__ ids, int P, int k, int E,
                                        int* chunk_expert, int* chunk_off, int* chunk_n,
-                                       int* n_chunks, int* tok_sorted, int* pos) {
+                                       int* n_chunks, int* tok_sorted, int* pos, int ep_ranks,
+                                       int ep_rank) {
   __shared__ int cnt[kMaxBatchExperts];
   __shared__ int off[kMaxBatchExperts];
   __shared__ int choff[kMaxBatchExperts];
@@ -505,7 +508,7 @@ __global__ void moe_batch_lists_kernel(const int* __restrict__ ids, int P, int k
       off[e] = o;
       choff[e] = c;
       o += cnt[e];
-      c += (cnt[e] + 15) / 16;
+      if (e % ep_ranks == ep_rank) c += (cnt[e] + 15) / 16;
     }
     *n_chunks = c;
   }
@@ -524,6 +527,7 @@ __global__ void moe_batch_lists_kernel(const int* __restrict__ ids, int P, int k
     tok_sorted[sp] = q / k;
   }
   for (int e = tid; e < E; e += blockDim.x) {
+    if (e % ep_ranks != ep_rank) continue;
     const int nc = (cnt[e] + 15) / 16;
     for (int c = 0; c < nc; ++c) {
       chunk_expert[choff[e] + c] = e;
@@ -548,9 +552,10 @@ __global__ void moe_batch_routesum_kernel(const float* __restrict__ contrib, con
 }
 
 int launch_moe_batch_lists(const int* ids, int P, int k, int E, int* chunk_expert, int* chunk_off,
-                           int* chunk_n, int* n_chunks, int* tok_sorted, int* pos, cudaStream_t stream) {
+                           int* chunk_n, int* n_chunks, int* tok_sorted, int* pos, int ep_ranks,
+                           int ep_rank, cudaStream_t stream) {
   moe_batch_lists_kernel<<<1, 512, 0, stream>>>(ids, P, k, E, chunk_expert, chunk_off, chunk_n, n_chunks,
-                                               tok_sorted, pos);
+                                               tok_sorted, pos, ep_ranks, ep_rank);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 

@@ -13,7 +13,8 @@ int launch_route_topk_softmax(const float* rlog, int* ids, float* w, int layers,
                               cudaStream_t stream);
 constexpr int kMaxBatchExperts = 1024;
 int launch_moe_batch_lists(const int* ids, int P, int k, int E, int* chunk_expert, int* chunk_off,
-                           int* chunk_n, int* n_chunks, int* tok_sorted, int* pos, cudaStream_t stream);
+                           int* chunk_n, int* n_chunks, int* tok_sorted, int* pos, int ep_ranks,
+                           int ep_rank, cudaStream_t stream);
 int launch_moe_batch_routesum(const float* contrib, const int* pos, const float* w, const float* x,
                               float* out, int T, int hidden, int k, cudaStream_t stream);
 int launch_route_topk_batched(const float* rlog, const float* gate_b, int* ids, float* w, int layers,

@@ -446,35 +446,17 @@ BatchScratch batch_scratch(void* base, int pairs, int hidden, int inter) {
   b.bytes = ints * 4 + (size_t)pairs * (inter + hidden) * 4;
   return b;
 }
-}  // namespace
 
-size_t ervf_moe_batched_scratch_bytes(int tokens, int top_k, int hidden, int inter) {
-  if (tokens <= 0 || top_k <= 0 || hidden <= 0 || inter <= 0) return 0;
-  return batch_scratch(nullptr, tokens * top_k, hidden, inter).bytes;
-}
-
-int ervf_moe_batched(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
-                     size_t up_scale_stride, const uint8_t* dn_codes, const uint8_t* dn_scales,
-                     size_t dn_code_stride, size_t dn_scale_stride, const float* globals,
-                     const int32_t* ids, const float* route_w, int tokens, int top_k, int n_experts,
-                     const float* x, float* out, int hidden, int inter, void* scratch,
-                     size_t scratch_bytes, void* stream) {
-  if (!up_codes || !up_scales || !dn_codes || !dn_scales || !globals || !ids || !route_w || !x ||
-      !out || !scratch)
-    return kErrNull;
-  const int pairs = tokens * top_k;
-  if (tokens <= 0 || top_k <= 0 || top_k > kMaxJobs || pairs > 4096 || n_experts <= 0 ||
-      n_experts > kMaxBatchExperts)
-    return kErrShape;
-  if (hidden <= 0 || inter <= 0 || hidden % 32 || inter % 32) return kErrShape;
-  const BatchScratch b = batch_scratch(scratch, pairs, hidden, inter);
-  if (scratch_bytes < b.bytes) return kErrArg;
-  if (!al(up_codes, 16) || !al(dn_codes, 16) || !al(up_scales, 2) || !al(dn_scales, 2) || !al(x, 16) ||
-      !al(scratch, 16) || ((up_code_stride | dn_code_stride) & 15u) || ((up_scale_stride | dn_scale_stride) & 1u))
-    return kErrAlign;
-  cudaStream_t st = S(stream);
+// Lists, up and down of the batched block: contrib[pos[p]] = the down output
+// of pair p for the pairs whose expert this rank owns (all with ep_ranks 1).
+int batch_slots(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
+                size_t up_scale_stride, const uint8_t* dn_codes, const uint8_t* dn_scales,
+                size_t dn_code_stride, size_t dn_scale_stride, const float* globals,
+                const int32_t* ids, int pairs, int top_k, int n_experts, const float* x, int hidden,
+                int inter, const BatchScratch& b, float* contrib, int ep_ranks, int ep_rank,
+                cudaStream_t st) {
   if (int e = launch_moe_batch_lists(ids, pairs, top_k, n_experts, b.chunk_expert, b.chunk_off, b.chunk_n,
-                                     b.n_chunks, b.tok_sorted, b.pos, st))
+                                     b.n_chunks, b.tok_sorted, b.pos, ep_ranks, ep_rank, st))
     return e;
   GroupedTc g{};
   g.chunk_expert = b.chunk_expert;
@@ -504,17 +486,117 @@ int ervf_moe_batched(const uint8_t* up_codes, const uint8_t* up_scales, size_t u
   g.gsel = 0;
   g.x = b.act;
   g.b_idx = nullptr;
-  g.out = b.contrib;
+  g.out = contrib;
   g.rows = hidden;
   g.cols = inter;
   g.relu2 = 0;
-  if (int e = launch_grouped_tc(g, st)) return e;
+  return launch_grouped_tc(g, st);
+}
+
+int check_batched(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
+                  size_t up_scale_stride, const uint8_t* dn_codes, const uint8_t* dn_scales,
+                  size_t dn_code_stride, size_t dn_scale_stride, const float* x, int tokens,
+                  int top_k, int n_experts, int hidden, int inter, const void* scratch,
+                  size_t scratch_bytes) {
+  const int pairs = tokens * top_k;
+  if (tokens <= 0 || top_k <= 0 || top_k > kMaxJobs || pairs > 4096 || n_experts <= 0 ||
+      n_experts > kMaxBatchExperts)
+    return kErrShape;
+  if (hidden <= 0 || inter <= 0 || hidden % 32 || inter % 32) return kErrShape;
+  if (scratch_bytes < batch_scratch(nullptr, pairs, hidden, inter).bytes) return kErrArg;
+  if (!al(up_codes, 16) || !al(dn_codes, 16) || !al(up_scales, 2) || !al(dn_scales, 2) || !al(x, 16) ||
+      !al(scratch, 16) || ((up_code_stride | dn_code_stride) & 15u) ||
+      ((up_scale_stride | dn_scale_stride) & 1u))
+    return kErrAlign;
+  return kOk;
+}
+}  // namespace
+
+size_t ervf_moe_batched_scratch_bytes(int tokens, int top_k, int hidden, int inter) {
+  if (tokens <= 0 || top_k <= 0 || hidden <= 0 || inter <= 0) return 0;
+  return batch_scratch(nullptr, tokens * top_k, hidden, inter).bytes;
+}
+
+int ervf_moe_batched(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
+                     size_t up_scale_stride, const uint8_t* dn_codes, const uint8_t* dn_scales,
+                     size_t dn_code_stride, size_t dn_scale_stride, const float* globals,
+                     const int32_t* ids, const float* route_w, int tokens, int top_k, int n_experts,
+                     const float* x, float* out, int hidden, int inter, void* scratch,
+                     size_t scratch_bytes, void* stream) {
+  if (!up_codes || !up_scales || !dn_codes || !dn_scales || !globals || !ids || !route_w || !x ||
+      !out || !scratch)
+    return kErrNull;
+  if (int e = check_batched(up_codes, up_scales, up_code_stride, up_scale_stride, dn_codes, dn_scales,
+                            dn_code_stride, dn_scale_stride, x, tokens, top_k, n_experts, hidden,
+                            inter, scratch, scratch_bytes))
+    return e;
+  const int pairs = tokens * top_k;
+  const BatchScratch b = batch_scratch(scratch, pairs, hidden, inter);
+  cudaStream_t st = S(stream);
+  if (int e = batch_slots(up_codes, up_scales, up_code_stride, up_scale_stride, dn_codes, dn_scales,
+                          dn_code_stride, dn_scale_stride, globals, ids, pairs, top_k, n_experts, x,
+                          hidden, inter, b, b.contrib, 1, 0, st))
+    return e;
   return launch_moe_batch_routesum(b.contrib, b.pos, route_w, x, out, tokens, hidden, top_k, st);
 }
 
-size_t ervf_ep_region_bytes(int hidden, int top_k) {
-  if (hidden <= 0 || top_k <= 0 || top_k > kMaxJobs) return 0;
-  return ep_region_bytes(hidden, top_k);
+int ervf_moe_batched_ep_slots(const uint8_t* up_codes, const uint8_t* up_scales,
+                              size_t up_code_stride, size_t up_scale_stride,
+                              const uint8_t* dn_codes, const uint8_t* dn_scales,
+                              size_t dn_code_stride, size_t dn_scale_stride, const float* globals,
+                              const int32_t* ids, int tokens, int top_k, int n_experts,
+                              const float* x, float* slots, int hidden, int inter, int ep_ranks,
+                              int ep_rank, void* scratch, size_t scratch_bytes, void* stream) {
+  if (!up_codes || !up_scales || !dn_codes || !dn_scales || !globals || !ids || !x || !slots ||
+      !scratch)
+    return kErrNull;
+  if (ep_ranks < 1 || ep_ranks > kEpMaxRanks || ep_rank < 0 || ep_rank >= ep_ranks) return kErrShape;
+  if (int e = check_batched(up_codes, up_scales, up_code_stride, up_scale_stride, dn_codes, dn_scales,
+                            dn_code_stride, dn_scale_stride, x, tokens, top_k, n_experts, hidden,
+                            inter, scratch, scratch_bytes))
+    return e;
+  if (!al(slots, 16)) return kErrAlign;
+  const BatchScratch b = batch_scratch(scratch, tokens * top_k, hidden, inter);
+  return batch_slots(up_codes, up_scales, up_code_stride, up_scale_stride, dn_codes, dn_scales,
+                     dn_code_stride, dn_scale_stride, globals, ids, tokens * top_k, top_k, n_experts,
+                     x, hidden, inter, b, slots, ep_ranks, ep_rank, S(stream));
+}
+
+int ervf_ep_batch_exchange_route_sum(const uint64_t* peers, int nranks, int rank, int buf,
+                                     const int32_t* ids, const float* route_w, int tokens,
+                                     int top_k, const float* x, float* out, int hidden, int inter,
+                                     const void* scratch, size_t scratch_bytes, int timeout_ms,
+                                     void* stream) {
+  if (!peers || !ids || !route_w || !out || !scratch) return kErrNull;
+  const int pairs = tokens * top_k;
+  if (nranks < 1 || nranks > kEpMaxRanks || rank < 0 || rank >= nranks) return kErrShape;
+  if (tokens <= 0 || top_k <= 0 || top_k > kMaxJobs || pairs > 4096 || hidden <= 0 || hidden % 4 ||
+      inter <= 0)
+    return kErrShape;
+  if (buf < 0 || buf >= kEpBufs || timeout_ms <= 0 || timeout_ms > 600000) return kErrArg;
+  const BatchScratch b = batch_scratch(const_cast<void*>(scratch), pairs, hidden, inter);
+  if (scratch_bytes < b.bytes) return kErrArg;
+  if (!al(peers, 8) || !al(out, 16) || (x && !al(x, 16))) return kErrAlign;
+  EpBatchExchange a{};
+  a.peers = peers;
+  a.nranks = nranks;
+  a.rank = rank;
+  a.buf = buf;
+  a.tokens = tokens;
+  a.top_k = top_k;
+  a.hidden = hidden;
+  a.ids = ids;
+  a.pos = b.pos;
+  a.route_w = route_w;
+  a.x = x;
+  a.out = out;
+  a.timeout_ns = (uint64_t)timeout_ms * 1000000ull;
+  return launch_ep_batch_exchange_sum(a, S(stream));
+}
+
+size_t ervf_ep_region_bytes(int hidden, int slots) {
+  if (hidden <= 0 || slots <= 0 || slots > 4096) return 0;
+  return ep_region_bytes(hidden, slots);
 }
 
 int ervf_ep_region_alloc(size_t bytes, void** region, void* ipc_handle) {

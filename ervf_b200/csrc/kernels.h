@@ -173,8 +173,8 @@ constexpr int kEpBufs = 3;
 constexpr size_t kEpSlotsOffset = 1024;
 constexpr int kEpThreads = 1024;
 
-inline size_t ep_region_bytes(int hidden, int top_k) {
-  return kEpSlotsOffset + (size_t)kEpBufs * top_k * hidden * sizeof(float);
+inline size_t ep_region_bytes(int hidden, int slots) {
+  return kEpSlotsOffset + (size_t)kEpBufs * slots * hidden * sizeof(float);
 }
 
 struct EpExchange {
@@ -188,5 +188,20 @@ struct EpExchange {
 };
 
 int launch_ep_exchange_sum(const EpExchange& a, bool pdl, cudaStream_t stream);
+
+// Batched form: pair p = t * top_k + s of token t; its output is slot
+// pos[p] of the region of rank ids[p] % nranks.
+struct EpBatchExchange {
+  const uint64_t* peers;
+  int nranks, rank, buf, tokens, top_k, hidden;
+  const int* ids;        // [tokens * top_k]
+  const int* pos;        // [tokens * top_k], the same on every rank
+  const float* route_w;  // [tokens * top_k]
+  const float* x;        // [tokens][hidden] or NULL
+  float* out;            // [tokens][hidden]
+  uint64_t timeout_ns;
+};
+
+int launch_ep_batch_exchange_sum(const EpBatchExchange& a, cudaStream_t stream);
 
 }  // namespace ervf

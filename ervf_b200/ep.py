@@ -36,14 +36,16 @@ class PeerExchange:
     Each rank allocates one region (``ervf_ep_region_alloc``), the 64-byte
     IPC handles are all-gathered over ``group``, and every peer's region is
     mapped here (``ervf_ep_region_open``).  ``peers`` is the device table
-    u64[world] the exchange kernel reads; ``slots(buf)`` the address where
-    this rank's down launch writes the slots it owns.  Set-up only: the
+    u64[world] the exchange kernel reads; ``slots(buf)`` the address of slot
+    buffer ``buf`` (``n_slots`` rows of ``hidden`` floats: top_k for one
+    token, tokens * top_k for a batch) where this rank's down launch writes
+    the slots it owns.  Set-up only: the
     per-layer exchange (``ervf_ep_exchange_route_sum``) is one kernel with no
     collective call.  ``close()`` unmaps the peers, waits for every rank and
     frees the own region.
     """
 
-    def __init__(self, group, world: int, rank: int, hidden: int, top_k: int, device):
+    def __init__(self, group, world: int, rank: int, hidden: int, n_slots: int, device):
         import ctypes
 
         import torch
@@ -51,10 +53,10 @@ class PeerExchange:
 
         from . import _lib
 
-        self.world, self.rank, self.hidden, self.top_k = world, rank, hidden, top_k
+        self.world, self.rank, self.hidden, self.n_slots = world, rank, hidden, n_slots
         self.group, self.device = group, device
         lib = _lib.load()
-        self.nbytes = int(lib.ervf_ep_region_bytes(hidden, top_k))
+        self.nbytes = int(lib.ervf_ep_region_bytes(hidden, n_slots))
         if self.nbytes == 0:
             raise ValueError("unsupported exchange shape")
         own = ctypes.c_void_p()
@@ -82,7 +84,7 @@ class PeerExchange:
         dist.barrier(group=group)
 
     def slots(self, buf: int) -> int:
-        return self.own + 1024 + buf * self.top_k * self.hidden * 4
+        return self.own + 1024 + buf * self.n_slots * self.hidden * 4
 
     def close(self) -> None:
         import torch.distributed as dist

@@ -137,6 +137,7 @@ class MoEDecoder:
             raise ValueError(f"exchange must be 'p2p' or 'nccl', not {exchange!r}")
         self.exchange, self.exchange_timeout_ms = exchange, int(exchange_timeout_ms)
         self.xchg = None
+        self._bxchg = None  # exchange regions of the batched block (sized per batch)
         if ep_ranks > 1 and exchange == "nccl":
             self.contrib = torch.zeros(k * bank.hidden, dtype=torch.float32, device=d)
             self.gathered = torch.zeros(ep_ranks * k * bank.hidden, dtype=torch.float32, device=d)
@@ -217,11 +218,20 @@ class MoEDecoder:
         if self.xchg is not None:
             self.xchg.close()
             self.xchg = None
+        if self._bxchg is not None:
+            self._bxchg.close()
+            self._bxchg = None
 
     def step_batch(self, x_in: torch.Tensor, rlogs: torch.Tensor) -> torch.Tensor:
         """A decode batch of T tokens through every layer, expert-major on the
         tensor cores (tolerance path).  x_in f32[T][hidden], rlogs
-        f32[L][T][E].  Returns the buffer holding x after the last layer."""
+        f32[L][T][E].  Returns the buffer holding x after the last layer.
+        With expert parallelism every rank streams only the experts it owns
+        for all T tokens, and one exchange kernel per layer reads each pair's
+        output from its owner over NVLink before the route-order sum (same
+        result as one GPU).  The first call with a new T sets up the exchange
+        regions (a collective over the ranks), so make it outside graph
+        capture."""
         b, k = self.bank, self.top_k
         L, T = b.n_layers, x_in.shape[0]
         d = b.device
@@ -230,15 +240,38 @@ class MoEDecoder:
             self.bids = torch.zeros(L * T, k, dtype=torch.int32, device=d)
             self.bw = torch.zeros(L * T, k, dtype=torch.float32, device=d)
             self.bx = torch.zeros(2, T, b.hidden, dtype=torch.float32, device=d)
+            if self.ep_ranks > 1:
+                from .ep import PeerExchange
+
+                if self._bxchg is not None:
+                    self._bxchg.close()
+                self._bxchg = PeerExchange(self.group, self.ep_ranks, self.ep_rank, b.hidden, T * k, d)
+                self._bnb = int(_lib.load().ervf_moe_batched_scratch_bytes(T, k, b.hidden, b.inter))
+                self._bscr = torch.empty(self._bnb, dtype=torch.uint8, device=d)
         self.fused.route_topk_batched(rlogs, None, self.bids, self.bw, L * T, b.n_experts, k,
                                       self.scaling)
         cur = x_in
         for l in range(L):
             nxt = self.bx[l & 1]
-            self.fused.moe_batched(b.up_codes[l], b.up_scales[l], b.up_code_bytes, b.up_scale_bytes,
-                                   b.dn_codes[l], b.dn_scales[l], b.dn_code_bytes, b.dn_scale_bytes,
-                                   b.globals[l], self.bids[l * T:(l + 1) * T], self.bw[l * T:(l + 1) * T],
-                                   T, k, b.n_experts, cur, nxt, b.hidden, b.inter)
+            ids, w = self.bids[l * T:(l + 1) * T], self.bw[l * T:(l + 1) * T]
+            if self.ep_ranks == 1:
+                self.fused.moe_batched(b.up_codes[l], b.up_scales[l], b.up_code_bytes,
+                                       b.up_scale_bytes, b.dn_codes[l], b.dn_scales[l],
+                                       b.dn_code_bytes, b.dn_scale_bytes, b.globals[l], ids, w, T, k,
+                                       b.n_experts, cur, nxt, b.hidden, b.inter)
+            else:
+                from .ep import exchange_buffer
+
+                buf = exchange_buffer(l, L)
+                _lib.call("ervf_moe_batched_ep_slots", ptr(b.up_codes[l]), ptr(b.up_scales[l]),
+                          int(b.up_code_bytes), int(b.up_scale_bytes), ptr(b.dn_codes[l]),
+                          ptr(b.dn_scales[l]), int(b.dn_code_bytes), int(b.dn_scale_bytes),
+                          ptr(b.globals[l]), ptr(ids), T, k, b.n_experts, ptr(cur),
+                          self._bxchg.slots(buf), b.hidden, b.inter, self.ep_ranks, self.ep_rank,
+                          ptr(self._bscr), self._bnb, self._s())
+                _lib.call("ervf_ep_batch_exchange_route_sum", ptr(self._bxchg.peers), self.ep_ranks,
+                          self.ep_rank, buf, ptr(ids), ptr(w), T, k, ptr(cur), ptr(nxt), b.hidden,
+                          b.inter, ptr(self._bscr), self._bnb, self.exchange_timeout_ms, self._s())
             cur = nxt
         return cur
 

@@ -228,7 +228,7 @@ ERVF_API int ervf_ep_expert_slots_ex(const uint8_t* up_codes, const uint8_t* up_
 #define ERVF_EP_SLOTS_OFFSET 1024
 #define ERVF_EP_BUFS 3
 #define ERVF_EP_MAX_RANKS 64
-ERVF_API size_t ervf_ep_region_bytes(int hidden, int top_k);
+ERVF_API size_t ervf_ep_region_bytes(int hidden, int slots);  /* slots = top_k, or tokens*top_k */
 ERVF_API int ervf_ep_region_alloc(size_t bytes, void** region, void* ipc_handle);
 ERVF_API int ervf_ep_region_open(const void* ipc_handle, void** region);
 ERVF_API int ervf_ep_region_close(void* region);
@@ -334,6 +334,36 @@ ERVF_API int ervf_moe_batched(const uint8_t* up_codes, const uint8_t* up_scales,
 
 /* Bytes of scratch ervf_moe_batched uses. */
 ERVF_API size_t ervf_moe_batched_scratch_bytes(int tokens, int top_k, int hidden, int inter);
+
+/* Expert-parallel form of ervf_moe_batched (no counterpart in the reference,
+ * which is single-GPU): the lists sort every pair on every rank (so the
+ * sorted position pos[p] of pair p is the same everywhere) but this rank runs
+ * up and down only for the experts it owns (e % ep_ranks == ep_rank), writing
+ * slots[pos[p]] (f32 [tokens*top_k][hidden]; normally slots[buf] of the
+ * rank's exchange region, see ervf_ep_region_alloc).  Scratch as for
+ * ervf_moe_batched. */
+ERVF_API int ervf_moe_batched_ep_slots(const uint8_t* up_codes, const uint8_t* up_scales,
+                                       size_t up_code_stride, size_t up_scale_stride,
+                                       const uint8_t* dn_codes, const uint8_t* dn_scales,
+                                       size_t dn_code_stride, size_t dn_scale_stride,
+                                       const float* globals, const int32_t* ids, int tokens,
+                                       int top_k, int n_experts, const float* x, float* slots,
+                                       int hidden, int inter, int ep_ranks, int ep_rank,
+                                       void* scratch, size_t scratch_bytes, void* stream);
+
+/* The batched exchange + route-order sum over NVLink peer memory, after
+ * ervf_moe_batched_ep_slots on every rank with the same scratch: publishes
+ * and waits for the epoch as ervf_ep_exchange_route_sum does, then out[t] =
+ * x[t] + acc, acc = fmaf(slot(p)[r], route_w[p], acc) over p = t*top_k + s,
+ * s in route order, slot(p) read from slots[buf][pos[p]] of the region of
+ * rank ids[p] % nranks -- identical to ervf_moe_batched on one GPU.  The
+ * region must hold tokens*top_k slots (ervf_ep_region_bytes(hidden,
+ * tokens*top_k)); two consecutive exchanges use different bufs. */
+ERVF_API int ervf_ep_batch_exchange_route_sum(const uint64_t* peers, int nranks, int rank, int buf,
+                                              const int32_t* ids, const float* route_w, int tokens,
+                                              int top_k, const float* x, float* out, int hidden,
+                                              int inter, const void* scratch, size_t scratch_bytes,
+                                              int timeout_ms, void* stream);
 
 /* Softmax top-k routing of `layers` logit rows f32[layers][n] (config 2,
  * Qwen shape; the reference's router is sigmoid only): per layer the top_k

@@ -6,9 +6,12 @@ bit-identical to the single-GPU routed sum (the oracle), through every slot
 buffer in turn; and a wait on a flag that nothing sets runs out after its
 limit, reports ERVF_ERR_TIMEOUT and leaves the context usable.
 
+The batched block as one rank equals ervf_moe_batched bit for bit.
+
 Two or more GPUs (skipped otherwise): one process per GPU over NCCL, experts
 sharded by id, every layer's slots exchanged over NVLink; each rank's x after
-every layer must equal one GPU's bit for bit, eager and in a CUDA graph.
+every layer must equal one GPU's bit for bit, eager and in a CUDA graph, and
+the batched block's likewise.
 """
 
 from __future__ import annotations
@@ -101,6 +104,50 @@ def test_single_rank_exchange_matches_oracle(oracle, experts, cuda):
             ex = {e: (*ups[e], *dns[e]) for e in range(E)}
             want = (x + oracle.moe_block(x, ex, ids, w, HIDDEN, INTER)).astype(np.float32)
             assert bits_equal(out.cpu().numpy(), want), (step, buf)
+        assert _lib.load().ervf_device_status() == _lib.OK
+    finally:
+        reg.free()
+
+
+def test_single_rank_batched_exchange_matches_moe_batched(fused, cuda):
+    """The expert-parallel batched block as one rank (slots into the exchange
+    region, then the batched exchange + route sum) equals ervf_moe_batched
+    bit for bit, through two slot buffers in turn."""
+    from ervf_b200 import _lib
+    from ervf_b200.moe import ExpertBank
+
+    T, k, E2 = 8, 6, 16
+    eb = ExpertBank.synthetic(1, E2, HIDDEN, INTER, cuda, seed=9)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(4)
+    reg = _Region(HIDDEN, T * k)
+    try:
+        peers = torch.tensor([reg.ptr], dtype=torch.int64, device=cuda)
+        nb = int(_lib.load().ervf_moe_batched_scratch_bytes(T, k, HIDDEN, INTER))
+        scr = torch.empty(nb, dtype=torch.uint8, device=cuda)
+        for buf in (0, 1):
+            x = torch.randn(T, HIDDEN, generator=g, device=cuda)
+            rl = torch.randn(T, E2, generator=g, device=cuda)
+            ids = torch.zeros(T, k, dtype=torch.int32, device=cuda)
+            w = torch.zeros(T, k, device=cuda)
+            fused.route_topk_batched(rl, None, ids, w, T, E2, k, 1.0)
+            want = torch.full((T, HIDDEN), float("nan"), device=cuda)
+            fused.moe_batched(eb.up_codes[0], eb.up_scales[0], eb.up_code_bytes, eb.up_scale_bytes,
+                              eb.dn_codes[0], eb.dn_scales[0], eb.dn_code_bytes, eb.dn_scale_bytes,
+                              eb.globals[0], ids, w, T, k, E2, x, want, HIDDEN, INTER)
+            out = torch.full((T, HIDDEN), float("nan"), device=cuda)
+            _lib.call("ervf_moe_batched_ep_slots", eb.up_codes[0].data_ptr(),
+                      eb.up_scales[0].data_ptr(), eb.up_code_bytes, eb.up_scale_bytes,
+                      eb.dn_codes[0].data_ptr(), eb.dn_scales[0].data_ptr(), eb.dn_code_bytes,
+                      eb.dn_scale_bytes, eb.globals[0].data_ptr(), ids.data_ptr(), T, k, E2,
+                      x.data_ptr(), reg.slots(buf, T * k, HIDDEN), HIDDEN, INTER, 1, 0,
+                      scr.data_ptr(), nb, _stream(cuda))
+            _lib.call("ervf_ep_batch_exchange_route_sum", peers.data_ptr(), 1, 0, buf,
+                      ids.data_ptr(), w.data_ptr(), T, k, x.data_ptr(), out.data_ptr(), HIDDEN,
+                      INTER, scr.data_ptr(), nb, 2000, _stream(cuda))
+            torch.cuda.synchronize()
+            assert torch.isfinite(want).all()
+            assert torch.equal(want.view(torch.int32), out.view(torch.int32)), buf
         assert _lib.load().ervf_device_status() == _lib.OK
     finally:
         reg.free()
@@ -214,6 +261,17 @@ def _worker(rank, world, port, q):
             torch.cuda.synchronize()
             if not torch.equal(want.view(torch.int32), y.view(torch.int32)):
                 bad.append(("graph", t))
+        # the batched block (expert-major, tensor cores), odd layer count
+        T = 8
+        xb = torch.randn(T, HIDDEN, generator=g, device=dev)
+        rb = torch.randn(L, T, E, generator=g, device=dev)
+        for t in range(2):
+            want = one.step_batch(xb, rb).clone()
+            got = ep.step_batch(xb, rb).clone()
+            torch.cuda.synchronize()
+            if not torch.equal(want.view(torch.int32), got.view(torch.int32)):
+                bad.append(("batch", t))
+            xb = want
         from ervf_b200 import _lib
 
         status = _lib.load().ervf_device_status()
