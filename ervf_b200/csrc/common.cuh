@@ -104,28 +104,18 @@ __device__ __forceinline__ float2 f16x2_to_f32x2(uint32_t h) {
 
 // The eight E2M1 codes of a 32-bit word (code i = nibble i, low first) as
 // exact binary32 values f[0..7]: hardware e2m1x2 -> f16x2, then f16 -> f32.
+// The halves are widened with __low2float / __high2float, which the compiler
+// folds into the half-select of the conversion (an explicit unpack of the
+// f16x2 word costs one more integer instruction per two weights).
 __device__ __forceinline__ void e2m1x8_to_f32(uint32_t q, float (&f)[8]) {
-  asm("{\n"
-      " .reg .b8 b0, b1, b2, b3;\n"
-      " .reg .b32 h0, h1, h2, h3;\n"
-      " .reg .b16 l0, u0, l1, u1, l2, u2, l3, u3;\n"
-      " mov.b32 {b0, b1, b2, b3}, %8;\n"
-      " cvt.rn.f16x2.e2m1x2 h0, b0;\n"
-      " cvt.rn.f16x2.e2m1x2 h1, b1;\n"
-      " cvt.rn.f16x2.e2m1x2 h2, b2;\n"
-      " cvt.rn.f16x2.e2m1x2 h3, b3;\n"
-      " mov.b32 {l0, u0}, h0;\n"
-      " mov.b32 {l1, u1}, h1;\n"
-      " mov.b32 {l2, u2}, h2;\n"
-      " mov.b32 {l3, u3}, h3;\n"
-      " cvt.f32.f16 %0, l0;\n cvt.f32.f16 %1, u0;\n"
-      " cvt.f32.f16 %2, l1;\n cvt.f32.f16 %3, u1;\n"
-      " cvt.f32.f16 %4, l2;\n cvt.f32.f16 %5, u2;\n"
-      " cvt.f32.f16 %6, l3;\n cvt.f32.f16 %7, u3;\n"
-      "}"
-      : "=f"(f[0]), "=f"(f[1]), "=f"(f[2]), "=f"(f[3]), "=f"(f[4]), "=f"(f[5]), "=f"(f[6]),
-        "=f"(f[7])
-      : "r"(q));
+  uint32_t h[4];
+  e2m1x8_to_f16x2(q, h);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 v = *reinterpret_cast<const __half2*>(&h[i]);
+    f[2 * i] = __low2float(v);
+    f[2 * i + 1] = __high2float(v);
+  }
 }
 
 // ------------------------------------------------- packed fp32 arithmetic
