@@ -377,6 +377,24 @@ def batched_decode(dec, device, hbm, world=1, tokens=32, steps=20):
                     + (", peer-memory exchange" if world > 1 else "")}
 
 
+def routed_decode(dec, device, hbm, steps=50):
+    """Config 4 at batch 1 with the router on the device between the layers
+    (per layer: router GEMV fp32 [128 x 2688] + top-k in one launch, then up
+    and down + routed sum), graph-timed: the decode step as the reference's
+    runtime runs it (runtime.py:705-746), minus the trunk."""
+    L, E = dec.bank.n_layers, dec.bank.n_experts
+    g = torch.Generator(device=device)
+    g.manual_seed(11)
+    gate_w = torch.randn(L, E, HIDDEN, generator=g, device=device) * 0.02
+    x = torch.randn(HIDDEN, generator=g, device=device)
+    ms = time_graph(lambda i: dec.step_with_router(x, gate_w), steps, device)
+    router_bytes = E * HIDDEN * 4 + HIDDEN * 4
+    token_bytes = L * (TOP_K * dec.bank.expert_bytes() + router_bytes)
+    return {"ms_per_token": round(ms, 4), "tok_s": round(1e3 / ms, 1),
+            "launches_per_token": 3 * L, "token_bytes": token_bytes,
+            "frac": round(token_bytes / ms / 1e6 / hbm, 4)}
+
+
 def cpu_sample(bank, layers_sampled=2, tokens=2):
     """Reference-path CPU baseline on a bounded sample: `tokens` tokens x
     `layers_sampled` layers of the same workload, torch FP32 dequant + matmul
@@ -584,6 +602,7 @@ def main():
     kern = kernel_roofline(dec, bank, device, hbm) if world == 1 else None
     gemv0 = gemv_shape(device, hbm) if (world == 1 and rank == 0) else None
     batch32 = batched_decode(dec, device, hbm, world)
+    routed = routed_decode(dec, device, hbm) if world == 1 else None
     extra = None
     if world == 1 and rank == 0:
         # config 2 (Qwen shapes) GEMVs and config 3 BF16 GEMVs, L2-cold
@@ -635,6 +654,8 @@ def main():
             line.update(extra)
         if batch32 is not None:
             line["batched_decode_b32"] = batch32
+        if routed is not None:
+            line["decode_with_device_router"] = routed
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_sample(bank)
         print(json.dumps(line), flush=True)

@@ -87,6 +87,8 @@ SIGNATURES: dict[str, list] = {
     "ervf_panel_major": [_vp, _vp, _vp, _i, _i, _vp],
     "ervf_bf16_gemv": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "ervf_route_topk": [_vp, _vp, _vp, _vp, _i, _i, _f, _i, _vp],
+    "ervf_f32_gemv": [_vp, _vp, _vp, _i, _i, _vp],
+    "ervf_route_gemv_topk": [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _vp, _i, _vp],
     "ervf_cache_assign": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp],
     "ervf_cache_fetch": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _i, _vp],
 }

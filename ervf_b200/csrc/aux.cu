@@ -7,6 +7,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "aux.h"
+#include "route.cuh"
 
 namespace ervf {
 
@@ -97,81 +98,11 @@ template <int NPL>
 __global__ void route_topk_warp_kernel(const float* __restrict__ rlog, const float* __restrict__ gate_b,
                                        int* __restrict__ ids, float* __restrict__ w, int layers, int n,
                                        int top_k, float scaling, int bad_pick, int bias_stride) {
-  const int lane = threadIdx.x & 31;
   const int layer = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (layer >= layers) return;
-  const float* lg = rlog + (size_t)layer * n;
-  const float* bs = gate_b ? gate_b + (size_t)layer * bias_stride : nullptr;
-  float sc[NPL], ch[NPL];
-#pragma unroll
-  for (int i = 0; i < NPL; ++i) {
-    const int e = lane + 32 * i;
-    if (e < n) {
-      const float s = 1.0f / (1.0f + expf(-lg[e]));
-      sc[i] = s;
-      ch[i] = s + (bs ? bs[e] : 0.0f);
-    } else {
-      sc[i] = 0.0f;
-      ch[i] = -3.0e38f;
-    }
-  }
-  auto argmax = [&]() -> int {
-    float bv = -3.0e38f;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < NPL; ++i)
-      if (ch[i] > bv) { bv = ch[i]; bi = lane + 32 * i; }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-    }
-    return bi == 0x7fffffff ? 0 : bi;
-  };
-  auto drop = [&](int e) {
-    if ((e & 31) == lane) {
-#pragma unroll
-      for (int i = 0; i < NPL; ++i)
-        if (i == (e >> 5)) ch[i] = -3.0e38f;
-    }
-  };
-  auto score_of = [&](int e) -> float {
-    float v = 0.0f;
-#pragma unroll
-    for (int i = 0; i < NPL; ++i)
-      if (i == (e >> 5)) v = sc[i];
-    return __shfl_sync(0xffffffffu, v, e & 31);
-  };
-  // Selection s is kept by lane s % 32 (top_k <= 64: two per lane at most),
-  // so the final normalisation runs on all lanes in parallel.
-  int my_id[2] = {0, 0};
-  float my_v[2] = {0.0f, 0.0f};
-  float wsum = 0.0f;
-  for (int s = 0; s < top_k; ++s) {
-    int bi = argmax();
-    if (bad_pick && s == top_k - 1) {
-      drop(bi);
-      bi = argmax();
-    }
-    drop(bi);
-    const float v = score_of(bi);
-    if ((s & 31) == lane) {
-      my_id[s >> 5] = bi;
-      my_v[s >> 5] = v;
-    }
-    wsum += v;
-  }
-  int* io = ids + (size_t)layer * top_k;
-  float* wo = w + (size_t)layer * top_k;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int s = lane + 32 * h;
-    if (s < top_k) {
-      io[s] = my_id[h];
-      wo[s] = my_v[h] / (wsum + 1e-20f) * scaling;
-    }
-  }
+  route_topk_warp<NPL>(rlog + (size_t)layer * n, gate_b ? gate_b + (size_t)layer * bias_stride : nullptr,
+                       ids + (size_t)layer * top_k, w + (size_t)layer * top_k, n, top_k, scaling,
+                       bad_pick);
 }
 
 // ------------------------------------------------------------- device LRU

@@ -1,7 +1,8 @@
-// bf16_gemv.cu -- BF16 dense GEMV for the hybrid's non-expert projections,
+// bf16_gemv.cu -- dense GEMVs: BF16 for the hybrid's non-expert projections,
 // bit-exact to the reference's gemv_bf16 (kennydd001/ervf
 // src/moe_lab/lightningstream_nemotron/gpu_kernels.py:21-49) for every column
-// of a batch of up to 8 activation vectors.
+// of a batch of up to 8 activation vectors; FP32 for the MoE router
+// (gemv_f32, gpu_kernels.py:51-74), alone or fused with the top-k router.
 //
 // Reference arithmetic: thread t of a 256-thread block walks k = t, t+256, ...
 // with acc = fmaf(bf16_to_f32(W[row,k]), x[k], acc); the 256 chains are
@@ -15,6 +16,7 @@
 // three are in registers; the group sums are combined across lanes 0,4,..,28.
 #include "common.cuh"
 #include "kernels.h"
+#include "route.cuh"
 
 namespace ervf {
 
@@ -97,7 +99,122 @@ __global__ void __launch_bounds__(256) bf16_gemv_kernel(const uint16_t* __restri
   }
 }
 
+// gemv_f32 (gpu_kernels.py:51-74): the same 256-chain walk, warp butterfly
+// and legacy combine as gemv_bf16 with fp32 weights.  One warp per row; lane
+// c owns chains 8c..8c+7 (two 128-bit loads per round).  Row sum in lane 0.
+__device__ __forceinline__ float f32_row(const float* __restrict__ wr, const float* __restrict__ x,
+                                         int cols, int lane) {
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+  const int nfull = cols >> 8;
+#pragma unroll 4
+  for (int i = 0; i < nfull; ++i) {
+    const int k = 256 * i + 8 * lane;
+    const float4 w0 = __ldcs(reinterpret_cast<const float4*>(wr + k));
+    const float4 w1 = __ldcs(reinterpret_cast<const float4*>(wr + k + 4));
+    const float4 x0 = __ldcg(reinterpret_cast<const float4*>(x + k));
+    const float4 x1 = __ldcg(reinterpret_cast<const float4*>(x + k + 4));
+    const float2 a01 = fma2(make_float2(w0.x, w0.y), make_float2(x0.x, x0.y), make_float2(acc[0], acc[1]));
+    const float2 a23 = fma2(make_float2(w0.z, w0.w), make_float2(x0.z, x0.w), make_float2(acc[2], acc[3]));
+    const float2 a45 = fma2(make_float2(w1.x, w1.y), make_float2(x1.x, x1.y), make_float2(acc[4], acc[5]));
+    const float2 a67 = fma2(make_float2(w1.z, w1.w), make_float2(x1.z, x1.w), make_float2(acc[6], acc[7]));
+    acc[0] = a01.x; acc[1] = a01.y; acc[2] = a23.x; acc[3] = a23.y;
+    acc[4] = a45.x; acc[5] = a45.y; acc[6] = a67.x; acc[7] = a67.y;
+  }
+  {
+    const int k = 256 * nfull + 8 * lane;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (k + j < cols) acc[j] = fmaf(wr[k + j], __ldcg(x + k + j), acc[j]);
+  }
+  return row_tree(acc);
+}
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(256) f32_gemv_kernel(const float* __restrict__ W,
+                                                       const float* __restrict__ x,
+                                                       float* __restrict__ out, int rows, int cols) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= rows) return;
+  const float s = f32_row(W + (size_t)row * cols, x, cols, lane);
+  if (lane == 0) out[row] = s;
+}
+
+// Router of one MoE layer in one launch: rlog = gemv_f32(gate_w, x) (one
+// warp per expert, kRouterWarps experts per CTA so that the 1.4 MB of router
+// weights spread over many SMs: the up launch that follows cannot start
+// streaming its experts before the ids exist), then the last CTA to finish
+// (counter, left zero) runs route_topk_f32 on rlog with one warp.  x may
+// come from the previous kernel on the stream (PDL-safe: it waits before
+// reading x).
+constexpr int kRouterWarps = 2;
+
+template <int NPL>
+__global__ void __launch_bounds__(32 * kRouterWarps) route_gemv_topk_kernel(
+    const float* __restrict__ W, const float* __restrict__ x, float* rlog,
+    const float* __restrict__ gate_b, int* __restrict__ ids, float* __restrict__ w, int n,
+    int cols, int top_k, float scaling, int bad_pick, unsigned* counter) {
+  __shared__ int last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRouterWarps + warp;
+  pdl_wait();
+  pdl_launch();
+  if (row < n) {
+    const float s = f32_row(W + (size_t)row * cols, x, cols, lane);
+    if (lane == 0) {
+      rlog[row] = s;
+      __threadfence();
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (warp == 0) route_topk_warp<NPL>(rlog, gate_b, ids, w, n, top_k, scaling, bad_pick);
+  if (threadIdx.x == 0) *counter = 0u;
+}
+
 }  // namespace
+
+int launch_f32_gemv(const float* W, const float* x, float* out, int rows, int cols,
+                    cudaStream_t stream) {
+  f32_gemv_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(W, x, out, rows, cols);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int launch_route_gemv_topk(const float* W, const float* x, float* rlog, const float* gate_b, int* ids,
+                           float* w, int n, int cols, int top_k, float scaling, int bad_pick,
+                           unsigned* counter, bool pdl, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((n + kRouterWarps - 1) / kRouterWarps);
+  cfg.blockDim = dim3(32 * kRouterWarps);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e;
+  if (n <= 128) {
+    e = cudaLaunchKernelEx(&cfg, route_gemv_topk_kernel<4>, W, x, rlog, gate_b, ids, w, n, cols, top_k,
+                           scaling, bad_pick, counter);
+  } else {
+    e = cudaLaunchKernelEx(&cfg, route_gemv_topk_kernel<8>, W, x, rlog, gate_b, ids, w, n, cols, top_k,
+                           scaling, bad_pick, counter);
+  }
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return kErrLaunch;
+  }
+  return kOk;
+}
 
 int launch_bf16_gemv(const uint16_t* W, const float* x, float* out, int rows, int cols, int batch,
                      cudaStream_t stream) {

@@ -674,6 +674,26 @@ int ervf_ep_exchange_route_sum(const uint64_t* peers, int nranks, int rank, int 
   return launch_ep_exchange_sum(a, (flags & ERVF_LAUNCH_PDL) != 0, S(stream));
 }
 
+int ervf_f32_gemv(const float* W, const float* x, float* out, int rows, int cols, void* stream) {
+  if (!W || !x || !out) return kErrNull;
+  if (rows <= 0 || cols <= 0 || cols % 4) return kErrShape;
+  if (!al(W, 16) || !al(x, 16) || !al(out, 4)) return kErrAlign;
+  return launch_f32_gemv(W, x, out, rows, cols, S(stream));
+}
+
+int ervf_route_gemv_topk(const float* gate_w, const float* x, float* rlog, const float* gate_b,
+                         int32_t* ids, float* w, int n, int hidden, int top_k, float scaling,
+                         int bad_pick, int32_t* counter, int flags, void* stream) {
+  if (!gate_w || !x || !rlog || !ids || !w || !counter) return kErrNull;
+  if (n <= 0 || n > 256 || hidden <= 0 || hidden % 4 || top_k <= 0 || top_k > 64 || top_k > n)
+    return kErrShape;
+  if (flags & ~ERVF_LAUNCH_PDL) return kErrArg;
+  if (!al(gate_w, 16) || !al(x, 16) || !al(rlog, 4) || !al(counter, 4)) return kErrAlign;
+  return launch_route_gemv_topk(gate_w, x, rlog, gate_b, ids, w, n, hidden, top_k, scaling, bad_pick,
+                                reinterpret_cast<unsigned*>(counter), (flags & ERVF_LAUNCH_PDL) != 0,
+                                S(stream));
+}
+
 int ervf_cache_assign(int32_t* slot_of, int32_t* expert_of, int32_t* last_used, int32_t* state2,
                       const int32_t* ids, int32_t* slots, int32_t* need, int32_t* stats2, int cap,
                       int top_k, void* stream) {

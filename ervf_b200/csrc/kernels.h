@@ -151,6 +151,14 @@ int launch_bf16_gemm_tc(const uint16_t* W, const float* x, float* out, int rows,
 int launch_bf16_gemv(const uint16_t* W, const float* x, float* out, int rows, int cols,
                      int batch, cudaStream_t stream);
 
+// FP32 GEMV (gemv_f32 semantics) and the fused router GEMV + sigmoid top-k
+// (counter: zero before, left zero).  n <= 256 experts.
+int launch_f32_gemv(const float* W, const float* x, float* out, int rows, int cols,
+                    cudaStream_t stream);
+int launch_route_gemv_topk(const float* W, const float* x, float* rlog, const float* gate_b, int* ids,
+                           float* w, int n, int cols, int top_k, float scaling, int bad_pick,
+                           unsigned* counter, bool pdl, cudaStream_t stream);
+
 int launch_weighted_accumulate(float* dst, const float* src, float weight, const float* w_ptr,
                                int n, cudaStream_t stream);
 

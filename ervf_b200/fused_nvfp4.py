@@ -165,6 +165,20 @@ class FusedNVFP4:
         _lib.call("ervf_route_topk", ptr(rlog), ptr(gate_b), ptr(ids), ptr(w), int(n),
                   int(top_k), float(np.float32(scaling)), int(bad_pick), self._s())
 
+    def route_gemv_topk(self, rlog, gate_w, x, gate_b, ids, w, n: int, hidden: int, top_k: int,
+                        scaling: float, bad_pick: int = 0, counter=None, flags: int = 0) -> None:
+        """The reference's ``mv_f32(rlog, gate_w, x)`` + ``route_topk`` pair
+        (runtime.py:710-713) in one launch, same rlog / ids / w bit for bit.
+        ``counter``: a zero int32 device word (one owned by this object by
+        default; every call leaves it zero)."""
+        if counter is None:
+            if getattr(self, "_rcounter", None) is None:
+                self._rcounter = torch.zeros(1, dtype=torch.int32, device=self.device)
+            counter = self._rcounter
+        _lib.call("ervf_route_gemv_topk", ptr(gate_w), ptr(x), ptr(rlog), ptr(gate_b), ptr(ids),
+                  ptr(w), int(n), int(hidden), int(top_k), float(np.float32(scaling)),
+                  int(bad_pick), ptr(counter), int(flags), self._s())
+
     def cache_assign(self, dev, ids, cap: int, top_k: int) -> None:
         _lib.call("ervf_cache_assign", ptr(dev["slot_of"]), ptr(dev["expert_of"]),
                   ptr(dev["last_used"]), ptr(dev["state2"]), ptr(ids), ptr(dev["slots"]),

@@ -1,8 +1,9 @@
-"""``GPUKernels.mv_bf16`` -- the BF16 dense GEMV of the reference's kernel
-wrapper (kennydd001/ervf src/moe_lab/lightningstream_nemotron/
-gpu_kernels.py:1549-1551) on the B200 C ABI, plus a batched form.
+"""``GPUKernels.mv_bf16`` / ``mv_f32`` -- the BF16 dense GEMV and the FP32
+router GEMV of the reference's kernel wrapper (kennydd001/ervf
+src/moe_lab/lightningstream_nemotron/gpu_kernels.py:1549-1555) on the B200 C
+ABI, plus a batched BF16 form.
 
-Only the GEMV that lies on the expert-decode path is provided; the
+Only the GEMVs that lie on the expert-decode path are provided; the
 reference's attention / Mamba / norm kernels are out of scope.
 """
 
@@ -48,3 +49,11 @@ class GPUKernels:
         _need(x, batch * cols, "x")
         _lib.call("ervf_bf16_gemv", ptr(W), ptr(x), ptr(out), int(rows), int(cols), int(batch),
                   self._s())
+
+    def mv_f32(self, out, W, x, rows: int, cols: int) -> None:
+        """out[rows] = fp32 W[rows, cols] @ x[cols], bit-exact to the
+        reference's gemv_f32 (the router projection, gpu_kernels.py:51-74)."""
+        _need(out, rows, "out")
+        _need(W, rows * cols, "W")
+        _need(x, cols, "x")
+        _lib.call("ervf_f32_gemv", ptr(W), ptr(x), ptr(out), int(rows), int(cols), self._s())

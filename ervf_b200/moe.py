@@ -275,6 +275,37 @@ class MoEDecoder:
             cur = nxt
         return cur
 
+    def step_with_router(self, x_in: torch.Tensor, gate_w: torch.Tensor,
+                         gate_b: torch.Tensor | None = None) -> torch.Tensor:
+        """One decode token through all layers with the router on the device
+        between them: per layer one launch computes the router logits from
+        the current hidden state (gate_w f32[L][E][hidden], the reference's
+        mv_f32) and routes them (route_topk, gate_b f32[L][E] or None), then
+        the grouped up and down launches follow -- the reference's per-layer
+        mv_f32 + route_topk + experts sequence (runtime.py:705-746), single
+        GPU, PDL-chained.  Returns the buffer holding x after the last layer."""
+        b, f, k = self.bank, self.fused, self.top_k
+        if self.ep_ranks != 1:
+            raise ValueError("step_with_router runs on one GPU")
+        if getattr(self, "rlog", None) is None:
+            self.rlog = torch.zeros(b.n_experts, dtype=torch.float32, device=b.device)
+        pdl = _lib.LAUNCH_PDL if self.pdl else 0
+        cur = x_in
+        for l in range(b.n_layers):
+            nxt = self.xs[l & 1]
+            ids, w = self.ids[l], self.w[l]
+            f.route_gemv_topk(self.rlog, gate_w[l], cur, None if gate_b is None else gate_b[l], ids,
+                              w, b.n_experts, b.hidden, k, self.scaling, flags=pdl)
+            # the router launch directly precedes the up launch: up waits
+            # before reading ids; down may read them early
+            f.moe_up_grouped(b.up_codes[l], b.up_scales[l], b.up_code_bytes, b.up_scale_bytes, ids,
+                             b.globals[l], k, cur, self.act, b.inter, b.hidden, flags=pdl)
+            f.moe_down_routesum(b.dn_codes[l], b.dn_scales[l], b.dn_code_bytes, b.dn_scale_bytes,
+                                ids, b.globals[l], w, k, self.act, nxt, b.hidden, b.inter, resid=cur,
+                                flags=pdl | (_lib.LAUNCH_IDS_READY if self.pdl else 0))
+            cur = nxt
+        return cur
+
     def step(self, x_in: torch.Tensor, rlogs: torch.Tensor) -> torch.Tensor:
         """One decode token through all layers; rlogs f32[L][E] are the
         router logits of every layer.  Returns the buffer holding x after

@@ -280,6 +280,26 @@ ERVF_API int ervf_panel_major(const uint8_t* codes, const uint8_t* scales, uint8
 ERVF_API int ervf_bf16_gemv(const uint16_t* W, const float* x, float* out, int rows, int cols, int batch,
                    void* stream);
 
+/* FP32 GEMV out[r] = sum_k W[r][k] * x[k], bit-exact to the reference's
+ * gemv_f32 at its default 256-thread block (gpu_kernels.py:51-74) and
+ * GPUKernels.mv_f32 (gpu_kernels.py:1553-1555): the router projection.
+ * cols % 4 == 0; W and x 16-byte aligned. */
+ERVF_API int ervf_f32_gemv(const float* W, const float* x, float* out, int rows, int cols,
+                           void* stream);
+
+/* The MoE router of one layer in one launch: rlog = gemv_f32(gate_w, x)
+ * (gate_w f32[n][hidden]) followed by route_topk_f32 on rlog -- the
+ * reference's mv_f32 + route_topk pair (runtime.py:710-713,
+ * gpu_kernels.py:51-74, fused_nvfp4.py:433-465), same rlog, ids and w bit for
+ * bit.  The last CTA to finish its experts routes; counter is one int32, zero
+ * before the first call and left zero.  flags: ERVF_LAUNCH_PDL (x may be the
+ * output of the previous kernel on the stream).  n <= 256, top_k <= 64,
+ * hidden % 4 == 0. */
+ERVF_API int ervf_route_gemv_topk(const float* gate_w, const float* x, float* rlog,
+                                  const float* gate_b, int32_t* ids, float* w, int n, int hidden,
+                                  int top_k, float scaling, int bad_pick, int32_t* counter,
+                                  int flags, void* stream);
+
 /* Device router head: replaces route_topk_f32 / FusedNVFP4.route_topk
  * (fused_nvfp4.py:433-465, :797-801).  n <= 1024, top_k <= 64. */
 ERVF_API int ervf_route_topk(const float* rlog, const float* gate_b, int32_t* ids, float* w, int n,

@@ -13,7 +13,7 @@ reference tree itself is only needed here.
 Sources used:
   src/moe_lab/lightningstream_nemotron/fused_nvfp4.py        _KERNEL_SOURCE
   scripts/nervf_nemotron/nervf01_geometry_audit.py           _ERVF_TEMPLATE (W = 4, 8, 32)
-  src/moe_lab/lightningstream_nemotron/gpu_kernels.py        _SOURCE (gemv_bf16)
+  src/moe_lab/lightningstream_nemotron/gpu_kernels.py        _SOURCE (gemv_bf16, gemv_f32)
 """
 
 from __future__ import annotations

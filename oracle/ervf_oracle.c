@@ -17,6 +17,7 @@
  *                      (gemv_down_masked_partial), :408-419 (reduce_partials);
  *                      panel-major layout runtime.py:34-52
  *   - BF16 GEMV:       gpu_kernels.py:21-49 (gemv_bf16)
+ *   - FP32 GEMV:       gpu_kernels.py:51-74 (gemv_f32, the router projection)
  *   - device router:   fused_nvfp4.py:433-465 (route_topk_f32)
  *   - device LRU:      fused_nvfp4.py:470-511 (cache_assign)
  *
@@ -274,6 +275,22 @@ ORACLE_API void oracle_bf16_gemv(const uint16_t *W, const float *x, float *out,
             }
             out[(size_t)b * rows + r] = tree256(a, ORACLE_TREE_LEGACY);
         }
+    }
+}
+
+/* gemv_f32 (gpu_kernels.py:51-74), 256-thread block: thread t walks
+ * k = t, t+256, ... with fmaf, then the same legacy tree as gemv_bf16. */
+ORACLE_API void oracle_f32_gemv(const float *W, const float *x, float *out, int rows, int cols)
+{
+    float a[256];
+    for (int r = 0; r < rows; ++r) {
+        const float *wr = W + (size_t)r * cols;
+        for (int t = 0; t < 256; ++t) {
+            float acc = 0.0f;
+            for (int k = t; k < cols; k += 256) acc = fmaf(wr[k], x[k], acc);
+            a[t] = acc;
+        }
+        out[r] = tree256(a, ORACLE_TREE_LEGACY);
     }
 }
 

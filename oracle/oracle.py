@@ -67,6 +67,7 @@ def lib():
                                          ctypes.c_int, ctypes.c_int]
         L.oracle_bf16_gemv.argtypes = [_u16p, _f32p, _f32p, ctypes.c_int, ctypes.c_int,
                                        ctypes.c_int]
+        L.oracle_f32_gemv.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int]
         L.oracle_route_topk.argtypes = [_f32p, _f32p, _i32p, _f32p, ctypes.c_int,
                                         ctypes.c_int, ctypes.c_float, ctypes.c_int]
         L.oracle_cache_assign.argtypes = [_i32p] * 8 + [ctypes.c_int, ctypes.c_int]
@@ -161,6 +162,14 @@ def bf16_gemv(W_u16, x, rows, cols, batch=1) -> np.ndarray:
     out = np.zeros(batch * rows, np.float32)
     lib().oracle_bf16_gemv(_p(W, _u16p), _p(x, _f32p), _p(out, _f32p), rows, cols, batch)
     return out.reshape(batch, rows)
+
+
+def f32_gemv(W, x, rows, cols) -> np.ndarray:
+    """gemv_f32 (gpu_kernels.py:51-74) at the reference's 256-thread block."""
+    W, x = _f32(W), _f32(x)
+    out = np.zeros(rows, np.float32)
+    lib().oracle_f32_gemv(_p(W, _f32p), _p(x, _f32p), _p(out, _f32p), rows, cols)
+    return out
 
 
 def route_topk(rlog, gate_b, top_k, scaling=1.0, bad_pick=0):

@@ -27,6 +27,7 @@ SIGS = {
     "ref_route_topk": [_vp, _vp, _vp, _vp, _i, _i, _f, _i, _vp],
     "ref_cache_assign": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp],
     "ref_gemv_bf16": [_vp, _vp, _vp, _i, _i, _vp],
+    "ref_gemv_f32": [_vp, _vp, _vp, _i, _i, _vp],
 }
 
 _lib = None

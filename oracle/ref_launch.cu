@@ -15,6 +15,7 @@
 //   route_topk_f32       fused_nvfp4.py:797-801
 //   cache_assign         fused_nvfp4.py:803-808
 //   gemv_bf16            gpu_kernels.py:1549-1551
+//   gemv_f32             gpu_kernels.py:1553-1555
 // Only tests/ and bench.py's reference leg load this library.
 #include <cuda_runtime.h>
 #include <stddef.h>
@@ -110,6 +111,12 @@ REF_API int REF_LAUNCH_NAME(const unsigned char* codes, const unsigned char* sca
 REF_API int ref_gemv_bf16(const unsigned short* W, const float* x, float* out, int rows, int cols,
                           void* stream) {
   gemv_bf16<<<rows, 256, cols * 4, (cudaStream_t)stream>>>(W, x, out, rows, cols);
+  return ref_status();
+}
+
+REF_API int ref_gemv_f32(const float* W, const float* x, float* out, int rows, int cols,
+                         void* stream) {
+  gemv_f32<<<rows, 256, cols * 4, (cudaStream_t)stream>>>(W, x, out, rows, cols);
   return ref_status();
 }
 #endif

@@ -53,6 +53,44 @@ def test_route_topk_matches_oracle(fused, oracle, cuda):
         np.testing.assert_allclose(w.cpu().numpy(), ow, rtol=3e-7)
 
 
+@pytest.mark.parametrize("n,hidden,k,bias,bad", [(128, 2688, 6, False, 0), (128, 2688, 6, True, 1),
+                                                 (200, 1024, 8, True, 0), (33, 64, 3, False, 0)])
+def test_route_gemv_topk_matches_oracle(fused, oracle, cuda, n, hidden, k, bias, bad):
+    """Router projection (gemv_f32) + sigmoid top-k in one launch equals the
+    reference pair mv_f32 + route_topk (runtime.py:710-713): rlog, ids and
+    weights bit for bit, over repeated calls (the counter stays zero)."""
+    from ervf_b200 import _lib
+
+    r = np.random.default_rng(n + hidden + k)
+    gw = r.standard_normal((n, hidden)).astype(np.float32) * 0.05
+    gb = (r.standard_normal(n).astype(np.float32) * 0.1) if bias else None
+    gwd = _t(gw, cuda)
+    gbd = _t(gb, cuda) if bias else None
+    for call in range(3):
+        x = r.standard_normal(hidden).astype(np.float32)
+        rlog = torch.zeros(n, device=cuda)
+        ids = torch.zeros(k, dtype=torch.int32, device=cuda)
+        w = torch.zeros(k, device=cuda)
+        fused.route_gemv_topk(rlog, gwd, _t(x, cuda), gbd, ids, w, n, hidden, k, 1.5, bad_pick=bad,
+                              flags=_lib.LAUNCH_PDL if call == 2 else 0)
+        torch.cuda.synchronize()
+        want_log = oracle.f32_gemv(gw, x, n, hidden)
+        oid, ow = oracle.route_topk(want_log, gb if bias else np.zeros(n, np.float32), k, 1.5, bad)
+        assert bits_equal(rlog.cpu().numpy(), want_log)
+        assert np.array_equal(ids.cpu().numpy(), oid)
+        # the weights use CUDA expf (the oracle's libm expf may differ by an
+        # ulp): within tolerance of the oracle, bit-equal to the standalone
+        # device router on the same logits
+        np.testing.assert_allclose(w.cpu().numpy(), ow, rtol=3e-7)
+        ids1 = torch.zeros(k, dtype=torch.int32, device=cuda)
+        w1 = torch.zeros(k, device=cuda)
+        fused.route_topk(rlog, gbd if bias else torch.zeros(n, device=cuda), ids1, w1, n, k, 1.5,
+                         bad_pick=bad)
+        torch.cuda.synchronize()
+        assert torch.equal(ids1, ids) and torch.equal(w1.view(torch.int32), w.view(torch.int32))
+    assert int(fused._rcounter.item()) == 0
+
+
 def test_route_topk_batched_matches_per_layer(fused, oracle, cuda):
     r = np.random.default_rng(12)
     for n, k in ((128, 6), (128, 8), (200, 6), (512, 4)):

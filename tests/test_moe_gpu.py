@@ -135,6 +135,56 @@ def test_decoder_step_pdl_chain_matches_oracle(fused, oracle, bank, cuda):
         assert bits_equal(y.cpu().numpy(), want), (use_graph, persistent)
 
 
+def test_decoder_step_with_router_matches_oracle(fused, oracle, bank, cuda):
+    """Three layers with the router on the device between them (router GEMV +
+    top-k, up, down + routed sum per layer, PDL-chained, eager and in a CUDA
+    graph) equal the oracle's recurrence x <- x + moe(x) with
+    ids, w = route_topk(gemv_f32(gate_w, x))."""
+    from ervf_b200.moe import ExpertBank, MoEDecoder
+
+    L, E, k = 3, 8, 6
+    eb = ExpertBank(L, E, HIDDEN, INTER, cuda)
+    for l in range(L):
+        for e in range(E):
+            eb.upload_expert(l, e, bank["ups"][(e + l) % E], bank["dns"][(e + 2 * l) % E])
+    dec = MoEDecoder(eb, k)
+    r = np.random.default_rng(23)
+    gw = r.standard_normal((L, E, HIDDEN)).astype(np.float32) * 0.05
+    gb = r.standard_normal((L, E)).astype(np.float32) * 0.1
+    x = x_regime(HIDDEN, "bf16", seed=29)
+    xd, gwd, gbd = _t(x, cuda), _t(gw, cuda), _t(gb, cuda)
+    want = x.copy()
+    for l in range(L):
+        rlog = oracle.f32_gemv(gw[l], want, E, HIDDEN)
+        oid, _ = oracle.route_topk(rlog, gb[l], k)
+        # routing weights with CUDA expf (the standalone device router on the
+        # oracle's logits), so that the expert sums compare bit for bit
+        ids_d = torch.zeros(k, dtype=torch.int32, device=cuda)
+        w_d = torch.zeros(k, device=cuda)
+        fused.route_topk(_t(rlog, cuda), gbd[l], ids_d, w_d, E, k, 1.0)
+        torch.cuda.synchronize()
+        ids, w = ids_d.cpu().numpy(), w_d.cpu().numpy()
+        assert np.array_equal(ids, oid)
+        experts = {e: (*bank["ups"][(e + l) % E], *bank["dns"][(e + 2 * l) % E]) for e in range(E)}
+        want = (want + oracle.moe_block(want, experts, ids, w, HIDDEN, INTER)).astype(np.float32)
+    for use_graph in (False, True):
+        dec.xbuf.fill_(float("nan"))
+        if use_graph:
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                dec.step_with_router(xd, gwd, gbd)
+            torch.cuda.current_stream().wait_stream(s)
+            with torch.cuda.graph(g):
+                y = dec.step_with_router(xd, gwd, gbd)
+            g.replay()
+        else:
+            y = dec.step_with_router(xd, gwd, gbd)
+        torch.cuda.synchronize()
+        assert bits_equal(y.cpu().numpy(), want), use_graph
+
+
 def test_routesum_residual_matches_f64(fused, oracle, bank, cuda):
     """x + moe(x) against a float64 dequant reference (tolerance, not bits)."""
     from ervf_b200.formats import dequantize

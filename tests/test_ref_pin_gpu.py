@@ -80,6 +80,30 @@ def test_bf16_oracle_equals_reference(ref, oracle, cuda):
     assert bits_equal(out.cpu().numpy(), oracle.bf16_gemv(W, x, rows, cols)[0])
 
 
+def test_f32_oracle_equals_reference(ref, oracle, cuda):
+    """The router projection: the oracle's gemv_f32 restatement against the
+    reference's own gemv_f32 kernel (gpu_kernels.py:51-74), and the library's
+    fused router against both."""
+    from ervf_b200 import FusedNVFP4, GPUKernels
+
+    for rows, cols, seed in ((128, 2688, 5), (37, 1000, 6)):
+        r = np.random.default_rng(seed)
+        W = r.standard_normal((rows, cols)).astype(np.float32) * 0.02
+        x = r.standard_normal(cols).astype(np.float32)
+        out = torch.zeros(rows, device=cuda)
+        Wd, xd = _t(W, cuda), _t(x, cuda)
+        ref.call("ref_gemv_f32", Wd.data_ptr(), xd.data_ptr(), out.data_ptr(),
+                 rows, cols, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        want = oracle.f32_gemv(W, x, rows, cols)
+        assert bits_equal(out.cpu().numpy(), want)
+        if cols % 4 == 0:
+            mine = torch.zeros(rows, device=cuda)
+            GPUKernels(device=cuda).mv_f32(mine, Wd, xd, rows, cols)
+            torch.cuda.synchronize()
+            assert bits_equal(mine.cpu().numpy(), want)
+
+
 def test_masked_down_oracle_equals_reference(ref, fused, oracle, cuda):
     hidden, inter = 2688, 1856
     codes, scales, g = random_nvfp4(hidden, inter, seed=12)
