@@ -104,7 +104,8 @@ class PeerExchange:
 def exchange_buffer(layer: int, n_layers: int) -> int:
     """Slot buffer of a layer: consecutive exchanges (the wrap from the last
     layer of one step to layer 0 of the next included) use different
-    buffers -- alternate 0 / 1, and the last layer of an odd count takes 2."""
+    buffers -- alternate 0 / 1, and the last layer of an odd count takes 2.
+    Needs n_layers >= 2."""
     if n_layers % 2 == 1 and layer == n_layers - 1:
         return 2
     return layer & 1

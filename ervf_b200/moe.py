@@ -144,6 +144,11 @@ class MoEDecoder:
         elif ep_ranks > 1:
             from .ep import PeerExchange
 
+            if L < 2:
+                # one layer would reuse one slot buffer in consecutive steps
+                raise ValueError("the peer-memory exchange needs at least two MoE layers; "
+                                 "use exchange='nccl'")
+
             self.xchg = PeerExchange(group, ep_ranks, ep_rank, bank.hidden, k, d)
         self.graph = None
         self.pdl = True

@@ -131,3 +131,16 @@ def test_dead_rank_is_detected_by_collective_timeout(oracle):
     assert codes[1] == 3
     status, msg = res.get(0, ("missing", ""))
     assert status == "error", (status, msg)
+
+
+@pytest.mark.parametrize("layers", [1, 2, 3, 5, 24, 25])
+def test_exchange_buffers_never_repeat_back_to_back(layers):
+    """Two consecutive exchanges (the step boundary included) never share a
+    slot buffer: a rank may run one exchange ahead of the slowest, so the
+    buffer it writes must not be the one a peer may still read."""
+    from ervf_b200.ep import exchange_buffer
+
+    seq = [exchange_buffer(l, layers) for _ in range(3) for l in range(layers)]
+    assert all(b in (0, 1, 2) for b in seq)
+    if layers > 1:  # a single layer is refused by MoEDecoder for this exchange
+        assert all(a != b for a, b in zip(seq, seq[1:]))
