@@ -257,16 +257,24 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
       }
       cp_async_commit();
     }
+    // B role, per unit: this thread's activation row (gathered once per unit
+    // in the grouped mode) and its 16-byte slot of the B tile
+    const int xn = MODE == kTcBf16 ? (bn & 7) : bn;  // kTcBf16: rows n and n + 8 share X[n]
+    const bool x_row = tid < 128 && xn < un;
+    const float* xrow = a.x;
+    if (x_row) {
+      size_t src = (size_t)xn;
+      if constexpr (MODE == kTcGrouped)
+        src = a.b_idx ? (size_t)__ldg(&a.b_idx[uoff + xn]) : (size_t)(uoff + xn);
+      xrow = a.x + src * a.cols + bc * 8;
+    }
+    const uint32_t b_slot = (uint32_t)((bn >> 3) * kTcBSBO + bc * 128 + (bn & 7) * 16);
     auto load_x = [&](int kb, float4 (&v)[2]) {
-      const int k = kb * kTcKB + bc * 8;
-      const int xn = MODE == kTcBf16 ? (bn & 7) : bn;  // kTcBf16: rows n and n + 8 share X[n]
-      if (tid < 128 && xn < un && k < a.cols) {
-        size_t src = (size_t)xn;
-        if constexpr (MODE == kTcGrouped)
-          src = a.b_idx ? (size_t)__ldg(&a.b_idx[uoff + xn]) : (size_t)(uoff + xn);
+      if (x_row && kb * kTcKB + bc * 8 < a.cols) {
         // activations may come from the previous launch: read through L2
-        v[0] = __ldcg(reinterpret_cast<const float4*>(a.x + src * a.cols + k));
-        v[1] = __ldcg(reinterpret_cast<const float4*>(a.x + src * a.cols + k + 4));
+        const float* p = xrow + kb * kTcKB;
+        v[0] = __ldcg(reinterpret_cast<const float4*>(p));
+        v[1] = __ldcg(reinterpret_cast<const float4*>(p + 4));
       } else {
         v[0] = v[1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
@@ -327,7 +335,7 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
           v = make_uint4(f32x2_to_f16x2(xv[0].x, xv[0].y), f32x2_to_f16x2(xv[0].z, xv[0].w),
                          f32x2_to_f16x2(xv[1].x, xv[1].y), f32x2_to_f16x2(xv[1].z, xv[1].w));
         }
-        *reinterpret_cast<uint4*>(sbuf + (bn >> 3) * kTcBSBO + bc * 128 + (bn & 7) * 16) = v;
+        *reinterpret_cast<uint4*>(sbuf + b_slot) = v;
       }
       if (kb + 1 < kb1) load_x(kb + 1, xv);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
