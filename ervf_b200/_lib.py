@@ -63,6 +63,10 @@ SIGNATURES: dict[str, list] = {
     "ervf_moe_batched": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _i, _i, _vp, _vp,
                          _i, _i, _vp, _sz, _vp],
     "ervf_moe_batched_scratch_bytes": [_i, _i, _i, _i],
+    "ervf_moe_batched_ex": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _i, _i, _vp,
+                            _vp, _i, _i, _i, _vp, _sz, _vp],
+    "ervf_moe_batched_ep_slots_ex": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _i, _i, _i,
+                                     _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp],
     "ervf_moe_batched_ep_slots": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _i, _i, _i,
                                   _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp],
     "ervf_ep_batch_exchange_route_sum": [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _vp,

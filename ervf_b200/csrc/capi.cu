@@ -428,8 +428,12 @@ namespace {
 struct BatchScratch {
   int *chunk_expert, *chunk_off, *chunk_n, *n_chunks, *tok_sorted, *pos;
   float *act, *contrib;
+  float* part;     // K-split partial accumulators [2][pairs][max(hidden, inter)]
+  unsigned* ucnt;  // K-split unit counters [pairs][ceil(max(hidden, inter) / 128)]
+  size_t ucnt_bytes;
   size_t bytes;
 };
+constexpr int kMaxKsplit = 2;
 BatchScratch batch_scratch(void* base, int pairs, int hidden, int inter) {
   BatchScratch b{};
   uint8_t* p = reinterpret_cast<uint8_t*>(base);
@@ -443,7 +447,12 @@ BatchScratch batch_scratch(void* base, int pairs, int hidden, int inter) {
   b.n_chunks = ip + 5 * (size_t)pairs;
   b.act = reinterpret_cast<float*>(p + ints * 4);
   b.contrib = b.act + (size_t)pairs * inter;
-  b.bytes = ints * 4 + (size_t)pairs * (inter + hidden) * 4;
+  const size_t rmax = (size_t)(hidden > inter ? hidden : inter);
+  b.part = b.contrib + (size_t)pairs * hidden;
+  b.ucnt = reinterpret_cast<unsigned*>(b.part + (size_t)kMaxKsplit * pairs * rmax);
+  b.ucnt_bytes = (size_t)pairs * ((rmax + 127) / 128) * 4;
+  b.bytes = ints * 4 + (size_t)pairs * (inter + hidden) * 4 + (size_t)kMaxKsplit * pairs * rmax * 4 +
+            b.ucnt_bytes;
   return b;
 }
 
@@ -454,7 +463,8 @@ int batch_slots(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_cod
                 size_t dn_code_stride, size_t dn_scale_stride, const float* globals,
                 const int32_t* ids, int pairs, int top_k, int n_experts, const float* x, int hidden,
                 int inter, const BatchScratch& b, float* contrib, int ep_ranks, int ep_rank,
-                cudaStream_t st) {
+                int ksplit, cudaStream_t st) {
+  if (ksplit > 1 && cudaMemsetAsync(b.ucnt, 0, b.ucnt_bytes, st) != cudaSuccess) return kErrLaunch;
   if (int e = launch_moe_batch_lists(ids, pairs, top_k, n_experts, b.chunk_expert, b.chunk_off, b.chunk_n,
                                      b.n_chunks, b.tok_sorted, b.pos, ep_ranks, ep_rank, st))
     return e;
@@ -465,6 +475,9 @@ int batch_slots(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_cod
   g.n_chunks = b.n_chunks;
   g.max_chunks = pairs;
   g.globals = globals;
+  g.ksplit = ksplit;
+  g.part = b.part;
+  g.ucnt = b.ucnt;
   // up: act[q] = relu(g_up * W_up x_token(q))^2 for sorted pair q
   g.codes = up_codes;
   g.scales = up_scales;
@@ -523,6 +536,19 @@ int ervf_moe_batched(const uint8_t* up_codes, const uint8_t* up_scales, size_t u
                      const int32_t* ids, const float* route_w, int tokens, int top_k, int n_experts,
                      const float* x, float* out, int hidden, int inter, void* scratch,
                      size_t scratch_bytes, void* stream) {
+  return ervf_moe_batched_ex(up_codes, up_scales, up_code_stride, up_scale_stride, dn_codes,
+                             dn_scales, dn_code_stride, dn_scale_stride, globals, ids, route_w,
+                             tokens, top_k, n_experts, x, out, hidden, inter, 1, scratch,
+                             scratch_bytes, stream);
+}
+
+int ervf_moe_batched_ex(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
+                        size_t up_scale_stride, const uint8_t* dn_codes, const uint8_t* dn_scales,
+                        size_t dn_code_stride, size_t dn_scale_stride, const float* globals,
+                        const int32_t* ids, const float* route_w, int tokens, int top_k,
+                        int n_experts, const float* x, float* out, int hidden, int inter,
+                        int ksplit, void* scratch, size_t scratch_bytes, void* stream) {
+  if (ksplit < 1 || ksplit > kMaxKsplit) return kErrArg;
   if (!up_codes || !up_scales || !dn_codes || !dn_scales || !globals || !ids || !route_w || !x ||
       !out || !scratch)
     return kErrNull;
@@ -535,7 +561,7 @@ int ervf_moe_batched(const uint8_t* up_codes, const uint8_t* up_scales, size_t u
   cudaStream_t st = S(stream);
   if (int e = batch_slots(up_codes, up_scales, up_code_stride, up_scale_stride, dn_codes, dn_scales,
                           dn_code_stride, dn_scale_stride, globals, ids, pairs, top_k, n_experts, x,
-                          hidden, inter, b, b.contrib, 1, 0, st))
+                          hidden, inter, b, b.contrib, 1, 0, ksplit, st))
     return e;
   return launch_moe_batch_routesum(b.contrib, b.pos, route_w, x, out, tokens, hidden, top_k, st);
 }
@@ -547,6 +573,21 @@ int ervf_moe_batched_ep_slots(const uint8_t* up_codes, const uint8_t* up_scales,
                               const int32_t* ids, int tokens, int top_k, int n_experts,
                               const float* x, float* slots, int hidden, int inter, int ep_ranks,
                               int ep_rank, void* scratch, size_t scratch_bytes, void* stream) {
+  return ervf_moe_batched_ep_slots_ex(up_codes, up_scales, up_code_stride, up_scale_stride,
+                                      dn_codes, dn_scales, dn_code_stride, dn_scale_stride, globals,
+                                      ids, tokens, top_k, n_experts, x, slots, hidden, inter,
+                                      ep_ranks, ep_rank, 1, scratch, scratch_bytes, stream);
+}
+
+int ervf_moe_batched_ep_slots_ex(const uint8_t* up_codes, const uint8_t* up_scales,
+                                 size_t up_code_stride, size_t up_scale_stride,
+                                 const uint8_t* dn_codes, const uint8_t* dn_scales,
+                                 size_t dn_code_stride, size_t dn_scale_stride,
+                                 const float* globals, const int32_t* ids, int tokens, int top_k,
+                                 int n_experts, const float* x, float* slots, int hidden,
+                                 int inter, int ep_ranks, int ep_rank, int ksplit, void* scratch,
+                                 size_t scratch_bytes, void* stream) {
+  if (ksplit < 1 || ksplit > kMaxKsplit) return kErrArg;
   if (!up_codes || !up_scales || !dn_codes || !dn_scales || !globals || !ids || !x || !slots ||
       !scratch)
     return kErrNull;
@@ -559,7 +600,7 @@ int ervf_moe_batched_ep_slots(const uint8_t* up_codes, const uint8_t* up_scales,
   const BatchScratch b = batch_scratch(scratch, tokens * top_k, hidden, inter);
   return batch_slots(up_codes, up_scales, up_code_stride, up_scale_stride, dn_codes, dn_scales,
                      dn_code_stride, dn_scale_stride, globals, ids, tokens * top_k, top_k, n_experts,
-                     x, hidden, inter, b, slots, ep_ranks, ep_rank, S(stream));
+                     x, hidden, inter, b, slots, ep_ranks, ep_rank, ksplit, S(stream));
 }
 
 int ervf_ep_batch_exchange_route_sum(const uint64_t* peers, int nranks, int rank, int buf,

@@ -139,6 +139,12 @@ struct GroupedTc {
   const int* n_chunks;
   int max_chunks;
   int relu2;
+  // K-split (1 or 2): part f32[ksplit][max_chunks][rows], ucnt u32[max_chunks *
+  // ceil(rows / 128)] zero before and left zero; results depend on ksplit
+  // (association of the partial sums), not on the grid or the arrival order
+  int ksplit;
+  float* part;
+  unsigned* ucnt;
 };
 int launch_grouped_tc(const GroupedTc& g, cudaStream_t stream);
 

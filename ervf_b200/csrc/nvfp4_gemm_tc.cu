@@ -79,6 +79,14 @@ struct TcArgs {
   size_t code_stride, scale_stride;
   const float* globals;
   int gsel, relu2, tiles;
+  // kTcGrouped K-split: unit = ((chunk, tile), split); each split writes its
+  // fp32 accumulator to part[split][pair][row]; the last of a unit's splits
+  // (counter ucnt[chunk * tiles + tile], left zero) adds them in split order,
+  // scales and stores -- deterministic, the same bits whatever the arrival
+  // order or the grid.
+  int ksplit, max_pairs;
+  float* part;
+  unsigned* ucnt;
 };
 
 // UMMA shared-memory descriptor, K-major, no swizzle (sm100 version 1).
@@ -194,6 +202,7 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
   const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
   // B role (threads < 128): batch row bn, 8-column chunk bc of the k-block
   const int bn = tid >> 3, bc = tid & 7;
+  __shared__ int s_last;
   bool dead = false;
   uint32_t gkb = 0;   // k-blocks issued by this CTA (stage ring position)
   uint32_t nacc = 0;  // accumulator commits waited for
@@ -203,11 +212,13 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
     const uint8_t* ucodes = a.codes;
     const uint8_t* uscales = a.scales;
     float ug = a.g;
+    int us = 0;  // grouped: the unit without its split
     if constexpr (MODE == kTcGrouped) {
-      const int chunk = unit / a.tiles;
+      us = unit / a.ksplit;
+      split = unit - us * a.ksplit;
+      const int chunk = us / a.tiles;
       if (chunk >= __ldg(a.n_chunks)) continue;  // uniform over the CTA
-      tile = unit - chunk * a.tiles;
-      split = 0;
+      tile = us - chunk * a.tiles;
       const int e = __ldg(&a.chunk_expert[chunk]);
       un = __ldg(&a.chunk_n[chunk]);
       uoff = __ldg(&a.chunk_off[chunk]);
@@ -219,8 +230,9 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
       split = unit - tile * a.splits;
       un = a.n;
     }
-    const int kb0 = (int)((long long)split * nkb / a.splits);
-    const int kb1 = (int)((long long)(split + 1) * nkb / a.splits);
+    const int nsplit = MODE == kTcGrouped ? a.ksplit : a.splits;
+    const int kb0 = (int)((long long)split * nkb / nsplit);
+    const int kb1 = (int)((long long)(split + 1) * nkb / nsplit);
     const int row = tile * kTcM + rr;
     const bool row_ok = row < a.rows;
     const uint8_t* crow = ucodes + (size_t)row * cb;
@@ -380,6 +392,11 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
       if (!dead && orow < a.rows) {
 #pragma unroll
         for (int j = 0; j < kTcN; ++j) {
+          if (MODE == kTcGrouped && a.ksplit > 1) {
+            if (j < un)
+              a.part[((size_t)split * a.max_pairs + uoff + j) * a.rows + orow] = __uint_as_float(v[j]);
+            continue;
+          }
           if (j < un) {
             float y = MODE == kTcBf16 ? (j < 8 ? __uint_as_float(v[j]) + __uint_as_float(v[j + 8]) : 0.0f)
                                       : __uint_as_float(v[j]) * ug;
@@ -400,6 +417,36 @@ __global__ void __launch_bounds__(kTcThreads) nvfp4_gemm_tc_kernel(TcArgs a) {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();  // the accumulator is read before the next unit's MMAs
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if constexpr (MODE == kTcGrouped) {
+      if (a.ksplit > 1) {
+        // the last split of this unit adds the partial accumulators in split
+        // order, applies the global scale (and relu^2) and stores
+        if (tid == 0) {
+          __threadfence();
+          s_last = atomicAdd(&a.ucnt[us], 1u) == (unsigned)(a.ksplit - 1);
+        }
+        __syncthreads();
+        if (s_last) {
+          __threadfence();
+          const int orow = tile * kTcM + tid;
+          if (tid < kTcM && !dead && orow < a.rows) {
+            for (int j = 0; j < un; ++j) {
+              const float* pp = a.part + (size_t)(uoff + j) * a.rows + orow;
+              float t = __ldcg(pp);
+              for (int sp = 1; sp < a.ksplit; ++sp) t += __ldcg(pp + (size_t)sp * a.max_pairs * a.rows);
+              float y = t * ug;
+              if (a.relu2) {
+                const float r = fmaxf(y, 0.0f);
+                y = r * r;
+              }
+              a.out[(size_t)(uoff + j) * a.rows + orow] = y;
+            }
+          }
+          if (tid == 0) a.ucnt[us] = 0u;
+        }
+        __syncthreads();  // s_last is rewritten for the next unit
+      }
+    }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -478,7 +525,12 @@ int launch_grouped_tc(const GroupedTc& g, cudaStream_t stream) {
   a.n = 16;
   a.splits = 1;
   a.tiles = (g.rows + kTcM - 1) / kTcM;
-  a.units = g.max_chunks * a.tiles;
+  a.ksplit = g.ksplit > 1 ? g.ksplit : 1;
+  a.max_pairs = g.max_chunks;
+  a.part = g.part;
+  a.ucnt = g.ucnt;
+  if (a.ksplit > 1 && (!a.part || !a.ucnt)) return kErrArg;
+  a.units = g.max_chunks * a.tiles * a.ksplit;
   a.chunk_expert = g.chunk_expert;
   a.chunk_off = g.chunk_off;
   a.chunk_n = g.chunk_n;

@@ -270,21 +270,23 @@ class FusedNVFP4:
     def moe_batched(self, up_codes, up_scales, up_code_stride: int, up_scale_stride: int,
                     dn_codes, dn_scales, dn_code_stride: int, dn_scale_stride: int, globals_,
                     ids, w, tokens: int, top_k: int, n_experts: int, x, out, hidden: int,
-                    inter: int, scratch=None) -> None:
+                    inter: int, scratch=None, ksplit: int = 1) -> None:
         """Expert-major batched routed-MoE block of `tokens` decode tokens on
         the tensor cores: out[t] = x[t] + sum over route slots (in order) of
-        w[t,s] * down(relu(up(x[t]))^2) with each expert read once."""
+        w[t,s] * down(relu(up(x[t]))^2) with each expert read once.
+        ``ksplit`` 2 splits the columns of every tensor-core unit over two CTAs
+        (deterministic; more parallelism for small batches or expert shards)."""
         nbytes = _lib.load().ervf_moe_batched_scratch_bytes(int(tokens), int(top_k), int(hidden),
                                                             int(inter))
         if scratch is None:
             if getattr(self, "_bscratch", None) is None or self._bscratch.numel() < nbytes:
                 self._bscratch = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
             scratch = self._bscratch
-        _lib.call("ervf_moe_batched", ptr(up_codes), ptr(up_scales), int(up_code_stride),
+        _lib.call("ervf_moe_batched_ex", ptr(up_codes), ptr(up_scales), int(up_code_stride),
                   int(up_scale_stride), ptr(dn_codes), ptr(dn_scales), int(dn_code_stride),
                   int(dn_scale_stride), ptr(globals_), ptr(ids), ptr(w), int(tokens), int(top_k),
-                  int(n_experts), ptr(x), ptr(out), int(hidden), int(inter), ptr(scratch),
-                  int(nbytes), self._s())
+                  int(n_experts), ptr(x), ptr(out), int(hidden), int(inter), int(ksplit),
+                  ptr(scratch), int(nbytes), self._s())
 
     def gemm_tc(self, out, codes, scales, x, global_scale: float, rows: int, cols: int,
                 n: int) -> None:

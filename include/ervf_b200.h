@@ -352,6 +352,22 @@ ERVF_API int ervf_moe_batched(const uint8_t* up_codes, const uint8_t* up_scales,
                               int n_experts, const float* x, float* out, int hidden, int inter,
                               void* scratch, size_t scratch_bytes, void* stream);
 
+/* ervf_moe_batched with a K-split of the tensor-core launches (ksplit 1 or
+ * 2): each (expert chunk, 128-row tile) is computed as ksplit CTAs over
+ * consecutive halves of the columns, and the last one adds the fp32 partial
+ * accumulators in split order before the global scale -- more CTAs for a
+ * small batch or a small expert shard.  Deterministic; the result depends on
+ * ksplit (association of the partial sums), not on the grid, the arrival
+ * order or the rank.  No counterpart in the reference. */
+ERVF_API int ervf_moe_batched_ex(const uint8_t* up_codes, const uint8_t* up_scales,
+                                 size_t up_code_stride, size_t up_scale_stride,
+                                 const uint8_t* dn_codes, const uint8_t* dn_scales,
+                                 size_t dn_code_stride, size_t dn_scale_stride,
+                                 const float* globals, const int32_t* ids, const float* route_w,
+                                 int tokens, int top_k, int n_experts, const float* x, float* out,
+                                 int hidden, int inter, int ksplit, void* scratch,
+                                 size_t scratch_bytes, void* stream);
+
 /* Bytes of scratch ervf_moe_batched uses. */
 ERVF_API size_t ervf_moe_batched_scratch_bytes(int tokens, int top_k, int hidden, int inter);
 
@@ -370,6 +386,16 @@ ERVF_API int ervf_moe_batched_ep_slots(const uint8_t* up_codes, const uint8_t* u
                                        int top_k, int n_experts, const float* x, float* slots,
                                        int hidden, int inter, int ep_ranks, int ep_rank,
                                        void* scratch, size_t scratch_bytes, void* stream);
+/* ervf_moe_batched_ep_slots with the K-split of ervf_moe_batched_ex. */
+ERVF_API int ervf_moe_batched_ep_slots_ex(const uint8_t* up_codes, const uint8_t* up_scales,
+                                          size_t up_code_stride, size_t up_scale_stride,
+                                          const uint8_t* dn_codes, const uint8_t* dn_scales,
+                                          size_t dn_code_stride, size_t dn_scale_stride,
+                                          const float* globals, const int32_t* ids, int tokens,
+                                          int top_k, int n_experts, const float* x, float* slots,
+                                          int hidden, int inter, int ep_ranks, int ep_rank,
+                                          int ksplit, void* scratch, size_t scratch_bytes,
+                                          void* stream);
 
 /* The batched exchange + route-order sum over NVLink peer memory, after
  * ervf_moe_batched_ep_slots on every rank with the same scratch: publishes

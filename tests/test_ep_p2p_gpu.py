@@ -112,7 +112,8 @@ def test_single_rank_exchange_matches_oracle(oracle, experts, cuda):
 def test_single_rank_batched_exchange_matches_moe_batched(fused, cuda):
     """The expert-parallel batched block as one rank (slots into the exchange
     region, then the batched exchange + route sum) equals ervf_moe_batched
-    bit for bit, through two slot buffers in turn."""
+    bit for bit, through three slot buffers in turn, without and with the
+    K-split."""
     from ervf_b200 import _lib
     from ervf_b200.moe import ExpertBank
 
@@ -125,7 +126,7 @@ def test_single_rank_batched_exchange_matches_moe_batched(fused, cuda):
         peers = torch.tensor([reg.ptr], dtype=torch.int64, device=cuda)
         nb = int(_lib.load().ervf_moe_batched_scratch_bytes(T, k, HIDDEN, INTER))
         scr = torch.empty(nb, dtype=torch.uint8, device=cuda)
-        for buf in (0, 1):
+        for buf, ks in ((0, 1), (1, 2), (2, 2)):
             x = torch.randn(T, HIDDEN, generator=g, device=cuda)
             rl = torch.randn(T, E2, generator=g, device=cuda)
             ids = torch.zeros(T, k, dtype=torch.int32, device=cuda)
@@ -134,13 +135,13 @@ def test_single_rank_batched_exchange_matches_moe_batched(fused, cuda):
             want = torch.full((T, HIDDEN), float("nan"), device=cuda)
             fused.moe_batched(eb.up_codes[0], eb.up_scales[0], eb.up_code_bytes, eb.up_scale_bytes,
                               eb.dn_codes[0], eb.dn_scales[0], eb.dn_code_bytes, eb.dn_scale_bytes,
-                              eb.globals[0], ids, w, T, k, E2, x, want, HIDDEN, INTER)
+                              eb.globals[0], ids, w, T, k, E2, x, want, HIDDEN, INTER, ksplit=ks)
             out = torch.full((T, HIDDEN), float("nan"), device=cuda)
-            _lib.call("ervf_moe_batched_ep_slots", eb.up_codes[0].data_ptr(),
+            _lib.call("ervf_moe_batched_ep_slots_ex", eb.up_codes[0].data_ptr(),
                       eb.up_scales[0].data_ptr(), eb.up_code_bytes, eb.up_scale_bytes,
                       eb.dn_codes[0].data_ptr(), eb.dn_scales[0].data_ptr(), eb.dn_code_bytes,
                       eb.dn_scale_bytes, eb.globals[0].data_ptr(), ids.data_ptr(), T, k, E2,
-                      x.data_ptr(), reg.slots(buf, T * k, HIDDEN), HIDDEN, INTER, 1, 0,
+                      x.data_ptr(), reg.slots(buf, T * k, HIDDEN), HIDDEN, INTER, 1, 0, ks,
                       scr.data_ptr(), nb, _stream(cuda))
             _lib.call("ervf_ep_batch_exchange_route_sum", peers.data_ptr(), 1, 0, buf,
                       ids.data_ptr(), w.data_ptr(), T, k, x.data_ptr(), out.data_ptr(), HIDDEN,
@@ -261,7 +262,9 @@ def _worker(rank, world, port, q):
             torch.cuda.synchronize()
             if not torch.equal(want.view(torch.int32), y.view(torch.int32)):
                 bad.append(("graph", t))
-        # the batched block (expert-major, tensor cores), odd layer count
+        # the batched block (expert-major, tensor cores), odd layer count; the
+        # same K-split on both sides (results depend on it, not on the rank)
+        one.batch_ksplit = ep.batch_ksplit
         T = 8
         xb = torch.randn(T, HIDDEN, generator=g, device=dev)
         rb = torch.randn(L, T, E, generator=g, device=dev)
