@@ -292,7 +292,7 @@ def _worker(rank, world, port, q):
 def test_multi_gpu_exchange_bit_identical_to_one_gpu():
     import torch.multiprocessing as mp
 
-    world = min(torch.cuda.device_count(), 4)
+    world = min(torch.cuda.device_count(), 8)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
