@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="only the decode-step line (no per-kernel, GEMV, batch-32 or router keys)")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel exchange of the slot outputs (N > 1)")
@@ -178,7 +180,7 @@ def kernel_roofline(dec, bank, device, hbm, iters=192):
     """Average device time of the two grouped expert kernels (a CUDA graph of
     `iters` launches each, timed with CUDA events), each launch on a
     different (layer, token) routing so that weights come from HBM."""
-    from ervf_b200.fused_nvfp4 import FusedNVFP4
+    from ervf_b200 import _lib
 
     f = dec.fused
     g = torch.Generator(device=device)
@@ -196,11 +198,11 @@ def kernel_roofline(dec, bank, device, hbm, iters=192):
         f.moe_up_grouped(bank.up_codes[l], bank.up_scales[l], bank.up_code_bytes,
                          bank.up_scale_bytes, ids[i], bank.globals[l], TOP_K, x, act, INTER, HIDDEN)
 
-    def down(i):
+    def down(i):  # the decode chain's variant: PDL launch, group-counter route sum
         l = i % L
         f.moe_down_routesum(bank.dn_codes[l], bank.dn_scales[l], bank.dn_code_bytes,
                             bank.dn_scale_bytes, ids[i], bank.globals[l], w, TOP_K, act, out,
-                            HIDDEN, INTER, resid=x)
+                            HIDDEN, INTER, resid=x, flags=_lib.LAUNCH_PDL | _lib.LAUNCH_IDS_READY)
 
     for fn in (up, down):
         for i in range(8):
@@ -229,17 +231,24 @@ def gemv_shape(device, hbm, rows=INTER, cols=HIDDEN, min_iters=64):
     from ervf_b200.formats import quantize_nvfp4_torch
 
     f = FusedNVFP4(device=device)
-    gen = torch.Generator(device=device)
-    gen.manual_seed(0)
-    codes, scales, gsc = quantize_nvfp4_torch(torch.randn(rows, cols, generator=gen,
-                                                          device=device) * 0.02)
+    if (rows, cols) == (1856, 2688):  # BASELINE config 0's exact inputs
+        from ervf_b200.formats import config0_inputs
+
+        c0, s0, g0, x0 = config0_inputs()
+        codes, scales = torch.from_numpy(c0).to(device), torch.from_numpy(s0).to(device)
+        x, gsc = torch.from_numpy(x0).to(device), g0
+    else:
+        gen = torch.Generator(device=device)
+        gen.manual_seed(0)
+        codes, scales, gsc = quantize_nvfp4_torch(torch.randn(rows, cols, generator=gen,
+                                                              device=device) * 0.02)
+        x = torch.randn(cols, device=device)
     l2 = torch.cuda.get_device_properties(device).L2_cache_size
     rec = codes.numel() + scales.numel()
     n = max(1, (8 * l2) // rec + 1) if rec < 2 * l2 else 2
     pc = codes.reshape(1, -1).repeat(n, 1)
     ps = scales.reshape(1, -1).repeat(n, 1)
     del codes, scales
-    x = torch.randn(cols, device=device)
     out = torch.zeros(rows, device=device)
     g = float(gsc)
 
@@ -395,16 +404,18 @@ def routed_decode(dec, device, hbm, steps=50):
             "frac": round(token_bytes / ms / 1e6 / hbm, 4)}
 
 
-def cpu_sample(bank, layers_sampled=2, tokens=2):
+def cpu_sample(bank, layers_sampled=4, tokens=2):
     """Reference-path CPU baseline on a bounded sample: `tokens` tokens x
-    `layers_sampled` layers of the same workload, torch FP32 dequant + matmul
-    with all host threads; extrapolated to tok/s over 24 layers."""
+    `layers_sampled` layers of the same workload (8 rounds by default), torch
+    FP32 dequant + matmul with all host threads; p50 over the rounds of one
+    layer's time (dequant + matmul = the headline, and matmul alone),
+    extrapolated to tok/s over 24 layers."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import cpu_baseline as cb
 
     cores = cb.use_all_cores()
     g = np.random.default_rng(7)
-    times = []
+    full, mm = [], []
     for t in range(tokens):
         x = torch.from_numpy(g.standard_normal(HIDDEN).astype(np.float32))
         for l in range(layers_sampled):
@@ -415,13 +426,16 @@ def cpu_sample(bank, layers_sampled=2, tokens=2):
                 experts[int(e)] = ((torch.from_numpy(uc), torch.from_numpy(us), float(ug)),
                                    (torch.from_numpy(dc), torch.from_numpy(ds), float(dg)))
             w = np.full(TOP_K, 1.0 / TOP_K, np.float32)
-            t0 = time.perf_counter()
-            x = cb.moe_layer(x, experts, ids, w, HIDDEN, INTER)
-            times.append(time.perf_counter() - t0)
-    per_layer = statistics.median(times)
+            x, t_dq, t_mm = cb.moe_layer_timed(x, experts, ids, w, HIDDEN, INTER)
+            full.append(t_dq + t_mm)
+            mm.append(t_mm)
+    per_layer = statistics.median(full)
+    per_layer_mm = statistics.median(mm)
     return {"value": 1.0 / (per_layer * N_LAYERS), "unit": UNIT, "cores": cores, "kind": "port",
+            "matmul_only_value": 1.0 / (per_layer_mm * N_LAYERS), "rounds": len(full),
             "sample": f"{tokens} tokens x {layers_sampled} of {N_LAYERS} layers (6 experts each), "
-                      f"median {per_layer * 1e3:.1f} ms/layer, extrapolated x{N_LAYERS} layers"}
+                      f"p50 of {len(full)} rounds: {per_layer * 1e3:.1f} ms/layer dequant + matmul "
+                      f"({per_layer_mm * 1e3:.1f} ms matmul only), extrapolated x{N_LAYERS} layers"}
 
 
 def reference_arm(args, rank, world):
@@ -443,16 +457,16 @@ def reference_arm(args, rank, world):
         dc, ds, dg = synthetic_nvfp4(HIDDEN, INTER, seed=500 + e)
         pool[e] = ((torch.from_numpy(uc.reshape(-1)), torch.from_numpy(us.reshape(-1)), float(ug)),
                    (torch.from_numpy(dc.reshape(-1)), torch.from_numpy(ds.reshape(-1)), float(dg)))
-    times = []
+    times, mm = [], []
     for step in range(args.warmup + args.steps):
         x = torch.from_numpy(g.standard_normal(HIDDEN).astype(np.float32))
         ids = g.choice(n_pool, TOP_K, replace=False)
         w = np.full(TOP_K, 1.0 / TOP_K, np.float32)
-        t0 = time.perf_counter()
-        cb.moe_layer(x, pool, ids, w, HIDDEN, INTER)
+        _, t_dq, t_mm = cb.moe_layer_timed(x, pool, ids, w, HIDDEN, INTER)
         if step >= args.warmup:
-            times.append(time.perf_counter() - t0)
-    per_layer = sum(times) / len(times)
+            times.append(t_dq + t_mm)
+            mm.append(t_mm)
+    per_layer = statistics.median(times)  # p50 over the K steps
     value = 1.0 / (per_layer * N_LAYERS)
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -462,8 +476,9 @@ def reference_arm(args, rank, world):
         "config": {"workload": "config4: 24 MoE layers x 128 NVFP4 experts (2688/1856), top-6, "
                                "batch 1", "parallelism": "cpu", "l2": "n/a"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": "each step: 1 token x 1 of 24 layers (6 experts, dequant + "
-                                   "matmul), extrapolated x24"},
+                         "matmul_only_value": 1.0 / (statistics.median(mm) * N_LAYERS),
+                         "sample": f"each step: 1 token x 1 of 24 layers (6 experts, dequant + "
+                                   f"matmul), p50 of {len(times)} steps, extrapolated x24"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -494,19 +509,9 @@ def main():
         return
     L = args.layers
     t0 = time.time()
-    bank = ExpertBank(L, N_EXPERTS, HIDDEN, INTER, device)
-    # every rank builds only the experts it owns (e % world == rank)
-    from ervf_b200.formats import quantize_nvfp4_torch
-
-    gen = torch.Generator(device=device)
-    for l in range(L):
-        for e in range(rank, N_EXPERTS, world):
-            recs = []
-            for off, (r, c) in ((0, (INTER, HIDDEN)), (500, (HIDDEN, INTER))):
-                gen.manual_seed(1000 * l + e + off)
-                recs.append(quantize_nvfp4_torch(torch.randn(r, c, generator=gen, device=device)
-                                                 * 0.02))
-            bank.upload_expert(l, e, recs[0], recs[1])
+    # every rank builds only the experts it owns (e % world == rank); seeds
+    # 1000 * layer + expert (+500 for down), N(0, 0.02), quantised on the device
+    bank = ExpertBank.synthetic(L, N_EXPERTS, HIDDEN, INTER, device, rank=rank, world=world)
     torch.cuda.synchronize(device)
     build_s = time.time() - t0
 
@@ -599,12 +604,13 @@ def main():
         dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
     e2e_value = args.steps / (float(e_t.item()) / 1e3)
 
-    kern = kernel_roofline(dec, bank, device, hbm) if world == 1 else None
-    gemv0 = gemv_shape(device, hbm) if (world == 1 and rank == 0) else None
-    batch32 = batched_decode(dec, device, hbm, world)
-    routed = routed_decode(dec, device, hbm) if world == 1 else None
+    full = not args.no_extras
+    kern = kernel_roofline(dec, bank, device, hbm) if (world == 1 and full) else None
+    gemv0 = gemv_shape(device, hbm) if (world == 1 and rank == 0 and full) else None
+    batch32 = batched_decode(dec, device, hbm, world) if full else None
+    routed = routed_decode(dec, device, hbm) if (world == 1 and full) else None
     extra = None
-    if world == 1 and rank == 0:
+    if world == 1 and rank == 0 and full:
         # config 2 (Qwen shapes) GEMVs and config 3 BF16 GEMVs, L2-cold
         extra = {"gemv_config2": {f"{r}x{c}": gemv_shape(device, hbm, r, c) for r, c in
                                   ((1536, 2048), (2048, 768))},
@@ -656,7 +662,7 @@ def main():
             line["batched_decode_b32"] = batch32
         if routed is not None:
             line["decode_with_device_router"] = routed
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and full:
             line["cpu_baseline"] = cpu_sample(bank)
         print(json.dumps(line), flush=True)
     if graph is not None:

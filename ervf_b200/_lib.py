@@ -55,16 +55,15 @@ SIGNATURES: dict[str, list] = {
     "ervf_moe_down_routesum": [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i,
                                _vp, _sz, _i, _i, _vp],
     "ervf_routesum_scratch_bytes": [_i, _i],
-    "ervf_moe_decode": [_vp, _sz, _sz, _sz, _sz, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _i, _vp, _sz,
-                        _vp],
-    "ervf_decode_scratch_bytes": [_i, _i],
+    "ervf_moe_layer": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i,
+                       _i, _i, _vp, _sz, _vp, _vp, _vp, _i, _vp],
     "ervf_moe_down_routesum_static": [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp,
                                       _i, _i, _i, _i, _vp],
     "ervf_moe_batched": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _i, _i, _vp, _vp,
                          _i, _i, _vp, _sz, _vp],
     "ervf_moe_batched_scratch_bytes": [_i, _i, _i, _i],
     "ervf_moe_batched_ex": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _i, _i, _vp,
-                            _vp, _i, _i, _i, _vp, _sz, _vp],
+                            _vp, _i, _i, _i, _i, _vp, _sz, _vp],
     "ervf_moe_batched_ep_slots_ex": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _i, _i, _i,
                                      _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp],
     "ervf_moe_batched_ep_slots": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _i, _i, _i,
@@ -72,7 +71,8 @@ SIGNATURES: dict[str, list] = {
     "ervf_ep_batch_exchange_route_sum": [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _vp,
                                          _sz, _i, _vp],
     "ervf_bf16_gemm_tc": [_vp, _vp, _vp, _i, _i, _i, _vp],
-    "ervf_nvfp4_gemm_tc": [_vp, _vp, _f, _vp, _vp, _i, _i, _i, _vp],
+    "ervf_nvfp4_gemm_tc": [_vp, _vp, _f, _vp, _vp, _i, _i, _i, _vp, _sz, _vp],
+    "ervf_nvfp4_gemm_tc_scratch_bytes": [_i, _i, _i],
     "ervf_route_topk_softmax": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "ervf_route_topk_batched": [_vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _vp],
     "ervf_ep_expert_slots": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _i, _vp, _vp, _vp,
@@ -90,6 +90,9 @@ SIGNATURES: dict[str, list] = {
     "ervf_down_masked_ind": [_vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp],
     "ervf_panel_major": [_vp, _vp, _vp, _i, _i, _vp],
     "ervf_bf16_gemv": [_vp, _vp, _vp, _i, _i, _i, _vp],
+    "ervf_nvfp4_gemm_rows_b": [_vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp],
+    "ervf_down_union": [_vp, _vp, _i, _vp, _vp, _f, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
+    "ervf_reduce_slots": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "ervf_route_topk": [_vp, _vp, _vp, _vp, _i, _i, _f, _i, _vp],
     "ervf_f32_gemv": [_vp, _vp, _vp, _i, _i, _vp],
     "ervf_route_gemv_topk": [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _vp, _i, _vp],
@@ -97,7 +100,7 @@ SIGNATURES: dict[str, list] = {
     "ervf_cache_fetch": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _i, _vp],
 }
 
-SIZE_RESULT = {"ervf_routesum_scratch_bytes", "ervf_decode_scratch_bytes",
+SIZE_RESULT = {"ervf_routesum_scratch_bytes", "ervf_nvfp4_gemm_tc_scratch_bytes",
                "ervf_moe_batched_scratch_bytes", "ervf_ep_region_bytes"}
 
 _lib = None

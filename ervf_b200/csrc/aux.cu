@@ -109,7 +109,11 @@ __global__ void route_topk_warp_kernel(const float* __restrict__ rlog, const flo
 //
 // cache_assign (fused_nvfp4.py:470-511): one thread walks the route slots in
 // order; hits refresh last_used, misses append while filling and then evict
-// the minimum last_used slot (lowest slot on ties).
+// the minimum last_used slot (lowest slot on ties).  This is a restatement of
+// the reference's serial state machine step for step, by contract: the
+// runtime reads the same slot / victim / stats state, so the order of every
+// update is part of the interface.  It is a compat path (the resident bank
+// needs no LRU) and is not on the timed decode path.
 __global__ void cache_assign_kernel(int* __restrict__ slot_of, int* __restrict__ expert_of,
                                     int* __restrict__ last_used, int* __restrict__ state2,
                                     const int* __restrict__ ids, int* __restrict__ slots,
@@ -216,7 +220,11 @@ __global__ void panel_scan_kernel(const float* __restrict__ act, int inter,
 // gemv_down_masked_partial + reduce_partials (fused_nvfp4.py:225-271,
 // :408-419) in one launch.  Block = 32 rows x nchunks chunks; chunk c of row
 // r accumulates active panels pi = c, c+nchunks, ... with columns ascending,
-// then the row's partials are summed in chunk order from 0.0.
+// then the row's partials are summed in chunk order from 0.0.  The inner loop
+// restates the reference's panel walk (panel stride, mask-bit order, fmaf per
+// set bit) by contract: that order is the masked down path's numeric result.
+// A compat path for the runtime's panel-major records, not on the timed
+// decode path.
 __global__ void down_masked_kernel(const uint8_t* __restrict__ bank, const float* __restrict__ act,
                                    const unsigned* __restrict__ masks, const int* __restrict__ plist,
                                    const int* __restrict__ pcount, float global_scale,
@@ -558,5 +566,62 @@ int launch_panel_major(const uint8_t* codes, const uint8_t* scales, uint8_t* blo
 }
 
 int read_aux_device_error(bool clear) { return read_unit_error(clear); }
+
+// ------------------------------------------------------ SweepMoE plumbing
+//
+// Row gather / scatter by a device index list and the batched route-order
+// slot sum of the expert-major block (sweepspec.py:244-375).
+
+namespace {
+
+// dst[b][:] = src[idx[b]][:] (cols floats each), b < n
+__global__ void gather_rows_kernel(const float* __restrict__ src, const int* __restrict__ idx, int cols,
+                                   float* __restrict__ dst) {
+  const int b = blockIdx.y;
+  const size_t row = (size_t)__ldg(&idx[b]);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < cols; i += gridDim.x * blockDim.x)
+    dst[(size_t)b * cols + i] = src[row * cols + i];
+}
+
+// dst[idx[b]][:] = src[b][:]
+__global__ void scatter_rows_kernel(const float* __restrict__ src, const int* __restrict__ idx, int cols,
+                                    float* __restrict__ dst) {
+  const int b = blockIdx.y;
+  const size_t row = (size_t)__ldg(&idx[b]);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < cols; i += gridDim.x * blockDim.x)
+    dst[row * cols + i] = src[(size_t)b * cols + i];
+}
+
+// out[b][r] = fmaf(w[b][s], contrib[b][s][r], out[b][r]) for s = 0..top_k-1
+// in route-slot order, starting from out's value (reduce_slots,
+// sweepspec.py:219-240: the per-node order of the token-major path).
+__global__ void reduce_slots_kernel(const float* __restrict__ contrib, const float* __restrict__ w,
+                                    float* __restrict__ out, int rows, int top_k) {
+  const int b = blockIdx.y;
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  float a = out[(size_t)b * rows + r];
+  for (int s = 0; s < top_k; ++s)
+    a = fmaf(__ldg(&w[b * top_k + s]), contrib[((size_t)b * top_k + s) * rows + r], a);
+  out[(size_t)b * rows + r] = a;
+}
+
+}  // namespace
+
+int launch_gather_rows(const float* src, const int* idx, int n, int cols, float* dst, cudaStream_t stream) {
+  gather_rows_kernel<<<dim3((cols + 1023) / 1024, n), 256, 0, stream>>>(src, idx, cols, dst);
+  return launched();
+}
+
+int launch_scatter_rows(const float* src, const int* idx, int n, int cols, float* dst, cudaStream_t stream) {
+  scatter_rows_kernel<<<dim3((cols + 1023) / 1024, n), 256, 0, stream>>>(src, idx, cols, dst);
+  return launched();
+}
+
+int launch_reduce_slots(const float* contrib, const float* w, float* out, int rows, int top_k, int B,
+                        cudaStream_t stream) {
+  reduce_slots_kernel<<<dim3((rows + 255) / 256, B), 256, 0, stream>>>(contrib, w, out, rows, top_k);
+  return launched();
+}
 
 }  // namespace ervf

@@ -45,8 +45,9 @@ int ervf_version(void) { return 100; }
 
 int ervf_device_status(void) {
   // read and clear every unit's word; report the first error found
-  const int v[4] = {read_gemv_device_error(true), read_aux_device_error(true),
-                    read_tc_device_error(true), read_ep_device_error(true)};
+  const int v[5] = {read_gemv_device_error(true), read_aux_device_error(true),
+                    read_tc_device_error(true), read_ep_device_error(true),
+                    read_mma_device_error(true)};
   for (int e : v)
     if (e) return e;
   return kOk;
@@ -199,8 +200,8 @@ int ervf_moe_down_routesum(const uint8_t* dn_codes, const uint8_t* dn_scales,
   b.resid = resid;
   b.rs_out = out;
   if (scratch) {
-    b.contrib = reinterpret_cast<float*>(scratch);
-    b.row_count = reinterpret_cast<int*>(b.contrib + (size_t)top_k * hidden);
+    b.grp_count = reinterpret_cast<unsigned*>(scratch);
+    b.contrib = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch) + routesum_counter_bytes(hidden));
   }
   b.pdl = (flags & ERVF_LAUNCH_PDL) ? 1 : 0;
   b.ids_ready = (flags & ERVF_LAUNCH_IDS_READY) ? 1 : 0;
@@ -221,45 +222,107 @@ int ervf_moe_down_routesum(const uint8_t* dn_codes, const uint8_t* dn_scales,
   return launch_nvfp4_batch(b, width, S(stream));
 }
 
-size_t ervf_decode_scratch_bytes(int hidden, int top_k) {
-  if (hidden <= 0 || top_k <= 0) return 0;
-  return ((size_t)top_k * hidden * 4 + (size_t)hidden * 4 + 15) / 16 * 16 + 16;
-}
-
-int ervf_moe_decode(const void* layer_table, size_t up_code_stride, size_t up_scale_stride,
-                    size_t dn_code_stride, size_t dn_scale_stride, const int32_t* ids,
-                    const float* route_w, int layers, int top_k, const float* x_in, float* xbuf,
-                    float* act, int hidden, int inter, void* scratch, size_t scratch_bytes,
-                    void* stream) {
-  if (!layer_table || !ids || !route_w || !x_in || !xbuf || !act || !scratch) return kErrNull;
-  if (layers <= 0 || top_k <= 0 || top_k > kMaxJobs) return kErrShape;
+int ervf_moe_layer(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
+                   size_t up_scale_stride, const uint8_t* dn_codes, const uint8_t* dn_scales,
+                   size_t dn_code_stride, size_t dn_scale_stride, const int32_t* ids,
+                   const float* globals, const float* route_w, int top_k, const float* x, float* act,
+                   float* out, int hidden, int inter, int n_experts, void* scratch,
+                   size_t scratch_bytes, const uint8_t* next_up_codes, const uint8_t* next_up_scales,
+                   const int32_t* next_ids, int flags, void* stream) {
+  if (!up_codes || !up_scales || !dn_codes || !dn_scales || !ids || !globals || !route_w || !x ||
+      !act || !out || !scratch)
+    return kErrNull;
+  if (flags & ~(ERVF_LAUNCH_PDL | ERVF_LAUNCH_IDS_READY)) return kErrArg;
+  if (top_k <= 0 || top_k > kMaxJobs || n_experts <= 0) return kErrShape;
   if (hidden <= 0 || inter <= 0 || hidden % 32 || inter % 32 || hidden > 4096 || inter > 4096)
     return kErrShape;
-  if (scratch_bytes < ervf_decode_scratch_bytes(hidden, top_k)) return kErrArg;
-  if (!al(layer_table, 8) || !al(x_in, 16) || !al(xbuf, 16) || !al(act, 16) || !al(scratch, 16))
+  if (scratch_bytes < routesum_scratch_bytes(hidden, top_k)) return kErrArg;
+  if ((next_up_codes != nullptr) != (next_ids != nullptr) ||
+      (next_up_codes != nullptr) != (next_up_scales != nullptr))
+    return kErrArg;
+  const uintptr_t ptr_bits = reinterpret_cast<uintptr_t>(up_codes) | reinterpret_cast<uintptr_t>(up_scales) |
+                             reinterpret_cast<uintptr_t>(dn_codes) | reinterpret_cast<uintptr_t>(dn_scales) |
+                             reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(act) |
+                             reinterpret_cast<uintptr_t>(scratch) |
+                             reinterpret_cast<uintptr_t>(next_up_codes) |
+                             reinterpret_cast<uintptr_t>(next_up_scales);
+  if ((ptr_bits & 15u) || ((up_code_stride | up_scale_stride | dn_code_stride | dn_scale_stride) & 15u) ||
+      !al(out, 4))
     return kErrAlign;
-  if ((up_code_stride | up_scale_stride | dn_code_stride | dn_scale_stride) & 15u) return kErrAlign;
-  DecodeArgs a{};
-  a.layers = layers;
-  a.top_k = top_k;
-  a.hidden = hidden;
-  a.inter = inter;
-  a.up_cs = up_code_stride;
-  a.up_ss = up_scale_stride;
-  a.dn_cs = dn_code_stride;
-  a.dn_ss = dn_scale_stride;
-  a.lay = reinterpret_cast<const DecodeLayer*>(layer_table);
-  a.ids = ids;
-  a.route_w = route_w;
-  a.x_in = x_in;
-  a.xb = xbuf;
-  a.act = act;
-  a.contrib = reinterpret_cast<float*>(scratch);
-  a.row_count = reinterpret_cast<int*>(a.contrib + (size_t)top_k * hidden);
-  a.grid_bar = reinterpret_cast<unsigned*>(
-      reinterpret_cast<uint8_t*>(scratch) + ((size_t)top_k * hidden * 4 + (size_t)hidden * 4 + 15) / 16 * 16);
-  if (cudaMemsetAsync(a.grid_bar, 0, sizeof(unsigned), S(stream)) != cudaSuccess) return kErrLaunch;
-  return launch_moe_decode(a, S(stream));
+  const size_t up_cb = (size_t)inter * hidden / 2, up_sb = (size_t)inter * hidden / 16;
+  const size_t dn_cb = up_cb, dn_sb = up_sb;
+  if (up_code_stride < up_cb || up_scale_stride < up_sb || dn_code_stride < dn_cb ||
+      dn_scale_stride < dn_sb)
+    return kErrArg;
+  const bool pdl = (flags & ERVF_LAUNCH_PDL) != 0;
+  GemvBatch u{};
+  u.rows = inter;
+  u.cols = hidden;
+  u.njobs = top_k;
+  u.relu2 = 1;
+  u.out_scale = 1.0f;
+  u.pdl = pdl ? 1 : 0;
+  u.ids_ready = (flags & ERVF_LAUNCH_IDS_READY) ? 1 : 0;
+  GemvBatch d{};
+  d.rows = hidden;
+  d.cols = inter;
+  d.njobs = top_k;
+  d.mode = 1;
+  d.out_scale = 1.0f;
+  d.route_w = route_w;
+  d.resid = x;
+  d.rs_out = out;
+  d.grp_count = reinterpret_cast<unsigned*>(scratch);
+  d.contrib = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch) + routesum_counter_bytes(hidden));
+  d.pdl = pdl ? 1 : 0;
+  d.ids_ready = pdl ? 1 : 0;  // the up launch read the ids after its wait
+  for (int s = 0; s < top_k; ++s) {
+    MatRef m{};
+    m.codes = up_codes;
+    m.scales = up_scales;
+    m.slot_ptr = ids + s;
+    m.id_ptr = ids + s;
+    m.globals = globals;
+    m.gsel = 1;
+    m.code_stride = up_code_stride;
+    m.scale_stride = up_scale_stride;
+    u.job[s].mat = m;
+    u.job[s].x = x;
+    u.job[s].out = act + (size_t)s * inter;
+    m.codes = dn_codes;
+    m.scales = dn_scales;
+    m.gsel = 0;
+    m.code_stride = dn_code_stride;
+    m.scale_stride = dn_scale_stride;
+    d.job[s].mat = m;
+    d.job[s].x = act + (size_t)s * inter;
+    d.job[s].out = nullptr;
+  }
+  // the up launch queues this layer's down records in L2, the down launch
+  // the next layer's up records (when given)
+  u.pf_codes = dn_codes;
+  u.pf_scales = dn_scales;
+  u.pf_code_stride = dn_code_stride;
+  u.pf_scale_stride = dn_scale_stride;
+  u.pf_code_bytes = dn_cb;
+  u.pf_scale_bytes = dn_sb;
+  u.pf_ids = ids;
+  u.pf_n = top_k;
+  u.pf_experts = n_experts;
+  if (next_ids) {
+    d.pf_codes = next_up_codes;
+    d.pf_scales = next_up_scales;
+    d.pf_code_stride = up_code_stride;
+    d.pf_scale_stride = up_scale_stride;
+    d.pf_code_bytes = up_cb;
+    d.pf_scale_bytes = up_sb;
+    d.pf_ids = next_ids;
+    d.pf_n = top_k;
+    d.pf_experts = n_experts;
+  }
+  if (!nvfp4_tma_ok(u) || !nvfp4_tma_ok(d)) return kErrShape;
+  if (int e = launch_nvfp4_batch(u, 0, S(stream))) return e;
+  return launch_nvfp4_batch(d, 0, S(stream));
 }
 
 size_t ervf_routesum_scratch_bytes(int hidden, int top_k) {
@@ -383,6 +446,54 @@ int ervf_bf16_gemv(const uint16_t* W, const float* x, float* out, int rows, int 
   return launch_bf16_gemv(W, x, out, rows, cols, batch, S(stream));
 }
 
+int ervf_nvfp4_gemm_rows_b(const uint8_t* codes, const uint8_t* scales, const float* x,
+                           const int32_t* nodes, float* out, float global_scale, int rows, int cols,
+                           int n, int apply_relu2, float* xbuf, void* stream) {
+  if (!codes || !scales || !x || !nodes || !out || !xbuf) return kErrNull;
+  if (n < 1 || n > kMaxJobs) return kErrShape;
+  if (int e = check_nvfp4_shape(rows, cols, 0)) return e;
+  if (!al(codes, 4) || !al(x, 4) || !al(out, 4) || !al(xbuf, 16)) return kErrAlign;
+  if (int e = launch_gather_rows(x, nodes, n, cols, xbuf, S(stream))) return e;
+  GemvBatch b{};
+  b.rows = rows;
+  b.cols = cols;
+  b.njobs = n;
+  b.relu2 = apply_relu2 ? 1 : 0;
+  b.out_scale = 1.0f;
+  b.legacy_tree = 1;  // the reference's batched kernel keeps gemv_nvfp4_rows' tree per column
+  for (int j = 0; j < n; ++j) {
+    b.job[j].mat = direct(codes, scales, global_scale);
+    b.job[j].x = xbuf + (size_t)j * cols;
+    b.job[j].out = out + (size_t)j * rows;
+  }
+  return launch_nvfp4_batch(b, 0, S(stream));
+}
+
+int ervf_down_union(const uint8_t* bank, const float* acts, int n, const int32_t* dst, float* contrib,
+                    float global_scale, int hidden, int inter, int nchunks, uint32_t* masks,
+                    int32_t* plist, int32_t* pcount, int32_t* nz, int32_t* nzc, float* tmp,
+                    void* stream) {
+  if (!bank || !acts || !dst || !contrib || !masks || !plist || !pcount || !nz || !nzc || !tmp)
+    return kErrNull;
+  if (n < 1 || n > 64 || hidden <= 0 || (hidden & 1) || inter <= 0 || (inter & 15) || inter > 65536)
+    return kErrShape;
+  if (nchunks <= 0 || nchunks > 32) return kErrArg;
+  for (int b = 0; b < n; ++b) {
+    if (int e = launch_down_masked(bank, acts + (size_t)b * inter, masks, plist, pcount, nz, nzc,
+                                   global_scale, nullptr, nullptr, 0, tmp + (size_t)b * hidden, hidden,
+                                   inter, nchunks, S(stream)))
+      return e;
+  }
+  return launch_scatter_rows(tmp, dst, n, hidden, contrib, S(stream));
+}
+
+int ervf_reduce_slots(const float* contrib, const float* weights, float* out, int rows, int top_k, int B,
+                      void* stream) {
+  if (!contrib || !weights || !out) return kErrNull;
+  if (rows <= 0 || top_k <= 0 || B <= 0 || B > 65535) return kErrShape;
+  return launch_reduce_slots(contrib, weights, out, rows, top_k, B, S(stream));
+}
+
 int ervf_route_topk(const float* rlog, const float* gate_b, int32_t* ids, float* w, int n,
                     int top_k, float scaling, int bad_pick, void* stream) {
   if (!rlog || !gate_b || !ids || !w) return kErrNull;
@@ -408,12 +519,45 @@ int ervf_route_topk_softmax(const float* rlog, int32_t* ids, float* w, int layer
   return launch_route_topk_softmax(rlog, ids, w, layers, n, top_k, S(stream));
 }
 
+namespace {
+constexpr int kTcMaxSplits = 4;
+struct TcScratch {
+  uint8_t* panel;
+  float* part;
+  unsigned* ucnt;
+  size_t bytes;
+};
+TcScratch tc_scratch(void* base, int rows, int cols, int n) {
+  TcScratch t{};
+  uint8_t* p = reinterpret_cast<uint8_t*>(base);
+  const size_t pan = mma_panel_bytes(1, cols);
+  const size_t part = (size_t)kTcMaxSplits * n * rows * sizeof(float);
+  const size_t cnt = ((size_t)(rows + 127) / 128 * sizeof(unsigned) + 15) / 16 * 16;
+  t.panel = p;
+  t.part = reinterpret_cast<float*>(p + pan);
+  t.ucnt = reinterpret_cast<unsigned*>(p + pan + part);
+  t.bytes = pan + part + cnt;
+  return t;
+}
+}  // namespace
+
+size_t ervf_nvfp4_gemm_tc_scratch_bytes(int rows, int cols, int n) {
+  if (rows <= 0 || cols <= 0 || n <= 0) return 0;
+  return tc_scratch(nullptr, rows, cols, n).bytes;
+}
+
 int ervf_nvfp4_gemm_tc(const uint8_t* codes, const uint8_t* scales, float global_scale,
-                       const float* x, float* out, int rows, int cols, int n, void* stream) {
-  if (!codes || !scales || !x || !out) return kErrNull;
-  if (rows <= 0 || cols <= 0 || cols % 32 || n < 1 || n > 16) return kErrShape;
-  if (!al(codes, 16) || !al(scales, 2) || !al(x, 16) || !al(out, 4)) return kErrAlign;
-  return launch_nvfp4_gemm_tc(codes, scales, global_scale, x, out, rows, cols, n, S(stream));
+                       const float* x, float* out, int rows, int cols, int n, void* scratch,
+                       size_t scratch_bytes, void* stream) {
+  if (!codes || !scales || !x || !out || !scratch) return kErrNull;
+  if (rows <= 0 || cols <= 0 || cols % 32 || cols > 4096 || n < 1 || n > 16) return kErrShape;
+  if (!al(codes, 16) || !al(scales, 16) || !al(x, 16) || !al(out, 4) || !al(scratch, 16)) return kErrAlign;
+  const TcScratch t = tc_scratch(scratch, rows, cols, n);
+  if (scratch_bytes < t.bytes) return kErrArg;
+  if (int e = launch_pack_panel(x, cols, nullptr, nullptr, nullptr, nullptr, 1, n, t.panel, S(stream)))
+    return e;
+  return launch_nvfp4_mma_single(codes, scales, global_scale, t.panel, out, rows, cols, n, t.part, t.ucnt,
+                                 kTcMaxSplits, S(stream));
 }
 
 int ervf_bf16_gemm_tc(const uint16_t* W, const float* x, float* out, int rows, int cols, int batch,
@@ -427,7 +571,8 @@ int ervf_bf16_gemm_tc(const uint16_t* W, const float* x, float* out, int rows, i
 namespace {
 struct BatchScratch {
   int *chunk_expert, *chunk_off, *chunk_n, *n_chunks, *tok_sorted, *pos;
-  float *act, *contrib;
+  uint8_t *up_panel, *dn_panel;  // f16 activation panels of the up / down launches
+  float* contrib;
   float* part;     // K-split partial accumulators [2][pairs][max(hidden, inter)]
   unsigned* ucnt;  // K-split unit counters [pairs][ceil(max(hidden, inter) / 128)]
   size_t ucnt_bytes;
@@ -445,82 +590,100 @@ BatchScratch batch_scratch(void* base, int pairs, int hidden, int inter) {
   b.tok_sorted = ip + 3 * (size_t)pairs;
   b.pos = ip + 4 * (size_t)pairs;
   b.n_chunks = ip + 5 * (size_t)pairs;
-  b.act = reinterpret_cast<float*>(p + ints * 4);
-  b.contrib = b.act + (size_t)pairs * inter;
-  const size_t rmax = (size_t)(hidden > inter ? hidden : inter);
-  b.part = b.contrib + (size_t)pairs * hidden;
-  b.ucnt = reinterpret_cast<unsigned*>(b.part + (size_t)kMaxKsplit * pairs * rmax);
+  size_t o = ints * 4;
+  b.up_panel = p + o;
+  o += mma_panel_bytes(pairs, hidden);
+  b.dn_panel = p + o;
+  o += mma_panel_bytes(pairs, inter);
+  b.contrib = reinterpret_cast<float*>(p + o);
+  o += (size_t)pairs * hidden * 4;
+  // rows of the tensor-core launches: hidden (down), inter or 2*inter (up, SwiGLU)
+  const size_t rmax = (size_t)(hidden > 2 * inter ? hidden : 2 * inter);
+  b.part = reinterpret_cast<float*>(p + o);
+  o += (size_t)kMaxKsplit * pairs * rmax * 4;
+  b.ucnt = reinterpret_cast<unsigned*>(p + o);
   b.ucnt_bytes = (size_t)pairs * ((rmax + 127) / 128) * 4;
-  b.bytes = ints * 4 + (size_t)pairs * (inter + hidden) * 4 + (size_t)kMaxKsplit * pairs * rmax * 4 +
-            b.ucnt_bytes;
+  b.bytes = o + b.ucnt_bytes;
   return b;
 }
 
-// Lists, up and down of the batched block: contrib[pos[p]] = the down output
-// of pair p for the pairs whose expert this rank owns (all with ep_ranks 1).
-int batch_slots(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
-                size_t up_scale_stride, const uint8_t* dn_codes, const uint8_t* dn_scales,
-                size_t dn_code_stride, size_t dn_scale_stride, const float* globals,
-                const int32_t* ids, int pairs, int top_k, int n_experts, const float* x, int hidden,
-                int inter, const BatchScratch& b, float* contrib, int ep_ranks, int ep_rank,
-                int ksplit, cudaStream_t st) {
+// Lists, activation panels, up and down of the batched block: contrib[pos[p]]
+// = the down output of pair p for the pairs whose expert this rank owns (all
+// with ep_ranks 1).  SwiGLU: the up records hold 2*inter rows (gate / up
+// interleaved).
+int batch_slots(const uint8_t* up_codes, const uint8_t* up_scales, const uint8_t* dn_codes,
+                const uint8_t* dn_scales, const float* globals, const int32_t* ids, int pairs,
+                int top_k, int n_experts, const float* x, int hidden, int inter, bool swiglu,
+                const BatchScratch& b, float* contrib, int ep_ranks, int ep_rank, int ksplit,
+                cudaStream_t st) {
   if (ksplit > 1 && cudaMemsetAsync(b.ucnt, 0, b.ucnt_bytes, st) != cudaSuccess) return kErrLaunch;
   if (int e = launch_moe_batch_lists(ids, pairs, top_k, n_experts, b.chunk_expert, b.chunk_off, b.chunk_n,
                                      b.n_chunks, b.tok_sorted, b.pos, ep_ranks, ep_rank, st))
     return e;
-  GroupedTc g{};
+  if (int e = launch_pack_panel(x, hidden, b.tok_sorted, b.chunk_off, b.chunk_n, b.n_chunks, pairs, 0,
+                                b.up_panel, st))
+    return e;
+  MmaGrouped g{};
   g.chunk_expert = b.chunk_expert;
   g.chunk_off = b.chunk_off;
   g.chunk_n = b.chunk_n;
   g.n_chunks = b.n_chunks;
   g.max_chunks = pairs;
+  g.max_pairs = pairs;
+  g.n_experts = n_experts;
   g.globals = globals;
   g.ksplit = ksplit;
   g.part = b.part;
   g.ucnt = b.ucnt;
-  // up: act[q] = relu(g_up * W_up x_token(q))^2 for sorted pair q
+  // up: relu(g_up * W_up x)^2 (or SwiGLU) as f16 into the down panels
   g.codes = up_codes;
   g.scales = up_scales;
-  g.code_stride = up_code_stride;
-  g.scale_stride = up_scale_stride;
-  g.gsel = 1;
-  g.x = x;
-  g.b_idx = b.tok_sorted;
-  g.out = b.act;
-  g.rows = inter;
+  g.rows = swiglu ? 2 * inter : inter;
   g.cols = hidden;
-  g.relu2 = 1;
-  if (int e = launch_grouped_tc(g, st)) return e;
+  g.gsel = 1;
+  g.panel = b.up_panel;
+  g.down = 0;
+  g.relu2 = swiglu ? 0 : 1;
+  g.swiglu = swiglu ? 1 : 0;
+  g.panel_out = b.dn_panel;
+  if (int e = launch_nvfp4_mma_grouped(g, st)) return e;
   // down: contrib[q] = g_down * W_down act[q]
   g.codes = dn_codes;
   g.scales = dn_scales;
-  g.code_stride = dn_code_stride;
-  g.scale_stride = dn_scale_stride;
-  g.gsel = 0;
-  g.x = b.act;
-  g.b_idx = nullptr;
-  g.out = contrib;
   g.rows = hidden;
   g.cols = inter;
+  g.gsel = 0;
+  g.panel = b.dn_panel;
+  g.down = 1;
   g.relu2 = 0;
-  return launch_grouped_tc(g, st);
+  g.swiglu = 0;
+  g.panel_out = nullptr;
+  g.out = contrib;
+  return launch_nvfp4_mma_grouped(g, st);
 }
 
 int check_batched(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
                   size_t up_scale_stride, const uint8_t* dn_codes, const uint8_t* dn_scales,
                   size_t dn_code_stride, size_t dn_scale_stride, const float* x, int tokens,
-                  int top_k, int n_experts, int hidden, int inter, const void* scratch,
+                  int top_k, int n_experts, int hidden, int inter, int up_rows, const void* scratch,
                   size_t scratch_bytes) {
   const int pairs = tokens * top_k;
   if (tokens <= 0 || top_k <= 0 || top_k > kMaxJobs || pairs > 4096 || n_experts <= 0 ||
       n_experts > kMaxBatchExperts)
     return kErrShape;
-  if (hidden <= 0 || inter <= 0 || hidden % 32 || inter % 32) return kErrShape;
+  if (hidden <= 0 || inter <= 0 || hidden % 32 || inter % 32 || hidden > 4096 || inter > 4096)
+    return kErrShape;
   if (scratch_bytes < batch_scratch(nullptr, pairs, hidden, inter).bytes) return kErrArg;
-  if (!al(up_codes, 16) || !al(dn_codes, 16) || !al(up_scales, 2) || !al(dn_scales, 2) || !al(x, 16) ||
-      !al(scratch, 16) || ((up_code_stride | dn_code_stride) & 15u) ||
-      ((up_scale_stride | dn_scale_stride) & 1u))
+  if (n_experts * (size_t)up_rows > 0x7FFFFFFF || n_experts * (size_t)hidden > 0x7FFFFFFF) return kErrShape;
+  if (!al(up_codes, 16) || !al(dn_codes, 16) || !al(up_scales, 16) || !al(dn_scales, 16) || !al(x, 16) ||
+      !al(scratch, 16))
     return kErrAlign;
+  // the tensor-core path reads each bank as one [n_experts * rows][cols] matrix
+  const size_t urows = (size_t)(up_rows), drows = (size_t)hidden;
+  if (up_code_stride != urows * hidden / 2 || up_scale_stride != urows * hidden / 16 ||
+      dn_code_stride != drows * inter / 2 || dn_scale_stride != drows * inter / 16)
+    return kErrArg;
+  if ((up_scale_stride | dn_scale_stride) & 15u) return kErrAlign;
   return kOk;
 }
 }  // namespace
@@ -538,7 +701,7 @@ int ervf_moe_batched(const uint8_t* up_codes, const uint8_t* up_scales, size_t u
                      size_t scratch_bytes, void* stream) {
   return ervf_moe_batched_ex(up_codes, up_scales, up_code_stride, up_scale_stride, dn_codes,
                              dn_scales, dn_code_stride, dn_scale_stride, globals, ids, route_w,
-                             tokens, top_k, n_experts, x, out, hidden, inter, 1, scratch,
+                             tokens, top_k, n_experts, x, out, hidden, inter, 1, 0, scratch,
                              scratch_bytes, stream);
 }
 
@@ -547,21 +710,21 @@ int ervf_moe_batched_ex(const uint8_t* up_codes, const uint8_t* up_scales, size_
                         size_t dn_code_stride, size_t dn_scale_stride, const float* globals,
                         const int32_t* ids, const float* route_w, int tokens, int top_k,
                         int n_experts, const float* x, float* out, int hidden, int inter,
-                        int ksplit, void* scratch, size_t scratch_bytes, void* stream) {
-  if (ksplit < 1 || ksplit > kMaxKsplit) return kErrArg;
+                        int ksplit, int flags, void* scratch, size_t scratch_bytes, void* stream) {
+  if (ksplit < 1 || ksplit > kMaxKsplit || (flags & ~ERVF_UP_SWIGLU)) return kErrArg;
   if (!up_codes || !up_scales || !dn_codes || !dn_scales || !globals || !ids || !route_w || !x ||
       !out || !scratch)
     return kErrNull;
+  const bool swiglu = (flags & ERVF_UP_SWIGLU) != 0;
   if (int e = check_batched(up_codes, up_scales, up_code_stride, up_scale_stride, dn_codes, dn_scales,
                             dn_code_stride, dn_scale_stride, x, tokens, top_k, n_experts, hidden,
-                            inter, scratch, scratch_bytes))
+                            inter, swiglu ? 2 * inter : inter, scratch, scratch_bytes))
     return e;
   const int pairs = tokens * top_k;
   const BatchScratch b = batch_scratch(scratch, pairs, hidden, inter);
   cudaStream_t st = S(stream);
-  if (int e = batch_slots(up_codes, up_scales, up_code_stride, up_scale_stride, dn_codes, dn_scales,
-                          dn_code_stride, dn_scale_stride, globals, ids, pairs, top_k, n_experts, x,
-                          hidden, inter, b, b.contrib, 1, 0, ksplit, st))
+  if (int e = batch_slots(up_codes, up_scales, dn_codes, dn_scales, globals, ids, pairs, top_k, n_experts, x,
+                          hidden, inter, swiglu, b, b.contrib, 1, 0, ksplit, st))
     return e;
   return launch_moe_batch_routesum(b.contrib, b.pos, route_w, x, out, tokens, hidden, top_k, st);
 }
@@ -594,13 +757,12 @@ int ervf_moe_batched_ep_slots_ex(const uint8_t* up_codes, const uint8_t* up_scal
   if (ep_ranks < 1 || ep_ranks > kEpMaxRanks || ep_rank < 0 || ep_rank >= ep_ranks) return kErrShape;
   if (int e = check_batched(up_codes, up_scales, up_code_stride, up_scale_stride, dn_codes, dn_scales,
                             dn_code_stride, dn_scale_stride, x, tokens, top_k, n_experts, hidden,
-                            inter, scratch, scratch_bytes))
+                            inter, inter, scratch, scratch_bytes))
     return e;
   if (!al(slots, 16)) return kErrAlign;
   const BatchScratch b = batch_scratch(scratch, tokens * top_k, hidden, inter);
-  return batch_slots(up_codes, up_scales, up_code_stride, up_scale_stride, dn_codes, dn_scales,
-                     dn_code_stride, dn_scale_stride, globals, ids, tokens * top_k, top_k, n_experts,
-                     x, hidden, inter, b, slots, ep_ranks, ep_rank, ksplit, S(stream));
+  return batch_slots(up_codes, up_scales, dn_codes, dn_scales, globals, ids, tokens * top_k, top_k,
+                     n_experts, x, hidden, inter, false, b, slots, ep_ranks, ep_rank, ksplit, S(stream));
 }
 
 int ervf_ep_batch_exchange_route_sum(const uint64_t* peers, int nranks, int rank, int buf,
@@ -761,10 +923,10 @@ int ervf_cache_fetch(const uint8_t* bank_c, const uint8_t* bank_s, uint8_t* cach
 // Allocation-free routed sum (no counterpart in the reference).
 //
 // The scratch of the spread-rows routed sum (contrib[top_k][hidden] floats +
-// hidden row counters) lives in this file-scope device array instead of a
-// caller buffer.  Limits: hidden <= kStaticRows, top_k <= kStaticJobs
+// the 32-row group counters) lives in this file-scope device array instead
+// of a caller buffer.  Limits: hidden <= kStaticRows, top_k <= kStaticJobs
 // (294,912 bytes).  Its device address is looked up once per device, with
-// that device current, on the first call.  Every call clears the row
+// that device current, on the first call.  Every call clears the group
 // counters on the stream (cudaMemsetAsync; no allocation) before the launch.
 // All calls on one device share the array: calls that overlap on the GPU race.
 
@@ -773,7 +935,7 @@ namespace {
 constexpr int kStaticRows = 8192;
 constexpr int kStaticJobs = 8;
 constexpr size_t kStaticScratchBytes =
-    (size_t)kStaticJobs * kStaticRows * sizeof(float) + (size_t)kStaticRows * sizeof(int);
+    (size_t)kStaticRows * sizeof(int) + (size_t)kStaticJobs * kStaticRows * sizeof(float);
 
 static __device__ __align__(256) unsigned char g_routesum_static[kStaticScratchBytes];
 
@@ -807,15 +969,15 @@ int ervf_moe_down_routesum_static(const uint8_t* dn_codes, const uint8_t* dn_sca
   if (top_k <= 0 || hidden <= 0) return kErrShape;
   void* scratch = static_scratch();
   if (!scratch) return kErrLaunch;
-  int* row_count = reinterpret_cast<int*>(reinterpret_cast<float*>(scratch) + (size_t)top_k * hidden);
-  if (cudaMemsetAsync(row_count, 0, (size_t)hidden * sizeof(int), S(stream)) != cudaSuccess)
+  // the group counters sit at the start of the array for every top_k
+  if (cudaMemsetAsync(scratch, 0, (size_t)(hidden + 31) / 32 * sizeof(unsigned), S(stream)) != cudaSuccess)
     return kErrLaunch;
-  // A memset now precedes the launch, so it runs without programmatic
-  // dependent launch; ERVF_LAUNCH_IDS_READY only matters with it.
+  // The memset is an ordinary stream dependency of the launch that follows;
+  // ERVF_LAUNCH_PDL keeps the spread-rows route sum (group counters in the
+  // array), without it a launch of 2..8 slots takes the cluster route sum.
   return ervf_moe_down_routesum(dn_codes, dn_scales, dn_code_stride, dn_scale_stride, ids, globals,
                                 route_w, top_k, act, base, resid, out, hidden, inter, scratch,
-                                kStaticScratchBytes, width, flags & ~(ERVF_LAUNCH_PDL | ERVF_LAUNCH_IDS_READY),
-                                stream);
+                                kStaticScratchBytes, width, flags, stream);
 }
 
 }  // extern "C"

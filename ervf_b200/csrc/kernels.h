@@ -59,16 +59,30 @@ struct GemvBatch {
   int pdl;
   int ids_ready;
   // mode 1 scratch on the TMA schedule: contrib[njobs][rows] fp32 and
-  // row_count[rows] int32 (all zero before the first call; every call leaves
-  // them zero).  Each job's row sums land in contrib; the last job to finish a
-  // row adds the row up in route order.  NULL: the width schedules are used.
+  // grp_count[ceil(rows / 32)] u32 (all zero before the first call; every
+  // call that completes leaves them zero; after ERVF_ERR_TIMEOUT the caller
+  // zeroes them again).  Each job's row values land in contrib; the producer
+  // warp that completes a 32-row group's count adds those rows up in route
+  // order.  NULL: the width schedules are used.
   float* contrib;
-  int* row_count;
+  unsigned* grp_count;
+  // L2 prefetch hint for the next launch: records of pf_n experts pf_ids[i]
+  // (clamped to [0, pf_experts)), codes at pf_codes + id * pf_code_stride
+  // (pf_code_bytes each) and scales at pf_scales + id * pf_scale_stride.  All
+  // addresses, strides and sizes multiples of 16 bytes; pf_n = 0: none.
+  const uint8_t* pf_codes;
+  const uint8_t* pf_scales;
+  size_t pf_code_stride, pf_scale_stride, pf_code_bytes, pf_scale_bytes;
+  const int* pf_ids;
+  int pf_n, pf_experts;
 };
 
-// Scratch bytes the routed-sum launch needs: contrib + row counters.
+// Scratch of the routed-sum launch: the group counters first (one u32 per
+// row reserved, rounded up to 16 bytes: the same place for every top_k, so a
+// buffer stays ready when reused with another top_k), then contrib.
+inline size_t routesum_counter_bytes(int rows) { return ((size_t)rows * sizeof(int) + 15) / 16 * 16; }
 inline size_t routesum_scratch_bytes(int rows, int njobs) {
-  return (size_t)njobs * rows * sizeof(float) + (size_t)rows * sizeof(int);
+  return routesum_counter_bytes(rows) + (size_t)njobs * rows * sizeof(float);
 }
 
 __host__ __device__ inline bool job_active(const GemvBatch& b, int job) {
@@ -80,32 +94,6 @@ __host__ __device__ inline bool job_active(const GemvBatch& b, int job) {
   return true;
 #endif
 }
-
-// Persistent decode (nvfp4_gemv.cu): all routed-MoE layers of one token in
-// one cooperative launch.
-struct DecodeLayer {
-  const uint8_t* up_c;
-  const uint8_t* up_s;
-  const uint8_t* dn_c;
-  const uint8_t* dn_s;
-  const float* globals;  // [E][2] = (g_down, g_up)
-};
-
-struct DecodeArgs {
-  int layers, top_k, hidden, inter;
-  size_t up_cs, up_ss, dn_cs, dn_ss;  // per-expert record strides (bytes)
-  const DecodeLayer* lay;             // [layers], device
-  const int* ids;                     // [layers][top_k]
-  const float* route_w;               // [layers][top_k]
-  const float* x_in;                  // [hidden]
-  float* xb;                          // [2][hidden]: layer l writes xb[l & 1]
-  float* act;                         // [top_k][inter]
-  float* contrib;                     // [top_k][hidden]
-  int* row_count;                     // [hidden], zero before and after
-  unsigned* grid_bar;                 // zero at launch
-};
-
-int launch_moe_decode(const DecodeArgs& a, cudaStream_t stream);
 
 // width 0: the TMA-staged B200 schedule (falls back to width 32 where its
 // preconditions do not hold); 4/8/16/32: W lanes per row, lane L owning the
@@ -148,6 +136,46 @@ struct GroupedTc {
 };
 int launch_grouped_tc(const GroupedTc& g, cudaStream_t stream);
 
+// Warp-specialised NVFP4 GEMM on the tensor cores (nvfp4_mma.cu).  The
+// activations come as f16 panels in the MMA's layout: panel[c][kb] = 8 KB
+// tile of up to 16 activation rows x 256 columns (launch_pack_panel builds
+// them from fp32 rows).
+size_t mma_panel_bytes(int chunks, int cols);
+int launch_pack_panel(const float* src, int cols, const int* idx, const int* chunk_off, const int* chunk_n,
+                      const int* n_chunks, int max_chunks, int n_single, uint8_t* panel,
+                      cudaStream_t stream);
+// out[j][r] = g * (W @ X[j])[r], j < n <= 16.  part / ucnt (may be NULL): K
+// split partials f32[max_splits][n][rows] and counters u32[ceil(rows/128)]
+// (zero before, left zero) -- used when the row tiles leave SMs idle.
+int launch_nvfp4_mma_single(const uint8_t* codes, const uint8_t* scales, float g, const uint8_t* panel,
+                            float* out, int rows, int cols, int n, float* part, unsigned* ucnt,
+                            int max_splits, cudaStream_t stream);
+// Grouped (expert-major) form: unit = (chunk, 128-row tile, K split) over a
+// bank of n_experts contiguous [rows x cols] records (code stride rows*cols/2,
+// scale stride rows*cols/16).  up (down = 0): relu^2 (or SwiGLU of row pairs)
+// of g_up * W x as f16 into panel_out, the down launch's panels; down: fp32
+// out[(chunk_off + j) * rows + r] = g_down * (W act)[r].
+struct MmaGrouped {
+  const uint8_t* codes;
+  const uint8_t* scales;
+  int n_experts, rows, cols;
+  const float* globals;
+  int gsel;
+  const uint8_t* panel;
+  const int* chunk_expert;
+  const int* chunk_off;
+  const int* chunk_n;
+  const int* n_chunks;
+  int max_chunks, max_pairs;
+  int down, relu2, swiglu;
+  float* out;
+  uint8_t* panel_out;
+  int ksplit;
+  float* part;      // [ksplit][max_pairs][rows]
+  unsigned* ucnt;   // [max_chunks * ceil(rows / 128)], zero before, left zero
+};
+int launch_nvfp4_mma_grouped(const MmaGrouped& g, cudaStream_t stream);
+
 // Batched BF16 GEMM on the tensor cores: out[n][r] = (W @ X[n])[r] for
 // n < N <= 8 (X split into bf16 high / low halves), fp32 accumulate.
 int launch_bf16_gemm_tc(const uint16_t* W, const float* x, float* out, int rows, int cols, int n,
@@ -178,6 +206,7 @@ int read_gemv_device_error(bool clear);
 int read_aux_device_error(bool clear);
 int read_tc_device_error(bool clear);
 int read_ep_device_error(bool clear);
+int read_mma_device_error(bool clear);
 
 // Expert-parallel exchange over NVLink peer memory (ep_p2p.cu).  Region
 // layout of every rank: u64 flag[kEpMaxRanks] at 0, u64 seq at 512, f32

@@ -20,6 +20,8 @@
 //    same tree, any alignment >= 4 bytes; also the fallback where the TMA
 //    schedule's preconditions (cols % 32 == 0, cols <= 4096, 16-B aligned
 //    bases) do not hold.
+#include <stdlib.h>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -178,11 +180,20 @@ __global__ void __launch_bounds__(256) nvfp4_gemv_sched(GemvBatch p, int tiles_p
 // and eight lanes combine ((S0+S4)+(S2+S6))+((S1+S5)+(S3+S7)).
 //
 // mode 1 (routed sum): the tree lane of a row writes the job's row value y_s
-// to contrib[s][row], publishes it (acq_rel atomic on a per-row count), and
-// the lane that completes a row's count adds the row up in ROUTE order,
-// acc = fmaf(y_s, w_s, acc) for s = 0..njobs-1 from base or 0, writes
-// resid + acc and resets the count -- the same sum as one thread walking the
-// slots in order, with the rows spread over every SM.
+// to contrib[s][row].  Rows are counted in groups of 32: after the item's
+// values are stored, the producer warp (idle once its copies are issued)
+// adds the item's row count to each group it touches with one acq_rel atomic
+// per group; the atomic that completes a group (njobs x its rows) makes its
+// warp add the group's 32 rows up in ROUTE order, acc = fmaf(y_s, w_s, acc)
+// for s = 0..njobs-1 from base or 0, and write resid + acc -- the same sum as
+// one thread walking the slots in order, with the rows spread over every SM
+// and no consumer thread ever waiting on an atomic.
+//
+// L2 prefetch: a launch may name the expert records the NEXT launch will read
+// (codes and scales of pf_n experts); each CTA issues cp.async.bulk.prefetch.L2
+// (this GPU's memory, no multicast) for a slice of them once its own ring is
+// filled, so that their HBM stream runs under this launch's compute.  A hint:
+// results do not depend on it.
 //
 // mode 1 with a cluster (2 <= njobs <= 8): the grid is cut into thread-block
 // clusters of njobs CTAs; cluster i owns one range of rows, and its CTA of
@@ -211,9 +222,20 @@ struct TmaCfg {
   int blk;          // rows per row block (4 or 8: 16-byte aligned scale rows)
   int kb;           // row blocks per item (kRt / blk)
   int bpj;          // row blocks per job
-  int cluster;      // mode 1: CTAs per cluster (= njobs), 0 = atomic route sum
+  int cluster;      // mode 1: CTAs per cluster (= njobs), 0 = group-counter route sum
   int ysm_off;      // cluster mode: row values of this CTA's range, kYsmRows floats
 };
+
+// Shared-memory header of nvfp4_gemv_tma (the chain buffer starts at 576):
+//   0   full[8]    mbarriers, a stage holds data
+//   64  empty[8]   mbarriers, a stage was read by the consumers
+//   128 jc[16]     code base of each job
+//   256 js[16]     scale base of each job
+//   384 jg[16]     global scale of each job
+//   448 jlist[16]  active jobs (expert-parallel filter)
+//   512 nact       number of active jobs
+//   516 done       items whose row values are stored (mode-1 publishing)
+constexpr int kPartOff = 576;
 
 constexpr int kYsmRows = 512;  // rows per cluster range (cluster mode)
 
@@ -231,34 +253,67 @@ __device__ __forceinline__ float ld_dsmem(const float* p, uint32_t rank) {
 }
 
 // One 16-byte code unit (4 chains x 8 codes) of one row, continuing the four
-// chain accumulators acc[0..3].  Chains 0,1 use the block scale s0 = s_2u,
-// chains 2,3 use s1 = s_2u+1; x[8j + m] is the activation of chain j's m-th
-// code.
+// chain accumulators: acc[0] = (chain 0, chain 1), acc[1] = (chain 2, chain 3).
+// Chains 0,1 use the block scale s0 = s_2u, chains 2,3 use s1 = s_2u+1.  The
+// activation comes pre-paired: xp[m] = (x[m], x[8 + m]) and xp[8 + m] =
+// (x[16 + m], x[24 + m]) for code m of the chain pair, x[8j + m] being the
+// activation of chain j's m-th code.  Each step is one packed multiply
+// (w = RN(e2m1 * s) for two chains) and one packed FMA (acc = fmaf(w, x, acc)
+// for two chains): the same IEEE operations, in the same per-chain order, as
+// the scalar chain.
 __device__ __forceinline__ void unit_fma(const uint4 q, const float s0, const float s1,
-                                         const float (&x)[32], float* acc) {
-  float f0[8], f1[8], f2[8], f3[8];
-  e2m1x8_to_f32(q.x, f0);
-  e2m1x8_to_f32(q.y, f1);
-  e2m1x8_to_f32(q.z, f2);
-  e2m1x8_to_f32(q.w, f3);
+                                         const float2 (&xp)[16], float2 (&acc)[2]) {
+  uint32_t h0[4], h1[4], h2[4], h3[4];
+  e2m1x8_to_f16x2(q.x, h0);
+  e2m1x8_to_f16x2(q.y, h1);
+  e2m1x8_to_f16x2(q.z, h2);
+  e2m1x8_to_f16x2(q.w, h3);
+  const float2 sa = make_float2(s0, s0), sb = make_float2(s1, s1);
+  float2 a01 = acc[0], a23 = acc[1];
 #pragma unroll
-  for (int m = 0; m < 8; ++m) {
-    acc[0] = fmaf(f0[m] * s0, x[m], acc[0]);
-    acc[1] = fmaf(f1[m] * s0, x[8 + m], acc[1]);
-    acc[2] = fmaf(f2[m] * s1, x[16 + m], acc[2]);
-    acc[3] = fmaf(f3[m] * s1, x[24 + m], acc[3]);
+  for (int i = 0; i < 4; ++i) {
+    const __half2 v0 = *reinterpret_cast<const __half2*>(&h0[i]);
+    const __half2 v1 = *reinterpret_cast<const __half2*>(&h1[i]);
+    const __half2 v2 = *reinterpret_cast<const __half2*>(&h2[i]);
+    const __half2 v3 = *reinterpret_cast<const __half2*>(&h3[i]);
+    a01 = fma2(mul2(make_float2(__low2float(v0), __low2float(v1)), sa), xp[2 * i], a01);
+    a23 = fma2(mul2(make_float2(__low2float(v2), __low2float(v3)), sb), xp[8 + 2 * i], a23);
+    a01 = fma2(mul2(make_float2(__high2float(v0), __high2float(v1)), sa), xp[2 * i + 1], a01);
+    a23 = fma2(mul2(make_float2(__high2float(v2), __high2float(v3)), sb), xp[9 + 2 * i], a23);
   }
+  acc[0] = a01;
+  acc[1] = a23;
 }
 
 // SiLU of the gate row, v / (1 + e^-v) in binary32 (CUDA expf).
 __device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
 
-// Activation of unit u from the swizzled shared copy (float4 i at u*8 + (i ^ (u & 7))).
-__device__ __forceinline__ void load_unit_x(const float4* xs, int u, float (&x)[32]) {
+// Shared copy of the activation: unit t (32 columns) holds 8 float4 slots;
+// slot k = (x[c], x[c + 8], x[c + 1], x[c + 9]) with c = 16 (k >> 2) + 2 (k & 3)
+// (column offsets inside the unit), stored at t * 8 + (k ^ (t & 7)) so that
+// the eight readers of one slot index hit different bank groups.  One slot
+// is two of the pairs unit_fma consumes.
+__device__ __forceinline__ float4 x_slot(const float* x, int t, int k) {
+  const int c = 32 * t + 16 * (k >> 2) + 2 * (k & 3);
+  const float2 a = *reinterpret_cast<const float2*>(x + c);
+  const float2 b = *reinterpret_cast<const float2*>(x + c + 8);
+  return make_float4(a.x, b.x, a.y, b.y);
+}
+
+__device__ __forceinline__ float4 x_slot_cg(const float* x, int t, int k) {
+  const int c = 32 * t + 16 * (k >> 2) + 2 * (k & 3);
+  const float2 a = __ldcg(reinterpret_cast<const float2*>(x + c));
+  const float2 b = __ldcg(reinterpret_cast<const float2*>(x + c + 8));
+  return make_float4(a.x, b.x, a.y, b.y);
+}
+
+// The activation pairs of unit u from the shared copy.
+__device__ __forceinline__ void load_unit_x(const float4* xs, int u, float2 (&xp)[16]) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float4 v = xs[u * 8 + (i ^ (u & 7))];
-    x[4 * i] = v.x; x[4 * i + 1] = v.y; x[4 * i + 2] = v.z; x[4 * i + 3] = v.w;
+  for (int k = 0; k < 8; ++k) {
+    const float4 v = xs[u * 8 + (k ^ (u & 7))];
+    xp[2 * k] = make_float2(v.x, v.y);
+    xp[2 * k + 1] = make_float2(v.z, v.w);
   }
 }
 
@@ -271,7 +326,7 @@ __device__ __forceinline__ void load_unit_x(const float4* xs, int u, float (&x)[
 template <int H, bool FULL>
 __device__ __forceinline__ void seg_rows(const uint8_t* smem, uint32_t coff, uint32_t soff,
                                          uint32_t rstep, uint32_t sstep, const float* lut,
-                                         const float (&x)[32], float (&acc)[H][4], int row0,
+                                         const float2 (&x)[16], float2 (&acc)[H][2], int row0,
                                          int rowstep, int nrows) {
 #pragma unroll
   for (int h = 0; h < H; ++h) {
@@ -285,13 +340,13 @@ __device__ __forceinline__ void seg_rows(const uint8_t* smem, uint32_t coff, uin
 
 template <int H, bool FULL>
 __device__ __forceinline__ void seg_store(float* part, uint32_t poff, uint32_t pstep,
-                                          const float (&acc)[H][4], int row0, int rowstep,
+                                          const float2 (&acc)[H][2], int row0, int rowstep,
                                           int nrows) {
 #pragma unroll
   for (int h = 0; h < H; ++h)
     if (FULL || row0 + h * rowstep < nrows)
       *reinterpret_cast<float4*>(part + poff + h * pstep) =
-          make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+          make_float4(acc[h][0].x, acc[h][0].y, acc[h][1].x, acc[h][1].y);
 }
 
 // The two segments of one consumer thread for one item (see the schedule
@@ -301,11 +356,11 @@ template <int H, bool FULL>
 __device__ __forceinline__ void segments(const uint8_t* smem, uint32_t stage_off, int scale_off,
                                          int cb, int sb, int team, int T, int par1, int par2,
                                          bool cont, int u1, int u2, int grp, int nrows,
-                                         const float* lut, const float4* xs, float (&x)[32],
+                                         const float* lut, const float4* xs, float2 (&x)[16],
                                          bool& x_stale, float* part) {
-  float acc[H][4];
+  float2 acc[H][2];
 #pragma unroll
-  for (int h = 0; h < H; ++h) acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.0f;
+  for (int h = 0; h < H; ++h) acc[h][0] = acc[h][1] = make_float2(0.0f, 0.0f);
   const int rowstep = 2 * T;
   const uint32_t rstep = (uint32_t)(rowstep * cb), sstep = (uint32_t)(rowstep * sb);
   const uint32_t pstep = (uint32_t)(rowstep * kRowPitch);
@@ -317,7 +372,7 @@ __device__ __forceinline__ void segments(const uint8_t* smem, uint32_t stage_off
   if (!cont) {
     seg_store<H, FULL>(part, row1 * kRowPitch + part_index(4 * grp), pstep, acc, row1, rowstep, nrows);
 #pragma unroll
-    for (int h = 0; h < H; ++h) acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.0f;
+    for (int h = 0; h < H; ++h) acc[h][0] = acc[h][1] = make_float2(0.0f, 0.0f);
   } else {
     load_unit_x(xs, u2, x);
   }
@@ -356,6 +411,97 @@ __device__ __forceinline__ bool next_item(ItemSeq& q, const TmaCfg& c, const int
   return true;
 }
 
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+__device__ __forceinline__ void st_release_cta(int* p, int v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_cta(const int* p) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+
+// This CTA's slice of the L2 prefetch: the records are cut into 32 KB chunks,
+// numbered across records, and CTA b issues chunks b, b + grid, ...  Ids are
+// clamped into [0, pf_experts) so that a stale id cannot leave the bank.
+__device__ __forceinline__ void l2_prefetch_slice(const GemvBatch& p) {
+  constexpr uint32_t kChunk = 32768;
+  const long long G = gridDim.x, b = blockIdx.x;
+  long long idx = 0;
+  for (int j = 0; j < p.pf_n; ++j) {
+    int id = p.pf_ids[j];
+    id = id < 0 ? 0 : (id >= p.pf_experts ? p.pf_experts - 1 : id);
+    for (int r = 0; r < 2; ++r) {
+      const uint8_t* base = r ? p.pf_scales + (size_t)id * p.pf_scale_stride
+                              : p.pf_codes + (size_t)id * p.pf_code_stride;
+      const size_t bytes = r ? p.pf_scale_bytes : p.pf_code_bytes;
+      const long long n = (long long)((bytes + kChunk - 1) / kChunk);
+      for (long long c = ((b - idx) % G + G) % G; c < n; c += G) {
+        const size_t off = (size_t)c * kChunk;
+        const uint32_t sz = (uint32_t)(bytes - off < kChunk ? bytes - off : kChunk);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off), "r"(sz) : "memory");
+      }
+      idx += n;
+    }
+  }
+}
+
+// Mode-1 publishing, run by the whole producer warp over the CTA's items in
+// order: wait (bounded) until the consumers have stored item i's row values,
+// add its rows to the 32-row groups it touches, and sum every group whose
+// count this completed.  Returns false when the wait ran out.
+__device__ __forceinline__ bool publish_items(const GemvBatch& p, const TmaCfg& c, ItemSeq q,
+                                              const int* jlist, const int* done, int lane) {
+  int it = 0, job, r0, nrows;
+  while (next_item(q, c, jlist, p.rows, job, r0, nrows)) {
+    bool ok = true;
+    if (lane == 0) {
+      const long long t0 = clock64();
+      while (ld_acquire_cta(done) <= it) {
+        if (clock64() - t0 > 4000000000LL) {
+          atomicExch(&g_device_error, kErrTimeout);
+          ok = false;
+          break;
+        }
+        nanosleep_ns(32);
+      }
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (!ok) return false;
+    ++it;
+    const int g0 = r0 >> 5, g1 = (r0 + nrows - 1) >> 5;
+    int last = -1;
+    if (lane <= g1 - g0) {
+      const int g = g0 + lane;
+      const int lo = max(r0, g << 5), hi = min(r0 + nrows, (g << 5) + 32);
+      const int target = p.njobs * (min(p.rows, (g << 5) + 32) - (g << 5));
+      const unsigned old = atom_add_acq_rel_gpu(p.grp_count + g, (unsigned)(hi - lo));
+      if ((int)old + (hi - lo) == target) last = g;
+    }
+    unsigned m = __ballot_sync(0xffffffffu, last >= 0);
+    while (m) {
+      const int src = __ffs(m) - 1;
+      m &= m - 1;
+      const int g = __shfl_sync(0xffffffffu, last, src);
+      const int r = (g << 5) + lane;
+      if (r < p.rows) {
+        float acc = p.base ? p.base[r] : 0.0f;
+        for (int s2 = 0; s2 < p.njobs; ++s2)
+          acc = fmaf(__ldcg(&p.contrib[(size_t)s2 * p.rows + r]), p.route_w[s2], acc);
+        p.rs_out[r] = p.resid ? p.resid[r] + acc : acc;
+      }
+      if (lane == src) p.grp_count[g] = 0u;  // every add of this group is in
+    }
+  }
+  return true;
+}
+
 template <int H>
 __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCfg c) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -369,16 +515,19 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
   float* jg = reinterpret_cast<float*>(smem + 384);
   int* jlist = reinterpret_cast<int*>(smem + 448);
   int* nact = jlist + kMaxJobs;
+  int* done = nact + 1;
   float* part = reinterpret_cast<float*>(smem + c.part_off);
   float4* xs = reinterpret_cast<float4*>(smem + c.xs_off);
   float* lut = reinterpret_cast<float*>(smem + c.lut_off);  // [256] of the current job
   uint8_t* stages = smem + c.stage_base;
+  const bool publish = p.mode == 1 && !c.cluster;
 
   if (tid == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
+    *done = 0;
     fence_mbar_init();
   }
   // Slot / id tables and globals: readable now if they were produced before
@@ -418,9 +567,16 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
 
   // ------------------------------------------------------------ producer
   if (tid >= kCT) {
-    if (tid == kCT) {
+    const int lane = tid - kCT;
+    if (lane == 0) {
+      ItemSeq qp = q;
       int it = 0, job, r0, nrows;
-      while (next_item(q, c, jlist, p.rows, job, r0, nrows)) {
+      bool prefetched = p.pf_n == 0;
+      while (next_item(qp, c, jlist, p.rows, job, r0, nrows)) {
+        if (it == S && !prefetched) {  // the ring is full: queue the next launch's records
+          l2_prefetch_slice(p);
+          prefetched = true;
+        }
         const int st = it % S;
         if (!mbar_wait(&empty[st], ((it / S) & 1) ^ 1)) break;
         ++it;
@@ -435,11 +591,14 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
         bulk_g2s(dst, jc[job] + (size_t)r0 * cb, code_bytes, &full[st]);
         if (s16) bulk_g2s(dst + c.scale_off, ssrc, s16, &full[st]);
       }
+      if (!prefetched) l2_prefetch_slice(p);
       // Leave no bulk copy in flight: wait (bounded) for the last stages.
       for (int k = (it > S ? it - S : 0); k < it; ++k) mbar_wait(&full[k % S], (k / S) & 1);
     }
-    grid_dep_wait();
+    __syncwarp();
+    grid_dep_wait();  // base / residual / route weights come from the predecessor
     grid_dep_launch();
+    if (publish) publish_items(p, c, q, jlist, done, lane);
     if (c.cluster) {  // every thread of the cluster takes both barriers
       cluster_sync_all();
       cluster_sync_all();
@@ -469,7 +628,7 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
   int cur_job = -1;
   // segment activation; a thread whose two segments share one unit keeps it
   // in registers until the job's activation changes
-  float x[32];
+  float2 x[16];
   bool x_stale = true;
   named_bar_sync(kBarC, kCT);
 
@@ -481,10 +640,9 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
     const GemvJob& J = p.job[job];
     if (J.x != cur_x || job != cur_job) {  // the previous item ended with a consumer barrier
       if (J.x != cur_x) {
-        const float4* src = reinterpret_cast<const float4*>(J.x);
         for (int f = tid; f < nu * 8; f += kCT) {
-          const int t = f >> 3, i = f & 7;
-          xs[t * 8 + (i ^ (t & 7))] = __ldg(src + f);
+          const int t = f >> 3, k = f & 7;
+          xs[t * 8 + (k ^ (t & 7))] = x_slot(J.x, t, k);
         }
         cur_x = J.x;
         x_stale = true;
@@ -518,27 +676,19 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
     y = combine8(legacy_fix(y, p.legacy_tree));
     // SwiGLU: rows 2i (gate) and 2i+1 (up) sit 8 lanes apart in one warp
     const float y_up = __shfl_down_sync(0xffffffffu, y, 8);
+    if (publish && tw == 0 && tr < nrows) p.contrib[(size_t)job * p.rows + r0 + tr] = y;
     named_bar_sync(kBarC, kCT);  // the chain buffer is rewritten by the next item
-    if (p.swiglu) {
+    if (publish) {
+      if (tid == 0) st_release_cta(done, it);  // the item's row values are stored
+    } else if (p.swiglu) {
       if (tw == 0 && (tr & 1) == 0 && tr + 1 < nrows)
         J.out[(r0 + tr) >> 1] = silu(y) * y_up;
     } else if (tw == 0 && tr < nrows) {
       const int r = r0 + tr;
       if (p.mode == 0) {
         J.out[r] = epilogue(y, p.relu2, p.out_scale);
-      } else if (c.cluster) {
-        ysm[r - row_lo] = y;
       } else {
-        p.contrib[(size_t)job * p.rows + r] = y;
-        unsigned old_cnt;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old_cnt) : "l"(&p.row_count[r]) : "memory");
-        if ((int)old_cnt == p.njobs - 1) {
-          float acc = p.base ? p.base[r] : 0.0f;
-          for (int s = 0; s < p.njobs; ++s)
-            acc = fmaf(__ldcg(&p.contrib[(size_t)s * p.rows + r]), p.route_w[s], acc);
-          p.rs_out[r] = p.resid ? p.resid[r] + acc : acc;
-          p.row_count[r] = 0;
-        }
+        ysm[r - row_lo] = y;  // cluster mode
       }
     }
   }
@@ -555,285 +705,6 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
       p.rs_out[r] = p.resid ? p.resid[r] + acc : acc;
     }
     cluster_sync_all();  // peers have read this CTA's row values
-  }
-}
-
-// Job-aligned split: the grid is cut into njobs contiguous CTA groups, one
-// per job, and each group splits its job's row blocks evenly, so that every
-// CTA works on a single job (one activation) per launch or phase.
-__device__ __forceinline__ void cta_blocks_per_job(int njobs, int bpj, ItemSeq& q) {
-  const int G = gridDim.x, b = blockIdx.x;
-  if (G < njobs) {
-    cta_blocks(njobs * bpj, q);
-    return;
-  }
-  const int j = (int)(((long long)b * njobs) / G);
-  const int c0 = (int)(((long long)j * G + njobs - 1) / njobs);
-  const int c1 = (int)(((long long)(j + 1) * G + njobs - 1) / njobs);
-  const int n = c1 - c0, k = b - c0;
-  const int per = bpj / n, rem = bpj % n;
-  q.blk = j * bpj + k * per + min(k, rem);
-  q.blk_end = q.blk + per + (k < rem ? 1 : 0);
-}
-
-// ======================================================================
-// Persistent decode: every routed-MoE layer of one token in one launch
-// ======================================================================
-//
-// Phases p = 0 .. 2L-1 alternate up (layer l = p/2: act[s] = relu2(up_s(x_l)))
-// and down (x_{l+1} = x_l + sum_s w_s down_s(act[s]) in route order), each
-// with the item schedule of nvfp4_gemv_tma, separated by grid barriers (a
-// cooperative launch keeps every CTA resident).  The producer warp never
-// waits at a grid barrier: expert weights do not depend on activations and
-// the routing of every layer is known before the launch, so the copy ring
-// keeps streaming the next phases' experts while the consumers wait.
-// Activations written by other CTAs are read through L2 (ld.global.cg).
-
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Grid barrier of the consumer threads (all CTAs): returns true when this
-// CTA gave up waiting (error word set) or was already dead.
-__device__ __forceinline__ bool grid_barrier(unsigned* bar, unsigned target, bool dead) {
-  named_bar_sync(kBarC, kCT);
-  if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(bar, 1u);
-    if (!dead) {
-      const long long t0 = clock64();
-      while (ld_acquire_gpu(bar) < target) {
-        if (clock64() - t0 > 4000000000LL) {
-          atomicExch(&g_device_error, kErrTimeout);
-          dead = true;
-          break;
-        }
-        nanosleep_ns(64);
-      }
-    }
-    __threadfence();
-  }
-  return named_bar_or(kBarC, kCT, dead);
-}
-
-// Job s of phase p: code / scale rows and global scale.
-__device__ __forceinline__ void decode_job(const DecodeArgs& a, int p, int s, const uint8_t*& cc,
-                                           const uint8_t*& ss, float& g) {
-  const int l = p >> 1;
-  const DecodeLayer& L = a.lay[l];
-  const size_t slot = (size_t)__ldg(&a.ids[l * a.top_k + s]);
-  if (p & 1) {
-    cc = L.dn_c + slot * a.dn_cs;
-    ss = L.dn_s + slot * a.dn_ss;
-    g = __ldg(&L.globals[slot * 2 + 0]);
-  } else {
-    cc = L.up_c + slot * a.up_cs;
-    ss = L.up_s + slot * a.up_ss;
-    g = __ldg(&L.globals[slot * 2 + 1]);
-  }
-}
-
-template <int H>
-__device__ __forceinline__ void decode_segments(const TmaCfg& c, int tid, bool full, const uint8_t* smem,
-                                                uint32_t stage_off, int cb, int sb, int nrows,
-                                                const float* lut, const float4* xs, float (&x)[32],
-                                                bool& x_stale, float* part) {
-  const int nu = c.n_u, n2 = c.n2, T = c.teams;
-  const int team = tid / nu, m = tid - team * nu;
-  if (team >= T) return;
-  const bool cont = m < 2 * n2;
-  const int grp = m < n2 ? m : m - n2;
-  const int u1 = grp, u2 = cont ? grp + 64 : grp;
-  const int par1 = (m >= n2 && m < 2 * n2) ? 1 : 0;
-  const int par2 = cont ? par1 : 1;
-  if (full) {
-    segments<H, true>(smem, stage_off, c.scale_off, cb, sb, team, T, par1, par2, cont, u1, u2, grp,
-                      nrows, lut, xs, x, x_stale, part);
-  } else {
-    segments<H, false>(smem, stage_off, c.scale_off, cb, sb, team, T, par1, par2, cont, u1, u2, grp,
-                       nrows, lut, xs, x, x_stale, part);
-  }
-}
-
-// Route-order sum of layer l for this CTA's slice of rows (the grid splits
-// the hidden rows evenly): x_{l+1}[r] = x_l[r] + acc, acc = fmaf(contrib[s][r],
-// w_s, acc) over the route slots in order from 0.0 -- the routed sum with
-// residual as ervf_moe_down_routesum computes it.  Reads through L2: other
-// CTAs wrote contrib.
-__device__ __forceinline__ void sum_rows(const DecodeArgs& a, int l) {
-  const float* xl = l == 0 ? a.x_in : a.xb + (size_t)((l - 1) & 1) * a.hidden;
-  float* xn = a.xb + (size_t)(l & 1) * a.hidden;
-  const float* w = a.route_w + (size_t)l * a.top_k;
-  const int G = gridDim.x, b = blockIdx.x;
-  const int lo = (int)((long long)b * a.hidden / G), hi = (int)((long long)(b + 1) * a.hidden / G);
-  for (int r = lo + (int)threadIdx.x; r < hi; r += kCT) {
-    float acc = 0.0f;
-    for (int s2 = 0; s2 < a.top_k; ++s2)
-      acc = fmaf(__ldcg(&a.contrib[(size_t)s2 * a.hidden + r]), __ldg(&w[s2]), acc);
-    xn[r] = __ldcg(&xl[r]) + acc;
-  }
-}
-
-template <int HU, int HD>
-__global__ void __launch_bounds__(kCT + 32, 2) nvfp4_moe_decode(DecodeArgs a, TmaCfg cu, TmaCfg cd) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int tid = threadIdx.x;
-  const int S = cu.stages;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [S], S <= 8
-  uint64_t* empty = full + 8;                         // [S]
-  int* jlist = reinterpret_cast<int*>(smem + 448);
-  float* part = reinterpret_cast<float*>(smem + cu.part_off);
-  float4* xs = reinterpret_cast<float4*>(smem + cu.xs_off);
-  float* lut = reinterpret_cast<float*>(smem + cu.lut_off);  // [256] of the current job
-  uint8_t* stages = smem + cu.stage_base;
-  const int P = 2 * a.layers;
-
-  if (tid == 0) {
-    for (int i = 0; i < S; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
-    }
-    fence_mbar_init();
-  }
-  if (tid < kMaxJobs) jlist[tid] = tid;  // every route slot is a job of every phase
-  __syncthreads();
-
-  // ------------------------------------------------------------ producer
-  if (tid >= kCT) {
-    if (tid == kCT) {
-      int it = 0;
-      bool ok = true;
-      for (int p = 0; p < P && ok; ++p) {
-        const TmaCfg& c = (p & 1) ? cd : cu;
-        const int rows = (p & 1) ? a.hidden : a.inter, cols = (p & 1) ? a.inter : a.hidden;
-        const int cb = cols >> 1, sb = cols >> 4;
-        ItemSeq q;
-        if (p & 1) {
-          cta_blocks_per_job(a.top_k, c.bpj, q);
-        } else {
-          cta_blocks(a.top_k * c.bpj, q);
-        }
-        int job, r0, nrows;
-        while (next_item(q, c, jlist, rows, job, r0, nrows)) {
-          const int st = it % S;
-          if (!mbar_wait(&empty[st], ((it / S) & 1) ^ 1)) {
-            ok = false;
-            break;
-          }
-          ++it;
-          const uint8_t *cc, *ss;
-          float g;
-          decode_job(a, p, job, cc, ss, g);
-          uint8_t* dst = stages + (size_t)st * cu.stage_bytes;
-          const uint32_t code_bytes = (uint32_t)(nrows * cb);
-          const uint32_t scale_bytes = (uint32_t)(nrows * sb);
-          const uint32_t s16 = scale_bytes & ~15u;
-          const uint8_t* ssrc = ss + (size_t)r0 * sb;
-          for (uint32_t i = s16; i < scale_bytes; ++i) dst[c.scale_off + i] = ssrc[i];
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          mbar_arrive_expect_tx(&full[st], code_bytes + s16);
-          bulk_g2s(dst, cc + (size_t)r0 * cb, code_bytes, &full[st]);
-          if (s16) bulk_g2s(dst + c.scale_off, ssrc, s16, &full[st]);
-        }
-      }
-      // Leave no bulk copy in flight: wait (bounded) for the last stages.
-      for (int k = (it > S ? it - S : 0); k < it; ++k) mbar_wait(&full[k % S], (k / S) & 1);
-    }
-    return;
-  }
-
-  // ----------------------------------------------------------- consumers
-  const int krt_max = (cu.kb * cu.blk > cd.kb * cd.blk) ? cu.kb * cu.blk : cd.kb * cd.blk;
-  for (int i = tid; i < krt_max * kRowPitch; i += kCT) part[i] = 0.0f;
-  const int tr = tid >> 3, tw = tid & 7;
-  float x[32];
-  bool dead = false;
-  int it = 0;
-  unsigned nbar = 0;  // grid barriers passed
-  named_bar_sync(kBarC, kCT);
-
-  for (int p = 0; p < P; ++p) {
-    const bool down = (p & 1) != 0;
-    const int l = p >> 1;
-    const TmaCfg& c = down ? cd : cu;
-    const int rows = down ? a.hidden : a.inter, cols = down ? a.inter : a.hidden;
-    const int cb = cols >> 1, sb = cols >> 4;
-    const int krt = down ? HD * 2 * cd.teams : HU * 2 * cu.teams;
-    const float* x_l = l == 0 ? a.x_in : a.xb + (size_t)((l - 1) & 1) * a.hidden;
-    // chain groups beyond this phase's units must read as zero in the tree
-    for (int i = tid; i < krt_max * kRowPitch; i += kCT) part[i] = 0.0f;
-    named_bar_sync(kBarC, kCT);
-    const float* cur_x = nullptr;
-    int cur_job = -1;
-    bool x_stale = true;
-    ItemSeq q;
-    if (down) {
-      cta_blocks_per_job(a.top_k, c.bpj, q);
-    } else {
-      cta_blocks(a.top_k * c.bpj, q);
-    }
-    int job, r0, nrows;
-    while (next_item(q, c, jlist, rows, job, r0, nrows)) {
-      const int st = it % S;
-      const uint32_t ph = (it / S) & 1;
-      ++it;
-      const float* xj = down ? a.act + (size_t)job * a.inter : x_l;
-      if (xj != cur_x || job != cur_job) {  // the previous item ended with a consumer barrier
-        if (xj != cur_x) {
-          const float4* src = reinterpret_cast<const float4*>(xj);
-          for (int f = tid; f < c.n_u * 8; f += kCT) {
-            const int t = f >> 3, i = f & 7;
-            xs[t * 8 + (i ^ (t & 7))] = __ldcg(src + f);
-          }
-          cur_x = xj;
-          x_stale = true;
-        }
-        if (job != cur_job) {
-          const uint8_t *cc, *ss;
-          float gs;
-          decode_job(a, p, job, cc, ss, gs);
-          lut[tid] = e4m3_lut_value((uint32_t)tid) * gs;
-          cur_job = job;
-        }
-        named_bar_sync(kBarC, kCT);
-      }
-      bool to = false;
-      if (!dead) to = !mbar_wait(&full[st], ph);
-      const uint32_t stage_off = (uint32_t)(cu.stage_base + st * cu.stage_bytes);
-      if (!dead && !to) {
-        if (down) {
-          decode_segments<HD>(c, tid, nrows == krt, smem, stage_off, cb, sb, nrows, lut, xs, x, x_stale,
-                              part);
-        } else {
-          decode_segments<HU>(c, tid, nrows == krt, smem, stage_off, cb, sb, nrows, lut, xs, x, x_stale,
-                              part);
-        }
-      }
-      dead = named_bar_or(kBarC, kCT, dead || to);
-      if (tid == 0 && !dead) mbar_arrive(&empty[st]);
-      float y = 0.0f;
-      if (!dead && tr < nrows) y = group_tree(part + tr * kRowPitch + tw * kGroupPitch);
-      y = combine8(y);
-      named_bar_sync(kBarC, kCT);  // the chain buffer is rewritten by the next item
-      if (!dead && tw == 0 && tr < nrows) {
-        const int r = r0 + tr;
-        if (!down) {
-          a.act[(size_t)job * a.inter + r] = epilogue(y, 1, 1.0f);
-        } else {
-          a.contrib[(size_t)job * a.hidden + r] = y;  // summed after the grid barrier
-        }
-      }
-    }
-    // every phase ends at a grid barrier; a down phase is followed by the
-    // slice-parallel route-order sum and (unless it was the last layer)
-    // another barrier before the next layer reads x_{l+1}
-    dead = grid_barrier(a.grid_bar, (unsigned)(++nbar * gridDim.x), dead);
-    if (down) {
-      if (!dead) sum_rows(a, l);
-      if (p + 1 < P) dead = grid_barrier(a.grid_bar, (unsigned)(++nbar * gridDim.x), dead);
-    }
   }
 }
 
@@ -881,7 +752,7 @@ int row_block(int cols) {
 
 bool tma_ok(const GemvBatch& b) {
   if (b.cols % 32 != 0 || b.cols > 4096) return false;
-  if (b.mode == 1 && (!b.contrib || !b.row_count)) return false;
+  if (b.mode == 1 && (!b.contrib || !b.grp_count)) return false;
   for (int j = 0; j < b.njobs; ++j) {
     const MatRef& m = b.job[j].mat;
     if (!al16(m.codes) || !al16(m.scales) || !al16(b.job[j].x)) return false;
@@ -907,6 +778,15 @@ int launch_ex(K kernel, dim3 grid, dim3 block, int smem, cudaStream_t stream, bo
 }
 
 constexpr int kCtasPerSm = 2;
+
+int max_h() {
+  static const int h = [] {
+    const char* e = getenv("ERVF_TMA_MAX_H");
+    const int v = e ? atoi(e) : 4;
+    return v < 1 ? 1 : (v > 4 ? 4 : v);
+  }();
+  return h;
+}
 
 // Cluster launch of the mode-1 (routed-sum) kernel: clusters of njobs CTAs,
 // as many as fit the SMs at two CTAs per SM; 0 when the cluster form does not
@@ -987,12 +867,13 @@ int launch_tma(const GemvBatch& b, cudaStream_t stream) {
   // PDL buys (29.0 vs 25.0 us per decode layer).
   const bool want_cluster = b.mode == 1 && !b.pdl && b.njobs >= 2 && b.njobs <= 8 && b.ep_ranks <= 1;
   // Largest H (rows per segment) whose chain buffer, activation and two
-  // stages fit two CTAs per SM, with kRt = teams * 2H <= 32 rows.
+  // stages fit two CTAs per SM, with kRt = teams * 2H <= 32 rows (capped by
+  // ERVF_TMA_MAX_H, a tuning knob read once per process; same results).
   int h = 0;
-  for (int cand = 4; cand >= 1; --cand) {
+  for (int cand = max_h(); cand >= 1; --cand) {
     const int krt = c.teams * 2 * cand;
     if (krt > 32 || krt % c.blk != 0) continue;
-    const int part_off = 576;  // after barriers, job tables and the active-job list
+    const int part_off = kPartOff;  // after barriers, job tables and the active-job list
     const int xs_off = align_up(part_off + krt * kRowPitch * 4, 16);
     const int lut_off = xs_off + c.n_u * 128;
     const int ysm_off = lut_off + 1024;
@@ -1023,44 +904,6 @@ int launch_tma(const GemvBatch& b, cudaStream_t stream) {
     case 2: return launch_h<2>(b, c, smem, stream);
     default: return launch_h<1>(b, c, smem, stream);
   }
-}
-
-// Persistent decode launch: item geometry of the up phase (cols = hidden)
-// and the down phase (cols = inter) with a shared stage ring and chain buffer.
-bool phase_cfg(int rows, int cols, int H, TmaCfg& c) {
-  c.n_u = cols / 32;
-  c.n2 = c.n_u > 64 ? c.n_u - 64 : 0;
-  c.teams = kCT / c.n_u;
-  if (c.teams > 16) c.teams = 16;
-  c.blk = row_block(cols);
-  const int krt = c.teams * 2 * H;
-  if (krt > 32 || krt % c.blk != 0) return false;
-  c.kb = krt / c.blk;
-  c.bpj = (rows + c.blk - 1) / c.blk;
-  c.scale_off = krt * (cols / 2);
-  return true;
-}
-
-template <int HU, int HD>
-int launch_decode_h(const DecodeArgs& a, TmaCfg cu, TmaCfg cd, int smem, cudaStream_t stream) {
-  auto kern = nvfp4_moe_decode<HU, HD>;
-  if (set_smem(kern, smem)) return kErrLaunch;
-  int nb = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kCT + 32, smem) != cudaSuccess)
-    return kErrLaunch;
-  if (nb < 1) return kErrShape;
-  if (nb > kCtasPerSm) nb = kCtasPerSm;
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(dev_info().sms * nb);
-  cfg.blockDim = dim3(kCT + 32);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;  // grid barriers need every CTA resident
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, a, cu, cd) == cudaSuccess ? kOk : kErrLaunch;
 }
 
 template <int W>
@@ -1095,47 +938,6 @@ int launch_nvfp4_batch(const GemvBatch& b, int width, cudaStream_t stream) {
     case 32: return launch_sched_w<32>(b, stream);
     default: return kErrArg;
   }
-}
-
-int launch_moe_decode(const DecodeArgs& a, cudaStream_t stream) {
-  const DevInfo& di = dev_info();
-  const int budget = (di.smem_sm - kCtasPerSm * 1024) / kCtasPerSm;
-  static const int combos[][2] = {{4, 4}, {4, 3}, {4, 2}, {4, 1}, {3, 3}, {2, 2}, {1, 1}};
-  for (const auto& hc : combos) {
-    TmaCfg cu{}, cd{};
-    if (!phase_cfg(a.inter, a.hidden, hc[0], cu) || !phase_cfg(a.hidden, a.inter, hc[1], cd)) continue;
-    const int krt_u = cu.kb * cu.blk, krt_d = cd.kb * cd.blk;
-    const int part_rows = krt_u > krt_d ? krt_u : krt_d;
-    const int stage_u = align_up(krt_u * (a.hidden / 2) + align_up(krt_u * (a.hidden / 16), 16), 128);
-    const int stage_d = align_up(krt_d * (a.inter / 2) + align_up(krt_d * (a.inter / 16), 16), 128);
-    const int stage = stage_u > stage_d ? stage_u : stage_d;
-    const int nu_max = cu.n_u > cd.n_u ? cu.n_u : cd.n_u;
-    const int part_off = 576;
-    const int xs_off = align_up(part_off + part_rows * kRowPitch * 4, 16);
-    const int lut_off = xs_off + nu_max * 128;
-    const int base = align_up(lut_off + 1024, 128);
-    if (base + 2 * stage > budget) continue;
-    int stages = (budget - base) / stage;
-    if (stages > 4) stages = 4;
-    for (TmaCfg* c : {&cu, &cd}) {
-      c->stages = stages;
-      c->stage_bytes = stage;
-      c->part_off = part_off;
-      c->xs_off = xs_off;
-      c->lut_off = lut_off;
-      c->stage_base = base;
-    }
-    const int smem = base + stages * stage;
-    const int hu = hc[0], hd = hc[1];
-    if (hu == 4 && hd == 4) return launch_decode_h<4, 4>(a, cu, cd, smem, stream);
-    if (hu == 4 && hd == 3) return launch_decode_h<4, 3>(a, cu, cd, smem, stream);
-    if (hu == 4 && hd == 2) return launch_decode_h<4, 2>(a, cu, cd, smem, stream);
-    if (hu == 4 && hd == 1) return launch_decode_h<4, 1>(a, cu, cd, smem, stream);
-    if (hu == 3) return launch_decode_h<3, 3>(a, cu, cd, smem, stream);
-    if (hu == 2) return launch_decode_h<2, 2>(a, cu, cd, smem, stream);
-    return launch_decode_h<1, 1>(a, cu, cd, smem, stream);
-  }
-  return kErrShape;
 }
 
 }  // namespace ervf

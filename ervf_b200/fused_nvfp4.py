@@ -270,12 +270,14 @@ class FusedNVFP4:
     def moe_batched(self, up_codes, up_scales, up_code_stride: int, up_scale_stride: int,
                     dn_codes, dn_scales, dn_code_stride: int, dn_scale_stride: int, globals_,
                     ids, w, tokens: int, top_k: int, n_experts: int, x, out, hidden: int,
-                    inter: int, scratch=None, ksplit: int = 1) -> None:
+                    inter: int, scratch=None, ksplit: int = 1, swiglu: bool = False) -> None:
         """Expert-major batched routed-MoE block of `tokens` decode tokens on
         the tensor cores: out[t] = x[t] + sum over route slots (in order) of
         w[t,s] * down(relu(up(x[t]))^2) with each expert read once.
         ``ksplit`` 2 splits the columns of every tensor-core unit over two CTAs
-        (deterministic; more parallelism for small batches or expert shards)."""
+        (deterministic; more parallelism for small batches or expert shards).
+        ``swiglu``: up records of 2*inter rows (gate / up interleaved),
+        act = silu(gate) * up (the Qwen3-shaped block)."""
         nbytes = _lib.load().ervf_moe_batched_scratch_bytes(int(tokens), int(top_k), int(hidden),
                                                             int(inter))
         if scratch is None:
@@ -286,14 +288,22 @@ class FusedNVFP4:
                   int(up_scale_stride), ptr(dn_codes), ptr(dn_scales), int(dn_code_stride),
                   int(dn_scale_stride), ptr(globals_), ptr(ids), ptr(w), int(tokens), int(top_k),
                   int(n_experts), ptr(x), ptr(out), int(hidden), int(inter), int(ksplit),
-                  ptr(scratch), int(nbytes), self._s())
+                  _lib.UP_SWIGLU if swiglu else 0, ptr(scratch), int(nbytes), self._s())
 
     def gemm_tc(self, out, codes, scales, x, global_scale: float, rows: int, cols: int,
                 n: int) -> None:
         """Batched NVFP4 GEMM on the tensor cores for n <= 16 activation rows:
-        out[j*rows + r] = g * (W @ x[j])[r] (tolerance path, fp32 accumulate)."""
+        out[j*rows + r] = g * (W @ x[j])[r] (tolerance path, fp32 accumulate,
+        deterministic).  Uses a scratch buffer owned by this object per shape
+        (calls through one FusedNVFP4 on different streams must not overlap)."""
+        key = ("tc", int(rows), int(cols), int(n))
+        cache = self.__dict__.setdefault("_scratch_cache", {})
+        if key not in cache:
+            nb = int(_lib.load().ervf_nvfp4_gemm_tc_scratch_bytes(int(rows), int(cols), int(n)))
+            cache[key] = torch.zeros(nb, dtype=torch.uint8, device=self.device)
+        scr = cache[key]
         _lib.call("ervf_nvfp4_gemm_tc", ptr(codes), ptr(scales), float(np.float32(global_scale)),
-                  ptr(x), ptr(out), int(rows), int(cols), int(n), self._s())
+                  ptr(x), ptr(out), int(rows), int(cols), int(n), ptr(scr), scr.numel(), self._s())
 
     def route_topk_softmax(self, rlogs, ids, w, layers: int, n: int, top_k: int) -> None:
         """Softmax top-k routing (Qwen-shaped experts) of `layers` logit rows:

@@ -95,14 +95,17 @@ class ExpertBank:
 
     @classmethod
     def synthetic(cls, n_layers: int, n_experts: int, hidden: int, inter: int, device=None,
-                  seed: int = 0, std: float = 0.02) -> "ExpertBank":
+                  seed: int = 0, std: float = 0.02, rank: int = 0,
+                  world: int = 1) -> "ExpertBank":
         """Seeded synthetic bank built on the device: weights ~ N(0, std)
         from a torch generator seeded with seed*1e6 + 1000*layer + expert
-        (+0 up, +500 down), quantised by ``quantize_nvfp4_torch``."""
+        (+0 up, +500 down), quantised by ``quantize_nvfp4_torch``.  With
+        world > 1 only the experts this rank owns (e % world == rank) are
+        built; the others stay uninitialised."""
         bank = cls(n_layers, n_experts, hidden, inter, device)
         gen = torch.Generator(device=bank.device)
         for layer in range(n_layers):
-            for e in range(n_experts):
+            for e in range(rank, n_experts, world):
                 recs = []
                 for off, (r, c) in ((0, (inter, hidden)), (500, (hidden, inter))):
                     gen.manual_seed(seed * 1_000_000 + 1000 * layer + e + off)
@@ -159,17 +162,10 @@ class MoEDecoder:
             self.xchg = PeerExchange(group, ep_ranks, ep_rank, bank.hidden, k, d)
         self.graph = None
         self.pdl = True
-        # persistent=True: one cooperative launch for all layers of the token
-        # (single GPU, bit-identical).  Off by default: on B200 the chain of
-        # PDL-overlapped per-layer launches is faster at batch 1 (0.61 vs
-        # 0.67 ms per 24-layer token); the three grid barriers per layer
-        # cost ~2.5-3 us each, mostly waiting for the slowest CTA.
-        self.persistent = False
-        self.table = torch.tensor(
-            [[ptr(bank.up_codes[l]), ptr(bank.up_scales[l]), ptr(bank.dn_codes[l]),
-              ptr(bank.dn_scales[l]), ptr(bank.globals[l])] for l in range(L)],
-            dtype=torch.int64, device=d)
-        nb = _lib.load().ervf_decode_scratch_bytes(bank.hidden, k)
+        # L2 prefetch of the next launch's routed expert records (a hint:
+        # results are the same with it off)
+        self.prefetch = True
+        nb = _lib.load().ervf_routesum_scratch_bytes(bank.hidden, k)
         self.scratch = torch.zeros(nb, dtype=torch.uint8, device=d)
 
     def _s(self) -> int:
@@ -189,16 +185,21 @@ class MoEDecoder:
         if self.ep_ranks == 1:
             # The routing launch precedes the first up launch directly, so
             # that one must wait before reading ids; every later launch may
-            # start streaming its experts while its predecessor drains.
-            up_flags = _lib.LAUNCH_PDL | (0 if first else _lib.LAUNCH_IDS_READY)
-            dn_flags = _lib.LAUNCH_PDL | _lib.LAUNCH_IDS_READY
+            # start streaming its experts while its predecessor drains.  The
+            # up launch queues this layer's down records into L2, the down
+            # launch the next layer's up records (routes of every layer are
+            # known before the step).
+            flags = _lib.LAUNCH_PDL | (0 if first else _lib.LAUNCH_IDS_READY)
             if not self.pdl:
-                up_flags = dn_flags = 0
-            f.moe_up_grouped(b.up_codes[l], b.up_scales[l], b.up_code_bytes, b.up_scale_bytes, ids,
-                             b.globals[l], k, x, self.act, b.inter, b.hidden, flags=up_flags)
-            f.moe_down_routesum(b.dn_codes[l], b.dn_scales[l], b.dn_code_bytes, b.dn_scale_bytes,
-                                ids, b.globals[l], w, k, self.act, out, b.hidden, b.inter, resid=x,
-                                flags=dn_flags)
+                flags = 0
+            nxt = l + 1 if (self.prefetch and l + 1 < b.n_layers) else None
+            pf = (ptr(b.up_codes[nxt]), ptr(b.up_scales[nxt]), ptr(self.ids[nxt])) if nxt is not None \
+                else (0, 0, 0)
+            _lib.call("ervf_moe_layer", ptr(b.up_codes[l]), ptr(b.up_scales[l]), int(b.up_code_bytes),
+                      int(b.up_scale_bytes), ptr(b.dn_codes[l]), ptr(b.dn_scales[l]),
+                      int(b.dn_code_bytes), int(b.dn_scale_bytes), ptr(ids), ptr(b.globals[l]),
+                      ptr(w), k, ptr(x), ptr(self.act), ptr(out), b.hidden, b.inter, b.n_experts,
+                      ptr(self.scratch), self.scratch.numel(), *pf, flags, self._s())
             return
         if self.xchg is not None:
             from .ep import exchange_buffer
@@ -324,13 +325,6 @@ class MoEDecoder:
         router logits of every layer.  Returns the buffer holding x after
         the last layer."""
         self.route(rlogs)
-        b = self.bank
-        if self.persistent and self.ep_ranks == 1:
-            _lib.call("ervf_moe_decode", ptr(self.table), int(b.up_code_bytes), int(b.up_scale_bytes),
-                      int(b.dn_code_bytes), int(b.dn_scale_bytes), ptr(self.ids), ptr(self.w),
-                      b.n_layers, self.top_k, ptr(x_in), ptr(self.xbuf), ptr(self.act), b.hidden,
-                      b.inter, ptr(self.scratch), self.scratch.numel(), self._s())
-            return self.xs[(b.n_layers - 1) & 1]
         cur = x_in
         for l in range(self.bank.n_layers):
             nxt = self.xs[l & 1]

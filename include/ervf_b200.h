@@ -119,9 +119,13 @@ ERVF_API int ervf_moe_up_grouped(const uint8_t* up_codes, const uint8_t* up_scal
  * contract runtime.py:588-596).
  * scratch: caller-owned device buffer of ervf_routesum_scratch_bytes(hidden,
  * top_k) bytes, 16-byte aligned, zero-filled once before its first use; each
- * call leaves it ready for the next (calls that share it must not overlap on
- * the GPU).  With scratch the rows spread over all SMs; scratch = NULL runs a
- * slower schedule that needs none. */
+ * call that completes leaves it ready for the next (calls that share it must
+ * not overlap on the GPU).  After ervf_device_status reports
+ * ERVF_ERR_TIMEOUT, zero it again before reusing it.  With scratch the rows
+ * spread over all SMs; scratch = NULL runs a slower schedule that needs none.
+ * Without ERVF_LAUNCH_PDL and with 2 <= top_k <= 8 the sum runs through a
+ * thread-block cluster (distributed shared memory) and leaves the scratch
+ * untouched; otherwise every launch uses it.  Same bits either way. */
 ERVF_API int ervf_moe_down_routesum(const uint8_t* dn_codes, const uint8_t* dn_scales,
                            size_t dn_code_stride, size_t dn_scale_stride, const int32_t* ids,
                            const float* globals, const float* route_w, int top_k, const float* act,
@@ -131,42 +135,42 @@ ERVF_API int ervf_moe_down_routesum(const uint8_t* dn_codes, const uint8_t* dn_s
 /* Bytes of scratch ervf_moe_down_routesum uses for (hidden, top_k). */
 ERVF_API size_t ervf_routesum_scratch_bytes(int hidden, int top_k);
 
-/* All routed-MoE layers of one decode token in one cooperative launch: for
- * l = 0..layers-1, act[s] = relu(up_{e}(x_l))^2 for the route slots s with
- * experts e = ids[l*top_k + s], then x_{l+1} = x_l + acc with acc =
- * fmaf(down_e(act[s]), route_w[l*top_k + s], acc) over s in route order from
- * 0.0 -- bit-identical to the per-layer ervf_moe_up_grouped +
- * ervf_moe_down_routesum chain (fused_nvfp4.py:970-984, route order
- * runtime.py:588-596; the reference runs one launch per expert GEMV).
- * layer_table: device array [layers][5] of 64-bit addresses (up codes, up
- * scales, down codes, down scales, globals f32[E][2] = (g_down, g_up)) of each
- * layer's expert bank, records `*_stride` bytes apart (16-byte multiples).
- * x_in [hidden]; xbuf [2][hidden]: layer l writes xbuf[(l & 1) * hidden], so the
- * result is xbuf[((layers - 1) & 1) * hidden]; act [top_k][inter]; scratch:
- * ervf_decode_scratch_bytes(hidden, top_k) bytes (route-slot outputs and the
- * grid-barrier counter; calls that share it must not overlap).  hidden,
- * inter: multiples of 32, <= 4096; top_k <= 16.  One cudaMemsetAsync precedes
- * the launch.  No counterpart in the reference. */
-ERVF_API int ervf_moe_decode(const void* layer_table, size_t up_code_stride,
-                             size_t up_scale_stride, size_t dn_code_stride,
-                             size_t dn_scale_stride, const int32_t* ids, const float* route_w,
-                             int layers, int top_k, const float* x_in, float* xbuf, float* act,
-                             int hidden, int inter, void* scratch, size_t scratch_bytes,
-                             void* stream);
-
-/* Bytes of scratch ervf_moe_decode uses for (hidden, top_k). */
-ERVF_API size_t ervf_decode_scratch_bytes(int hidden, int top_k);
+/* One routed-MoE layer of one token, two launches: act[s] =
+ * relu(up_{ids[s]}(x))^2, then out[r] = x[r] + acc with acc =
+ * fmaf(down_{ids[s]}(act[s])[r], route_w[s], acc) over s = 0..top_k-1 in route
+ * order from 0.0 -- bit-identical to ervf_moe_up_grouped followed by
+ * ervf_moe_down_routesum(resid = x), i.e. to the reference's per-expert
+ * gemv_into + accumulate_into sequence (fused_nvfp4.py:970-984, route order
+ * runtime.py:571-596).  Adds an L2 prefetch: the up launch queues this
+ * layer's routed down records into L2, and the down launch queues the next
+ * layer's routed up records (next_up_codes / next_up_scales / next_ids, same
+ * strides as this layer's up bank; all three NULL for none), so that expert
+ * weights stream from HBM under the previous launch's compute.  The hint
+ * never changes results; prefetch ids are clamped to [0, n_experts).
+ * scratch: as for ervf_moe_down_routesum (zeroed once, left ready).  All
+ * pointers and record strides 16-byte aligned; hidden, inter multiples of 32,
+ * <= 4096; top_k <= 16.  B200 schedule only. */
+ERVF_API int ervf_moe_layer(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_code_stride,
+                            size_t up_scale_stride, const uint8_t* dn_codes, const uint8_t* dn_scales,
+                            size_t dn_code_stride, size_t dn_scale_stride, const int32_t* ids,
+                            const float* globals, const float* route_w, int top_k, const float* x,
+                            float* act, float* out, int hidden, int inter, int n_experts,
+                            void* scratch, size_t scratch_bytes, const uint8_t* next_up_codes,
+                            const uint8_t* next_up_scales, const int32_t* next_ids, int flags,
+                            void* stream);
 
 /* ervf_moe_down_routesum without a scratch argument.  No counterpart in the
  * reference.  The scratch is a fixed device array inside the library, so the
  * call allocates nothing: hidden <= 8192 and top_k <= 8, else
  * ERVF_ERR_SCRATCH_LIMIT before anything runs.  The first call on a device
  * looks up the array's address with that device current; make it before any
- * stream capture begins.  Each call clears the array's row counters with
- * cudaMemsetAsync on `stream`, then launches without programmatic dependent
- * launch (the PDL / IDS_READY bits of `flags` are ignored).  All calls on a
- * device share the one array: calls that overlap on the GPU race.  Results
- * are bit-identical to ervf_moe_down_routesum. */
+ * stream capture begins.  Each call clears the array's group counters with
+ * cudaMemsetAsync on `stream` before its launch.  `flags` as for
+ * ervf_moe_down_routesum: with ERVF_LAUNCH_PDL (or top_k == 1) the route sum
+ * runs through the array; without it, 2..8 slots take the cluster route sum,
+ * which needs no scratch.  All calls on a device share the one array: calls
+ * that overlap on the GPU race.  Results are bit-identical to
+ * ervf_moe_down_routesum. */
 ERVF_API int ervf_moe_down_routesum_static(const uint8_t* dn_codes, const uint8_t* dn_scales,
                                            size_t dn_code_stride, size_t dn_scale_stride,
                                            const int32_t* ids, const float* globals,
@@ -313,17 +317,54 @@ ERVF_API int ervf_route_topk_batched(const float* rlog, const float* gate_b, int
                                      int layers, int n, int top_k, float scaling, int bad_pick,
                                      int bias_stride, void* stream);
 
-/* Batched NVFP4 GEMM on the sm_100a tensor cores (tcgen05.mma, fp32
- * accumulator in tensor memory): out[j*rows + r] = g * sum_k W[r][k] *
- * x[j*cols + k] for the j < n <= 16 activation rows of a decode batch.  W is
- * decoded exactly to f16 (e2m1 x E4M3), x is rounded to f16, g is applied to
- * the fp32 result: held to rel-L2 <= 1e-3 against the FP32 dequantise-then-
- * matmul, not to the batch-1 chain order.  cols % 32 == 0; codes 16-byte,
- * x 16-byte aligned.  Replaces the batched SIMT gemm_nvfp4_rows_b
- * (sweepspec.py:28-240) for one matrix. */
+/* SweepMoE (sweepspec.py:244-375) building blocks.
+ *
+ * ervf_nvfp4_gemm_rows_b: out[b*rows + r] = op(W x[nodes[b]])[r] for b < n
+ * <= 16, each column bit-identical to the reference's gemm_nvfp4_rows_b
+ * (sweepspec.py:28-141), i.e. to gemv_nvfp4_rows on that activation row (the
+ * legacy 256-chain tree); op = relu(v)^2 when apply_relu2.  x is [*][cols]
+ * with rows picked by the device list nodes[n]; xbuf: caller scratch of
+ * n*cols floats, 16-byte aligned (the gathered rows). */
+ERVF_API int ervf_nvfp4_gemm_rows_b(const uint8_t* codes, const uint8_t* scales, const float* x,
+                                   const int32_t* nodes, float* out, float global_scale, int rows,
+                                   int cols, int n, int apply_relu2, float* xbuf, void* stream);
+
+/* ervf_down_union: contrib[dst[b]*hidden + r] = the masked panel-major down
+ * projection of acts[b*inter ..] (the record at `bank`, runtime.py:34-52
+ * layout), b < n <= 64 -- bit-identical to the reference's down_union
+ * (gemm_down_masked_b over the union panel mask + reduce_partials_scatter,
+ * sweepspec.py:143-216: a column where node b is zero adds fmaf(w, 0, acc) =
+ * acc, so the union mask and b's own mask give the same bits).  masks ..
+ * nzc: the masked-down state of ervf_down_masked; tmp: n*hidden floats. */
+ERVF_API int ervf_down_union(const uint8_t* bank, const float* acts, int n, const int32_t* dst,
+                            float* contrib, float global_scale, int hidden, int inter, int nchunks,
+                            uint32_t* masks, int32_t* plist, int32_t* pcount, int32_t* nz,
+                            int32_t* nzc, float* tmp, void* stream);
+
+/* ervf_reduce_slots: out[b*rows + r] = fmaf(weights[b*top_k + s],
+ * contrib[(b*top_k + s)*rows + r], .) over s = 0..top_k-1 in route-slot
+ * order, starting from out's value (reduce_slots, sweepspec.py:219-240). */
+ERVF_API int ervf_reduce_slots(const float* contrib, const float* weights, float* out, int rows,
+                              int top_k, int B, void* stream);
+
+/* Batched NVFP4 GEMM on the tensor cores for decode batches:
+ * out[b*rows + r] = global_scale * sum_k W[r][k] * x[b*cols + k] for b < n <= 16,
+ * W the NVFP4 matrix (codes + E4M3 block scales as in ervf_nvfp4_gemv).
+ * Weights decoded exactly to f16, x rounded to f16, fp32 accumulate in tensor
+ * memory: held to rel-L2 <= 1e-3 against a float64 dequantise-then-matmul,
+ * not to the batch-1 chain order.  Deterministic: a K split (used when the
+ * row tiles alone leave SMs idle) adds its partials in split order, so the
+ * bits do not change from run to run.  cols % 32 == 0, cols <= 4096; codes,
+ * scales and x 16-byte aligned.  scratch: ervf_nvfp4_gemm_tc_scratch_bytes
+ * (rows, cols, n) bytes, 16-byte aligned, zero-filled once (its split
+ * counters are left zero by every call that completes).  Replaces the batched
+ * SIMT gemm_nvfp4_rows_b (sweepspec.py:28-240) for one matrix. */
 ERVF_API int ervf_nvfp4_gemm_tc(const uint8_t* codes, const uint8_t* scales, float global_scale,
                                 const float* x, float* out, int rows, int cols, int n,
-                                void* stream);
+                                void* scratch, size_t scratch_bytes, void* stream);
+
+/* Bytes of scratch ervf_nvfp4_gemm_tc uses for (rows, cols, n). */
+ERVF_API size_t ervf_nvfp4_gemm_tc_scratch_bytes(int rows, int cols, int n);
 
 /* Batched BF16 GEMM on the tensor cores for the dense projections:
  * out[b*rows + r] = sum_k W[r][k] * x[b*cols + k] for b < batch <= 8, fp32
@@ -340,10 +381,15 @@ ERVF_API int ervf_bf16_gemm_tc(const uint16_t* W, const float* x, float* out, in
  * every expert is read once for all the tokens routed to it (chunks of <= 16
  * tokens as the MMA's N columns), act = relu(up(x))^2, contrib = down(act),
  * then out[t] = x[t] + acc, acc = fmaf(contrib[t,s], w[t,s], acc) over s in
- * route order.  Four launches (lists, up, down, route sum).  Tolerance path
- * (rel-L2 <= 1e-3; weights exact in f16, x and act rounded to f16).  Bank as
- * in ervf_moe_up_grouped / ervf_moe_down_routesum; tokens*top_k <= 4096,
- * n_experts <= 1024; scratch: ervf_moe_batched_scratch_bytes(...) bytes. */
+ * route order.  Five launches (lists, activation panels, up, down, route
+ * sum); up and down run on the warp-specialised tensor-core kernel, the up
+ * epilogue writing act as f16 straight into the down launch's activation
+ * panels.  Tolerance path (rel-L2 <= 1e-3; weights exact in f16, x and act
+ * rounded to f16).  Bank as in ervf_moe_up_grouped / ervf_moe_down_routesum,
+ * records contiguous (code stride = rows * cols / 2, scale stride = rows *
+ * cols / 16, 16-byte aligned); hidden, inter multiples of 32, <= 4096;
+ * tokens*top_k <= 4096, n_experts <= 1024; scratch:
+ * ervf_moe_batched_scratch_bytes(...) bytes, 16-byte aligned. */
 ERVF_API int ervf_moe_batched(const uint8_t* up_codes, const uint8_t* up_scales,
                               size_t up_code_stride, size_t up_scale_stride,
                               const uint8_t* dn_codes, const uint8_t* dn_scales,
@@ -358,15 +404,17 @@ ERVF_API int ervf_moe_batched(const uint8_t* up_codes, const uint8_t* up_scales,
  * accumulators in split order before the global scale -- more CTAs for a
  * small batch or a small expert shard.  Deterministic; the result depends on
  * ksplit (association of the partial sums), not on the grid, the arrival
- * order or the rank.  No counterpart in the reference. */
+ * order or the rank.  flags: ERVF_UP_SWIGLU for SwiGLU experts (up records of
+ * 2*inter rows, gate / up interleaved; act = silu(gate) * up with CUDA expf,
+ * the Qwen3-shaped block).  No counterpart in the reference. */
 ERVF_API int ervf_moe_batched_ex(const uint8_t* up_codes, const uint8_t* up_scales,
                                  size_t up_code_stride, size_t up_scale_stride,
                                  const uint8_t* dn_codes, const uint8_t* dn_scales,
-                                 size_t dn_code_stride, size_t dn_scale_stride,
-                                 const float* globals, const int32_t* ids, const float* route_w,
-                                 int tokens, int top_k, int n_experts, const float* x, float* out,
-                                 int hidden, int inter, int ksplit, void* scratch,
-                                 size_t scratch_bytes, void* stream);
+                                 size_t dn_code_stride, size_t dn_scale_stride, const float* globals,
+                                 const int32_t* ids, const float* route_w, int tokens, int top_k,
+                                 int n_experts, const float* x, float* out, int hidden, int inter,
+                                 int ksplit, int flags, void* scratch, size_t scratch_bytes,
+                                 void* stream);
 
 /* Bytes of scratch ervf_moe_batched uses. */
 ERVF_API size_t ervf_moe_batched_scratch_bytes(int tokens, int top_k, int hidden, int inter);

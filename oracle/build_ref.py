@@ -14,6 +14,7 @@ Sources used:
   src/moe_lab/lightningstream_nemotron/fused_nvfp4.py        _KERNEL_SOURCE
   scripts/nervf_nemotron/nervf01_geometry_audit.py           _ERVF_TEMPLATE (W = 4, 8, 32)
   src/moe_lab/lightningstream_nemotron/gpu_kernels.py        _SOURCE (gemv_bf16, gemv_f32)
+  src/moe_lab/lightningstream_nemotron/sweepspec.py          _SOURCE (SweepMoE's batched kernels)
 """
 
 from __future__ import annotations
@@ -28,12 +29,15 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
 LIB = OUT / "libervf_ref.so"
-REF = Path(os.environ.get("ERVF_REFERENCE", "/root/reference"))
+# The kennydd001/ervf checkout: $ERVF_REFERENCE, else a directory named
+# `reference` beside this repository's root.
+REF = Path(os.environ.get("ERVF_REFERENCE") or HERE.parent.parent / "reference")
 
 FILES = {
     "fused": ("src/moe_lab/lightningstream_nemotron/fused_nvfp4.py", "_KERNEL_SOURCE"),
     "ervf": ("scripts/nervf_nemotron/nervf01_geometry_audit.py", "_ERVF_TEMPLATE"),
     "gpu": ("src/moe_lab/lightningstream_nemotron/gpu_kernels.py", "_SOURCE"),
+    "sweep": ("src/moe_lab/lightningstream_nemotron/sweepspec.py", "_SOURCE"),
 }
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -63,10 +67,12 @@ def build(force: bool = False) -> Path | None:
     for w in (4, 8, 32):
         (OUT / f"ref_ervf_w{w}.cu").write_text(tmpl.replace("__W__", str(w)))
     (OUT / "ref_gpu_kernels.cu").write_text(literal(REF / FILES["gpu"][0], FILES["gpu"][1]))
+    (OUT / "ref_sweep.cu").write_text(literal(REF / FILES["sweep"][0], FILES["sweep"][1]))
 
     launch = HERE / "ref_launch.cu"
     units = [("fused", ["-DREF_FUSED", "-std=c++14"]),
-             ("gpu", ["-DREF_GPU_KERNELS", "-std=c++14", "--use_fast_math"])]
+             ("gpu", ["-DREF_GPU_KERNELS", "-std=c++14", "--use_fast_math"]),
+             ("sweep", ["-DREF_SWEEP", "-std=c++14"])]
     for w in (4, 8, 32):
         units.append((f"ervf_w{w}", ["-DREF_ERVF_W=%d" % w, "-std=c++14",
                                      f"-DREF_KERNEL_NAME=ref_kernel_ervf_w{w}",

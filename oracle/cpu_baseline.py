@@ -12,6 +12,7 @@ tables (E4M3 NaN -> 0), then ``torch.matmul``.
 from __future__ import annotations
 
 import os
+import time
 
 import numpy as np
 import torch
@@ -61,3 +62,22 @@ def moe_layer(x: torch.Tensor, experts, ids, weights, hidden: int, inter: int) -
         dn = dequant(dc, ds, dg, hidden, inter)
         out += float(weights[s]) * (dn @ h)
     return out
+
+
+def moe_layer_timed(x: torch.Tensor, experts, ids, weights, hidden: int, inter: int):
+    """moe_layer with the two phases timed apart: returns (out, dequant_s,
+    matmul_s), the seconds spent dequantising the routed experts and in the
+    matmuls (+ relu^2 and the weighted sum)."""
+    out = x.clone()
+    t_dq = t_mm = 0.0
+    for s, e in enumerate(ids):
+        (uc, us, ug), (dc, ds, dg) = experts[int(e)]
+        t0 = time.perf_counter()
+        up = dequant(uc, us, ug, inter, hidden)
+        dn = dequant(dc, ds, dg, hidden, inter)
+        t1 = time.perf_counter()
+        h = torch.clamp(up @ x, min=0.0) ** 2
+        out += float(weights[s]) * (dn @ h)
+        t_mm += time.perf_counter() - t1
+        t_dq += t1 - t0
+    return out, t_dq, t_mm

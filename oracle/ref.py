@@ -28,6 +28,11 @@ SIGS = {
     "ref_cache_assign": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp],
     "ref_gemv_bf16": [_vp, _vp, _vp, _i, _i, _vp],
     "ref_gemv_f32": [_vp, _vp, _vp, _i, _i, _vp],
+    "ref_panel_scan": [_vp, _i, _vp, _vp, _vp, _vp, _vp, _vp],
+    "ref_gemm_rows_b": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp],
+    "ref_down_masked_b": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp],
+    "ref_reduce_partials_scatter": [_vp, _vp, _vp, _i, _i, _i, _vp],
+    "ref_reduce_slots": [_vp, _vp, _vp, _i, _i, _i, _vp],
 }
 
 _lib = None

@@ -16,6 +16,10 @@
 //   cache_assign         fused_nvfp4.py:803-808
 //   gemv_bf16            gpu_kernels.py:1549-1551
 //   gemv_f32             gpu_kernels.py:1553-1555
+//   panel_scan           fused_nvfp4.py:157-187 (as down_union calls it, sweepspec.py:339-343)
+//   SweepMoE kernels     sweepspec.py:317-375 (gemm_nvfp4_rows_b grid rows, block 256, smem
+//                        n*cols*4; gemm_down_masked_b grid (ceil(hidden/128), nchunks), block
+//                        128; reduce_partials_scatter / reduce_slots grid ceil(rows/256), 256)
 // Only tests/ and bench.py's reference leg load this library.
 #include <cuda_runtime.h>
 #include <stddef.h>
@@ -78,6 +82,12 @@ REF_API int ref_down_masked(float* out, const unsigned char* bank, const float* 
   return ref_status();
 }
 
+REF_API int ref_panel_scan(const float* act, int inter, unsigned int* masks, int* plist, int* pcount,
+                           int* nz, int* nzc, void* stream) {
+  panel_scan<<<1, 256, 0, (cudaStream_t)stream>>>(act, inter, masks, plist, pcount, nz, nzc);
+  return ref_status();
+}
+
 REF_API int ref_route_topk(const float* rlog, const float* gate_b, int* ids, float* w, int n, int top_k,
                            float scaling, int bad_pick, void* stream) {
   route_topk_f32<<<1, 128, 0, (cudaStream_t)stream>>>(rlog, gate_b, ids, w, n, top_k, scaling,
@@ -102,6 +112,45 @@ REF_API int REF_LAUNCH_NAME(const unsigned char* codes, const unsigned char* sca
   const int rpb = 256 / REF_ERVF_W;
   REF_KERNEL_NAME<<<(rows + rpb - 1) / rpb, 256, cols * 4, (cudaStream_t)stream>>>(
       codes, scales, e2m1, e4m3, x, out, g, rows, cols, relu2, out_scale);
+  return ref_status();
+}
+
+#elif defined(REF_SWEEP)
+#include "ref_sweep.cu"
+
+REF_API int ref_gemm_rows_b(const unsigned char* codes, const unsigned char* scales, const float* e2m1,
+                            const float* e4m3, const float* x, const int* nodes, float* out, float g,
+                            int rows, int cols, int B, int relu2, void* stream) {
+  const int shared = B * cols * 4;
+  if (cudaFuncSetAttribute(gemm_nvfp4_rows_b, cudaFuncAttributeMaxDynamicSharedMemorySize, shared) !=
+      cudaSuccess)
+    return -4;
+  gemm_nvfp4_rows_b<<<rows, 256, shared, (cudaStream_t)stream>>>(codes, scales, e2m1, e4m3, x, nodes, out,
+                                                                 g, rows, cols, B, relu2);
+  return ref_status();
+}
+
+REF_API int ref_down_masked_b(const unsigned char* bank, const float* act, const int* plist,
+                              const unsigned int* masks, const int* pcount, const float* e2m1,
+                              const float* e4m3, float* partials, float g, int hidden, int inter, int B,
+                              int nchunks, void* stream) {
+  dim3 grid((hidden + 127) / 128, nchunks);
+  gemm_down_masked_b<<<grid, 128, 0, (cudaStream_t)stream>>>(bank, act, plist, masks, pcount, e2m1, e4m3,
+                                                             partials, g, hidden, inter, B);
+  return ref_status();
+}
+
+REF_API int ref_reduce_partials_scatter(const float* partials, const int* dst, float* contrib, int rows,
+                                        int nchunks, int B, void* stream) {
+  reduce_partials_scatter<<<(rows + 255) / 256, 256, 0, (cudaStream_t)stream>>>(partials, dst, contrib,
+                                                                               rows, nchunks, B);
+  return ref_status();
+}
+
+REF_API int ref_reduce_slots(const float* contrib, const float* weights, float* out, int rows, int top_k,
+                             int B, void* stream) {
+  reduce_slots<<<(rows + 255) / 256, 256, 0, (cudaStream_t)stream>>>(contrib, weights, out, rows, top_k,
+                                                                     B);
   return ref_status();
 }
 

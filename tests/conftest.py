@@ -50,11 +50,21 @@ def rng(seed):
     return np.random.default_rng(seed)
 
 
-def random_nvfp4(rows, cols, seed, nan_scales=False):
+def random_nvfp4(rows, cols, seed, nan_scales=False, full_range=False):
     """Random codes and block scales (bytes), as the reference's verifiers use
-    (e1f21_independent_verify.py:173-176); scale bytes avoid huge values."""
+    (e1f21_independent_verify.py:173-176).  By default the scale bytes avoid
+    huge values (0x20-0x4F); full_range=True draws every byte 0x00-0xFF:
+    negative scales (0x80-0xFE), subnormal (0x01-0x07), large (0x50-0x7E),
+    zero and the NaN bytes 0x7F / 0xFF."""
     r = rng(seed)
     codes = r.integers(0, 256, size=rows * cols // 2, dtype=np.uint8)
+    if full_range:
+        scales = r.integers(0, 256, size=rows * cols // 16, dtype=np.uint8)
+        # make sure every class is present even in small cases
+        special = np.array([0x00, 0x01, 0x07, 0x50, 0x7E, 0x7F, 0x80, 0x81, 0xFE, 0xFF], np.uint8)
+        scales[:min(special.size, scales.size)] = special[:scales.size]
+        g = np.float32(r.uniform(1e-4, 1e-2))
+        return codes, scales, g
     scales = r.integers(0x20, 0x50, size=rows * cols // 16, dtype=np.uint8)
     if nan_scales:
         idx = r.choice(scales.size, size=max(1, scales.size // 50), replace=False)
@@ -95,3 +105,21 @@ def rel_l2(a, b) -> float:
     b = np.asarray(b, np.float64)
     n = np.linalg.norm(b)
     return float(np.linalg.norm(a - b) / (n if n > 0 else 1.0))
+
+
+def dequant_torch(codes, scales, g, rows, cols, dtype=None):
+    """float64 (default) dequantisation on the tensors' device: E2M1 code x
+    E4M3 block scale (NaN bytes -> 0, as the kernels' tables) x global scale.
+    A tolerance reference for the tensor-core paths."""
+    import torch
+
+    from ervf_b200.formats import e2m1_table, e4m3_device_table
+
+    dtype = dtype or torch.float64
+    dev = codes.device
+    e2 = torch.from_numpy(e2m1_table()).to(dev, dtype)
+    e4 = torch.from_numpy(e4m3_device_table()).to(dev, dtype)
+    c = codes.reshape(rows, cols // 2).long()
+    nib = torch.stack([c & 15, c >> 4], dim=2).reshape(rows, cols)
+    s = e4[scales.reshape(rows, cols // 16).long()].repeat_interleave(16, dim=1)
+    return e2[nib] * s * float(g)

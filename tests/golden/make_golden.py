@@ -1,7 +1,7 @@
 """Generates the golden fixtures of tests/golden/ from the reference.
 
-Run in a container that has the kennydd001/ervf tree (default
-/root/reference, override with ERVF_REFERENCE):
+Run where the kennydd001/ervf tree is present ($ERVF_REFERENCE, else a
+directory named ``reference`` beside this repository's root):
 
     python tests/golden/make_golden.py codec     # CPU: reference nvfp4.py
     python tests/golden/make_golden.py gemv      # GPU: reference CUDA kernels
@@ -24,7 +24,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = Path(os.environ.get("ERVF_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("ERVF_REFERENCE") or ROOT.parent / "reference")
 
 
 def codec():
@@ -41,12 +41,31 @@ def codec():
                         dq_codes=codes, dq_scales=scales, dq_g=g, dq_out=out)
 
 
-GEMV_CASES = [  # (rows, cols, seed, regime, relu2, width)
-    (64, 2688, 1, "random", 0, 16), (64, 2688, 2, "adversarial", 1, 16),
-    (48, 1856, 3, "zero_heavy", 0, 16), (40, 2048, 4, "dense", 1, 4),
-    (40, 768, 5, "random", 0, 8), (33, 2688, 6, "random", 1, 32),
-    (16, 4096, 7, "adversarial", 0, 256),
+GEMV_CASES = [  # (rows, cols, seed, regime, relu2, width, full-range scale bytes)
+    (64, 2688, 1, "random", 0, 16, 0), (64, 2688, 2, "adversarial", 1, 16, 0),
+    (48, 1856, 3, "zero_heavy", 0, 16, 0), (40, 2048, 4, "dense", 1, 4, 0),
+    (40, 768, 5, "random", 0, 8, 0), (33, 2688, 6, "random", 1, 32, 0),
+    (16, 4096, 7, "adversarial", 0, 256, 0),
+    (64, 2688, 8, "random", 0, 16, 1), (48, 1856, 9, "adversarial", 1, 16, 1),
+    (40, 3712, 10, "random", 0, 4, 1), (33, 768, 11, "zero_heavy", 1, 32, 1),
+    (24, 2688, 12, "dense", 0, 256, 1),
 ]
+
+# BASELINE config 0 (ervf_b200.formats.config0_inputs) through the reference
+# ERVF-16 kernel, plain and relu^2, and through the legacy 256-thread kernel
+CONFIG0_CASES = [("config0_w16", 16, 0), ("config0_w16_relu2", 16, 1), ("config0_legacy", 256, 0)]
+
+
+def case_inputs(i):
+    rows, cols, seed, regime, relu2, width, full = GEMV_CASES[i]
+    sys.path.insert(0, str(ROOT / "tests"))
+    from conftest import random_nvfp4, x_regime
+
+    if full:
+        codes, scales, g = random_nvfp4(rows, cols, seed, full_range=True)
+    else:
+        codes, scales, g = random_nvfp4(rows, cols, seed, nan_scales=True)
+    return codes, scales, g, x_regime(cols, regime, seed)
 
 
 def gemv():
@@ -56,22 +75,27 @@ def gemv():
     sys.path.insert(0, str(ROOT / "oracle"))
     sys.path.insert(0, str(ROOT))
     import ref
-    from conftest import random_nvfp4, x_regime
-    from ervf_b200.formats import e2m1_table, e4m3_device_table
+    from ervf_b200.formats import config0_inputs, e2m1_table, e4m3_device_table
 
     dev = torch.device("cuda")
     e2m1 = torch.from_numpy(e2m1_table()).to(dev)
     e4m3 = torch.from_numpy(e4m3_device_table()).to(dev)
-    outs = {}
-    for i, (rows, cols, seed, regime, relu2, width) in enumerate(GEMV_CASES):
-        codes, scales, g = random_nvfp4(rows, cols, seed, nan_scales=True)
-        x = x_regime(cols, regime, seed)
+
+    def run(codes, scales, x, g, rows, cols, relu2, width):
         c, s, xd = (torch.from_numpy(a).to(dev) for a in (codes, scales, x))
         out = torch.zeros(rows, device=dev)
         ref.call(ref.ervf_fn(width), c.data_ptr(), s.data_ptr(), e2m1.data_ptr(), e4m3.data_ptr(),
                  xd.data_ptr(), out.data_ptr(), float(g), rows, cols, relu2, 1.0, 0)
         torch.cuda.synchronize()
-        outs[f"case{i}"] = out.cpu().numpy()
+        return out.cpu().numpy()
+
+    outs = {}
+    for i, (rows, cols, seed, regime, relu2, width, full) in enumerate(GEMV_CASES):
+        codes, scales, g, x = case_inputs(i)
+        outs[f"case{i}"] = run(codes, scales, x, g, rows, cols, relu2, width)
+    codes, scales, g, x = config0_inputs()
+    for key, width, relu2 in CONFIG0_CASES:
+        outs[key] = run(codes, scales, x, g, 1856, 2688, relu2, width)
     dst = Path(os.environ.get("GOLDEN_OUT", HERE))
     np.savez_compressed(dst / "gemv_reference.npz", **outs)
 

@@ -3,7 +3,8 @@
 Builds the synthetic checkpoint of tests/ckpt_synth.py (seed 0) in a
 temporary directory, opens it with kennydd001/ervf's ShardIndex
 (src/moe_lab/lightningstream_nemotron/loader.py:54-185, imported from the
-reference tree, which must be at ERVF_REFERENCE or /root/reference) and
+reference tree: $ERVF_REFERENCE, else a directory named ``reference``
+beside this repository's root) and
 records what it returns: sha256 of read_raw for every tensor, get_scalar of
 every weight_scale_2, sha256 of dequantize_linear of every NVFP4 projection
 (float32 bytes), get_float32 of the BF16 / F32 tensors, quant_kind and
@@ -23,7 +24,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent))
-REF = Path(os.environ.get("ERVF_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("ERVF_REFERENCE") or HERE.parents[2] / "reference")
 sys.path.insert(0, str(REF / "src"))
 
 import numpy as np  # noqa: E402

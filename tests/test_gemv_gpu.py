@@ -25,6 +25,7 @@ SHAPES = [
     (33, 2704),     # cols % 32 == 16 -> width-32 fallback
     (64, 4096),
     (24, 8192),     # cols > 4096 -> width-32 fallback
+    (96, 3712),     # shared-expert down: 52 second-round chain groups
 ]
 
 
@@ -44,9 +45,10 @@ def run_product(fused, codes, scales, x, g, rows, cols, relu2=False, out_scale=1
     return out.cpu().numpy()
 
 
+@pytest.mark.parametrize("full_range", [False, True])
 @pytest.mark.parametrize("rows,cols", SHAPES)
-def test_gemv_matches_oracle_all_widths(fused, oracle, cuda, rows, cols):
-    codes, scales, g = random_nvfp4(rows, cols, seed=rows * 7 + cols)
+def test_gemv_matches_oracle_all_widths(fused, oracle, cuda, rows, cols, full_range):
+    codes, scales, g = random_nvfp4(rows, cols, seed=rows * 7 + cols, full_range=full_range)
     x = x_regime(cols, "random", seed=cols)
     want = oracle.nvfp4_gemv(codes, scales, x, g, rows, cols)
     for width in (0, 4, 8, 16, 32):

@@ -95,9 +95,9 @@ def test_grouped_up_and_routesum_match_unfused(fused, oracle, bank, cuda, width)
 
 
 def test_decoder_step_pdl_chain_matches_oracle(fused, oracle, bank, cuda):
-    """Three layers of the decode step -- batched routing, then either the
-    PDL-chained grouped launches or the one persistent launch, eager and in a
-    CUDA graph -- equal the oracle's route-order recurrence."""
+    """Three layers of the decode step -- batched routing, then the
+    PDL-chained per-layer launches with and without the L2 prefetch, eager
+    and in a CUDA graph -- equal the oracle's route-order recurrence."""
     from ervf_b200.moe import ExpertBank, MoEDecoder
 
     L, E, k = 3, 8, 6
@@ -110,8 +110,8 @@ def test_decoder_step_pdl_chain_matches_oracle(fused, oracle, bank, cuda):
     rl = r.standard_normal((L, E)).astype(np.float32)
     x = x_regime(HIDDEN, "bf16", seed=21)
     xd, rd = _t(x, cuda), _t(rl, cuda)
-    for use_graph, persistent in ((False, False), (True, False), (False, True), (True, True)):
-        dec.persistent = persistent
+    for use_graph, prefetch in ((False, True), (True, True), (False, False), (True, False)):
+        dec.prefetch = prefetch
         dec.xbuf.fill_(float("nan"))
         if use_graph:
             g = torch.cuda.CUDAGraph()
@@ -132,7 +132,7 @@ def test_decoder_step_pdl_chain_matches_oracle(fused, oracle, bank, cuda):
             experts = {e: (*bank["ups"][(e + l) % E], *bank["dns"][(e + 2 * l) % E]) for e in range(E)}
             want = (want + oracle.moe_block(want, experts, ids, w, HIDDEN, INTER)).astype(np.float32)
             assert np.array_equal(dec.ids[l].cpu().numpy(), ids)
-        assert bits_equal(y.cpu().numpy(), want), (use_graph, persistent)
+        assert bits_equal(y.cpu().numpy(), want), (use_graph, prefetch)
 
 
 def test_decoder_step_with_router_matches_oracle(fused, oracle, bank, cuda):
@@ -256,3 +256,36 @@ def test_batched_step_matches_f64(fused, oracle, bank, cuda):
     y2 = dec.step_batch(_t(x, cuda), _t(rl, cuda)).cpu().numpy()
     assert rel_l2(y2, want) <= 1e-3
     assert rel_l2(y2, y1) <= 1e-3
+
+
+def test_moe_layer_entry_matches_oracle(oracle, bank, cuda):
+    """ervf_moe_layer (up + down + route-order sum + residual, with and without
+    the L2 prefetch of the next layer's records, with and without PDL) equals
+    the oracle's routed block plus x, bit for bit."""
+    from ervf_b200 import _lib
+    from ervf_b200.fused_nvfp4 import ptr
+
+    k = 6
+    ids_h = np.array([2, 5, 7, 0, 3, 1], np.int32)
+    nxt_h = np.array([4, 6, 1, 0, 7, 2], np.int32)
+    w_h = np.random.default_rng(8).uniform(0.05, 0.4, k).astype(np.float32)
+    x = x_regime(HIDDEN, "bf16", seed=12)
+    ids, nxt, w, xd = _t(ids_h, cuda), _t(nxt_h, cuda), _t(w_h, cuda), _t(x, cuda)
+    act = torch.zeros(k * INTER, device=cuda)
+    nb = _lib.load().ervf_routesum_scratch_bytes(HIDDEN, k)
+    scratch = torch.zeros(nb, dtype=torch.uint8, device=cuda)
+    experts = {e: (*bank["ups"][e], *bank["dns"][e]) for e in range(8)}
+    want = (x + oracle.moe_block(x, experts, ids_h, w_h, HIDDEN, INTER)).astype(np.float32)
+    cb, sb = INTER * HIDDEN // 2, INTER * HIDDEN // 16
+    for flags in (0, _lib.LAUNCH_PDL, _lib.LAUNCH_PDL | _lib.LAUNCH_IDS_READY):
+        for pf in ((ptr(bank["up_c"]), ptr(bank["up_s"]), ptr(nxt)), (0, 0, 0)):
+            out = torch.full((HIDDEN,), float("nan"), device=cuda)
+            _lib.call("ervf_moe_layer", ptr(bank["up_c"]), ptr(bank["up_s"]), cb, sb, ptr(bank["dn_c"]),
+                      ptr(bank["dn_s"]), cb, sb, ptr(ids), ptr(bank["g_d"]), ptr(w), k, ptr(xd),
+                      ptr(act), ptr(out), HIDDEN, INTER, 8, ptr(scratch), nb, *pf, flags,
+                      torch.cuda.current_stream().cuda_stream)
+            torch.cuda.synchronize()
+            assert bits_equal(out.cpu().numpy(), want), (flags, pf[2] != 0)
+    # the scratch is left ready: every 32-row group counter (at its start) back at zero
+    cnt = scratch[:HIDDEN * 4].view(torch.int32)[:(HIDDEN + 31) // 32]
+    assert torch.count_nonzero(cnt).item() == 0

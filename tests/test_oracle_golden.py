@@ -15,18 +15,30 @@ from conftest import bits_equal, random_nvfp4, rel_l2, x_regime
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE / "golden"))
-from make_golden import GEMV_CASES  # noqa: E402
+from make_golden import CONFIG0_CASES, GEMV_CASES, case_inputs  # noqa: E402
 
 
 @pytest.mark.parametrize("i", range(len(GEMV_CASES)))
 def test_oracle_matches_reference_kernel_golden(oracle, i):
-    rows, cols, seed, regime, relu2, width = GEMV_CASES[i]
+    rows, cols, seed, regime, relu2, width, full = GEMV_CASES[i]
     g = np.load(HERE / "golden" / "gemv_reference.npz")[f"case{i}"]
-    codes, scales, gs = random_nvfp4(rows, cols, seed, nan_scales=True)
-    x = x_regime(cols, regime, seed)
+    codes, scales, gs, x = case_inputs(i)
     tree = oracle.TREE_LEGACY if width == 256 else oracle.TREE_ERVF
     got = oracle.nvfp4_gemv(codes, scales, x, gs, rows, cols, apply_relu2=bool(relu2), tree=tree)
     assert bits_equal(got, g)
+
+
+@pytest.mark.parametrize("key,width,relu2", CONFIG0_CASES)
+def test_oracle_matches_reference_kernel_on_config0(oracle, key, width, relu2):
+    """BASELINE config 0's exact inputs: the oracle equals the reference's
+    ERVF-16 (and legacy) kernel output stored from a B200 run."""
+    from ervf_b200.formats import config0_inputs
+
+    gold = np.load(HERE / "golden" / "gemv_reference.npz")
+    codes, scales, g, x = config0_inputs()
+    tree = oracle.TREE_LEGACY if width == 256 else oracle.TREE_ERVF
+    got = oracle.nvfp4_gemv(codes, scales, x, g, 1856, 2688, apply_relu2=bool(relu2), tree=tree)
+    assert bits_equal(got, gold[key])
 
 
 def test_oracle_close_to_float64_dequant(oracle):

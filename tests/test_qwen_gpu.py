@@ -133,3 +133,39 @@ def test_qwen_block_matches_f64(fused, qbank, cuda):
         a = gate / (1.0 + np.exp(-gate)) * up
         ref += float(w_h[s]) * (dequantize(dc, ds, dg, HIDDEN, INTER) @ a)
     assert rel_l2(out.cpu().numpy(), ref) < 1e-5
+
+
+def test_qwen_block_batch16_on_tensor_cores_matches_f64(fused, qbank, cuda):
+    """Config 2 at batch 16: softmax top-8 routing, then the expert-major
+    batched block on the tensor cores with the SwiGLU epilogue (gate / up row
+    pairs), route-order sum and residual -- within rel-L2 1e-3 of a float64
+    dequantise-then-matmul of the same bytes and routing (K-split 1 and 2)."""
+    from ervf_b200.formats import dequantize
+
+    T = 16
+    r = np.random.default_rng(77)
+    rl = r.standard_normal((T, E)).astype(np.float32)
+    x = np.stack([x_regime(HIDDEN, "bf16", seed=60 + t) for t in range(T)]).astype(np.float32)
+    ids = torch.zeros(T, K, dtype=torch.int32, device=cuda)
+    w = torch.zeros(T, K, device=cuda)
+    fused.route_topk_softmax(_t(rl, cuda), ids, w, T, E, K)
+    ids_h, w_h = ids.cpu().numpy(), w.cpu().numpy()
+    deq_up = {e: dequantize(*qbank["ups"][e][:2], qbank["ups"][e][2], 2 * INTER, HIDDEN) for e in range(E)}
+    deq_dn = {e: dequantize(*qbank["dns"][e][:2], qbank["dns"][e][2], HIDDEN, INTER) for e in range(E)}
+    ref = x.astype(np.float64).copy()
+    for t in range(T):
+        for s in range(K):
+            e = int(ids_h[t, s])
+            gu = deq_up[e] @ x[t].astype(np.float64)
+            gate, up = gu[0::2], gu[1::2]
+            ref[t] += float(w_h[t, s]) * (deq_dn[e] @ (gate / (1.0 + np.exp(-gate)) * up))
+    for ksplit in (1, 2):
+        out = torch.full((T, HIDDEN), float("nan"), device=cuda)
+        fused.moe_batched(qbank["up_c"], qbank["up_s"], 2 * INTER * HIDDEN // 2, 2 * INTER * HIDDEN // 16,
+                          qbank["dn_c"], qbank["dn_s"], HIDDEN * INTER // 2, HIDDEN * INTER // 16,
+                          qbank["g"], ids, w, T, K, E, _t(x, cuda), out, HIDDEN, INTER, ksplit=ksplit,
+                          swiglu=True)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        assert np.isfinite(got).all()
+        assert rel_l2(got, ref) <= 1e-3, (ksplit, rel_l2(got, ref))

@@ -66,6 +66,73 @@ def test_product_equals_reference_kernel(ref, fused):
     assert bits_equal(out.cpu().numpy(), want)
 
 
+def _product(fused, codes, scales, x, g, rows, cols, relu2, width=0, use_ervf=True):
+    dev = fused.device
+    fused.ervf_width, fused.use_ervf = width, use_ervf
+    out = torch.full((rows,), float("nan"), device=dev)
+    fused.gemv_into(out, _t(codes, dev), _t(scales, dev), _t(x, dev), g, rows, cols,
+                    apply_relu2=relu2)
+    torch.cuda.synchronize()
+    fused.ervf_width, fused.use_ervf = 0, True
+    return out.cpu().numpy()
+
+
+def test_config0_exact_inputs_against_reference_kernels(ref, fused, oracle):
+    from ervf_b200.formats import config0_inputs
+
+    rows, cols = 1856, 2688
+    codes, scales, g, x = config0_inputs()
+    for relu2 in (False, True):
+        want = ref_gemv(ref, fused, 16, codes, scales, x, g, rows, cols, relu2)
+        for width in (4, 8, 32):
+            assert bits_equal(ref_gemv(ref, fused, width, codes, scales, x, g, rows, cols, relu2),
+                              want), width
+        assert bits_equal(oracle.nvfp4_gemv(codes, scales, x, g, rows, cols, apply_relu2=relu2), want)
+        for width in (0, 4, 8, 16, 32):
+            assert bits_equal(_product(fused, codes, scales, x, g, rows, cols, relu2, width), want), width
+        legacy = ref_gemv(ref, fused, 256, codes, scales, x, g, rows, cols, relu2)
+        assert bits_equal(_product(fused, codes, scales, x, g, rows, cols, relu2, use_ervf=False),
+                          legacy)
+
+
+@pytest.mark.parametrize("rows,cols", [(1856, 2688), (2688, 1856), (2048, 768), (37, 2688),
+                                       (64, 4096)])
+def test_full_scale_byte_range_against_reference_kernels(ref, fused, oracle, rows, cols):
+    """Every scale byte class -- negative, subnormal, large, zero, NaN -- through
+    the reference kernels, the oracle and the product."""
+    codes, scales, g = random_nvfp4(rows, cols, seed=rows + 5 * cols, full_range=True)
+    for regime in ("random", "adversarial"):
+        x = x_regime(cols, regime, seed=rows)
+        for relu2 in (False, True):
+            want = oracle.nvfp4_gemv(codes, scales, x, g, rows, cols, apply_relu2=relu2)
+            for width in (4, 8, 16, 32):
+                assert bits_equal(ref_gemv(ref, fused, width, codes, scales, x, g, rows, cols, relu2),
+                                  want), (regime, relu2, width)
+            legacy = oracle.nvfp4_gemv(codes, scales, x, g, rows, cols, apply_relu2=relu2,
+                                       tree=oracle.TREE_LEGACY)
+            assert bits_equal(ref_gemv(ref, fused, 256, codes, scales, x, g, rows, cols, relu2), legacy)
+            for width in (0, 16):
+                assert bits_equal(_product(fused, codes, scales, x, g, rows, cols, relu2, width),
+                                  want), (regime, relu2, width)
+
+
+@pytest.mark.parametrize("rows,cols", [(3712, 2688), (2688, 3712), (131072, 2688)])
+def test_shared_expert_and_lm_head_shapes_against_reference(ref, fused, oracle, rows, cols):
+    """The runtime's other NVFP4 GEMVs (runtime.py:510-515 shared expert up /
+    down, :827-829 lm_head) through the same kernel: product == reference
+    ERVF-16 kernel bit for bit (cols 3712 runs the B200 schedule with 52
+    second-round chain groups); the oracle on the first rows."""
+    codes, scales, g = random_nvfp4(rows, cols, seed=rows + cols, full_range=True)
+    x = x_regime(cols, "bf16", seed=3)
+    for relu2 in ((False, True) if rows < 100000 else (False,)):
+        want = ref_gemv(ref, fused, 16, codes, scales, x, g, rows, cols, relu2)
+        assert bits_equal(_product(fused, codes, scales, x, g, rows, cols, relu2), want)
+        n = min(rows, 4096)
+        o = oracle.nvfp4_gemv(codes[:n * cols // 2], scales[:n * cols // 16], x, g, n, cols,
+                              apply_relu2=relu2)
+        assert bits_equal(o, want[:n])
+
+
 def test_bf16_oracle_equals_reference(ref, oracle, cuda):
     rows, cols = 512, 2688
     r = np.random.default_rng(4)

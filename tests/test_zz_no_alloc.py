@@ -56,12 +56,17 @@ def _routing(seed, k):
 
 
 def test_static_scratch_matches_caller_scratch_twice(cuda, oracle, down_bank):
+    """Calls in a row on the fixed array.  With ERVF_LAUNCH_PDL, or one route
+    slot, the route sum runs through the array's group counters; the
+    unflagged 8-slot call takes the cluster route sum (no scratch)."""
     from ervf_b200 import _lib
 
     nbytes = _lib.load().ervf_routesum_scratch_bytes(HIDDEN, 8)
     scratch = torch.zeros(nbytes, dtype=torch.uint8, device=cuda)
-    cases = [(11, 6, "resid"), (12, 8, "base")]
-    for seed, k, kind in cases:  # two calls in a row, different routings
+    pdl = _lib.LAUNCH_PDL
+    cases = [(11, 6, "resid", pdl), (12, 8, "base", pdl), (13, 1, "resid", 0), (14, 8, "base", 0),
+             (15, 3, "resid", pdl)]
+    for seed, k, kind, flags in cases:  # calls in a row, different routings
         ids_h, w_h, act_h = _routing(seed, k)
         v = x_regime(HIDDEN, "random", seed=seed)
         ids, w, act, vv = _t(ids_h, cuda), _t(w_h, cuda), _t(act_h, cuda), _t(v, cuda)
@@ -69,9 +74,9 @@ def test_static_scratch_matches_caller_scratch_twice(cuda, oracle, down_bank):
         want = torch.full((HIDDEN,), float("nan"), device=cuda)
         got = torch.full((HIDDEN,), float("nan"), device=cuda)
         _lib.call("ervf_moe_down_routesum", *_args(down_bank, ids, w, k, act, base, resid, want),
-                  _p(scratch), ctypes.c_size_t(nbytes), 0, 0, _stream())
+                  _p(scratch), ctypes.c_size_t(nbytes), 0, flags, _stream())
         _lib.call("ervf_moe_down_routesum_static",
-                  *_args(down_bank, ids, w, k, act, base, resid, got), 0, 0, _stream())
+                  *_args(down_bank, ids, w, k, act, base, resid, got), 0, flags, _stream())
         torch.cuda.synchronize()
         assert bits_equal(got.cpu().numpy(), want.cpu().numpy())
         # and against the oracle: route-order fmaf over the down GEMVs
@@ -88,7 +93,7 @@ def test_static_scratch_matches_caller_scratch_twice(cuda, oracle, down_bank):
 def test_static_scratch_rejects_oversize(cuda, down_bank):
     from ervf_b200 import _lib
 
-    ids_h, w_h, act_h = _routing(13, 8)
+    ids_h, w_h, act_h = _routing(23, 8)
     ids, w, act = _t(ids_h, cuda), _t(w_h, cuda), _t(act_h, cuda)
     out = torch.zeros(HIDDEN, device=cuda)
     big_ids = _t(np.arange(9, dtype=np.int32) % N_EXPERTS, cuda)
