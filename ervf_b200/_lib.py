@@ -57,6 +57,9 @@ SIGNATURES: dict[str, list] = {
     "ervf_routesum_scratch_bytes": [_i, _i],
     "ervf_moe_layer": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i,
                        _i, _i, _vp, _sz, _vp, _vp, _vp, _i, _vp],
+    "ervf_moe_token": [_vp, _i, _sz, _sz, _sz, _sz, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _vp, _sz, _i,
+                       _vp],
+    "ervf_moe_token_scratch_bytes": [_i, _i, _i, _i],
     "ervf_moe_down_routesum_static": [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp,
                                       _i, _i, _i, _i, _vp],
     "ervf_moe_batched": [_vp, _vp, _sz, _sz, _vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _i, _i, _vp, _vp,
@@ -91,7 +94,8 @@ SIGNATURES: dict[str, list] = {
     "ervf_panel_major": [_vp, _vp, _vp, _i, _i, _vp],
     "ervf_bf16_gemv": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "ervf_nvfp4_gemm_rows_b": [_vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp],
-    "ervf_down_union": [_vp, _vp, _i, _vp, _vp, _f, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
+    "ervf_down_union": [_vp, _vp, _i, _vp, _vp, _f, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                        _vp],
     "ervf_reduce_slots": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "ervf_route_topk": [_vp, _vp, _vp, _vp, _i, _i, _f, _i, _vp],
     "ervf_f32_gemv": [_vp, _vp, _vp, _i, _i, _vp],
@@ -101,6 +105,7 @@ SIGNATURES: dict[str, list] = {
 }
 
 SIZE_RESULT = {"ervf_routesum_scratch_bytes", "ervf_nvfp4_gemm_tc_scratch_bytes",
+               "ervf_moe_token_scratch_bytes",
                "ervf_moe_batched_scratch_bytes", "ervf_ep_region_bytes"}
 
 _lib = None

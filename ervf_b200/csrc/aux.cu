@@ -556,6 +556,38 @@ int launch_down_masked(const uint8_t* bank, const float* act, unsigned* masks, i
   return launched();
 }
 
+// sum[c] = sum over b < n of acts[b][c], nodes in order: the union panel
+// mask of the batched masked down (down_union, sweepspec.py:337-343) is the
+// nonzero pattern of this sum.
+__global__ void node_sum_kernel(const float* __restrict__ acts, int n, int inter, float* __restrict__ sum) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= inter) return;
+  float a = 0.0f;
+  for (int b = 0; b < n; ++b) a += acts[(size_t)b * inter + c];
+  sum[c] = a;
+}
+
+int launch_down_union(const uint8_t* bank, const float* acts, int n, float* act_sum, unsigned* masks,
+                      int* plist, int* pcount, int* nz, int* nzc, float global_scale, float* out, int rows,
+                      int inter, int nchunks, cudaStream_t stream) {
+  const int npanel = inter >> 4;
+  node_sum_kernel<<<(inter + 255) / 256, 256, 0, stream>>>(acts, n, inter, act_sum);
+  if (launched() != kOk) return kErrLaunch;
+  panel_scan_kernel<<<1, 256, npanel * sizeof(unsigned), stream>>>(act_sum, inter, masks, plist, pcount,
+                                                                   nz, nzc);
+  if (launched() != kOk) return kErrLaunch;
+  // every node walks the union panel list and masks: a column where the
+  // node is zero adds fmaf(w, 0, acc) = acc, and the panel -> chunk
+  // assignment (by position in the list) is the reference's
+  for (int b = 0; b < n; ++b) {
+    down_masked_kernel<<<(rows + 31) / 32, 32 * nchunks, 0, stream>>>(
+        bank, acts + (size_t)b * inter, masks, plist, pcount, global_scale, nullptr, nullptr, 0,
+        out + (size_t)b * rows, rows, inter, nchunks);
+    if (launched() != kOk) return kErrLaunch;
+  }
+  return kOk;
+}
+
 int launch_panel_major(const uint8_t* codes, const uint8_t* scales, uint8_t* block, int rows,
                        int inter, cudaStream_t stream) {
   const size_t total = (size_t)(inter >> 4) * ((size_t)rows + 16u * (size_t)(rows >> 1));

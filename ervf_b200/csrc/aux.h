@@ -31,6 +31,9 @@ int launch_down_masked(const uint8_t* bank, const float* act, unsigned* masks, i
                        int nchunks, cudaStream_t stream);
 int launch_ep_route_sum(const float* gathered, const int* ids, const float* w, int top_k,
                         const float* x, float* out, int hidden, int nranks, cudaStream_t stream);
+int launch_down_union(const uint8_t* bank, const float* acts, int n, float* act_sum, unsigned* masks,
+                      int* plist, int* pcount, int* nz, int* nzc, float global_scale, float* out, int rows,
+                      int inter, int nchunks, cudaStream_t stream);
 int launch_gather_rows(const float* src, const int* idx, int n, int cols, float* dst, cudaStream_t stream);
 int launch_scatter_rows(const float* src, const int* idx, int n, int cols, float* dst, cudaStream_t stream);
 int launch_reduce_slots(const float* contrib, const float* w, float* out, int rows, int top_k, int B,

@@ -45,9 +45,9 @@ int ervf_version(void) { return 100; }
 
 int ervf_device_status(void) {
   // read and clear every unit's word; report the first error found
-  const int v[5] = {read_gemv_device_error(true), read_aux_device_error(true),
+  const int v[6] = {read_gemv_device_error(true), read_aux_device_error(true),
                     read_tc_device_error(true), read_ep_device_error(true),
-                    read_mma_device_error(true)};
+                    read_mma_device_error(true), read_token_device_error(true)};
   for (int e : v)
     if (e) return e;
   return kOk;
@@ -325,6 +325,48 @@ int ervf_moe_layer(const uint8_t* up_codes, const uint8_t* up_scales, size_t up_
   return launch_nvfp4_batch(d, 0, S(stream));
 }
 
+int ervf_moe_token(const uint64_t* layer_ptrs, int n_layers, size_t up_code_stride,
+                   size_t up_scale_stride, size_t dn_code_stride, size_t dn_scale_stride,
+                   const int32_t* ids, const float* route_w, int top_k, int n_experts, const float* x,
+                   float* out, int hidden, int inter, void* scratch, size_t scratch_bytes, int flags,
+                   void* stream) {
+  if (!layer_ptrs || !ids || !route_w || !x || !out || !scratch) return kErrNull;
+  if (flags & ~ERVF_LAUNCH_PDL) return kErrArg;
+  if (n_layers <= 0 || top_k <= 0 || top_k > kMaxJobs || n_experts <= 0) return kErrShape;
+  if (hidden <= 0 || inter <= 0 || hidden % 32 || inter % 32 || hidden > 4096 || inter > 4096)
+    return kErrShape;
+  if (scratch_bytes < moe_token_scratch_bytes(n_layers, hidden, inter, top_k)) return kErrArg;
+  if (!al(scratch, 256) || !al(x, 16) || !al(out, 4) || !al(layer_ptrs, 8) ||
+      ((up_code_stride | up_scale_stride | dn_code_stride | dn_scale_stride) & 15u))
+    return kErrAlign;
+  const size_t cb = (size_t)inter * hidden / 2, sb = (size_t)inter * hidden / 16;
+  if (up_code_stride < cb || up_scale_stride < sb || dn_code_stride < cb || dn_scale_stride < sb)
+    return kErrArg;
+  MoeTokenArgs a{};
+  a.layer_ptrs = reinterpret_cast<const unsigned long long*>(layer_ptrs);
+  a.up_code_stride = up_code_stride;
+  a.up_scale_stride = up_scale_stride;
+  a.dn_code_stride = dn_code_stride;
+  a.dn_scale_stride = dn_scale_stride;
+  a.ids = ids;
+  a.route_w = route_w;
+  a.x = x;
+  a.out = out;
+  a.n_layers = n_layers;
+  a.top_k = top_k;
+  a.n_experts = n_experts;
+  a.hidden = hidden;
+  a.inter = inter;
+  a.scratch = scratch;
+  a.pdl = (flags & ERVF_LAUNCH_PDL) != 0;
+  return launch_moe_token(a, S(stream));
+}
+
+size_t ervf_moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top_k) {
+  if (n_layers <= 0 || hidden <= 0 || inter <= 0 || top_k <= 0) return 0;
+  return moe_token_scratch_bytes(n_layers, hidden, inter, top_k);
+}
+
 size_t ervf_routesum_scratch_bytes(int hidden, int top_k) {
   if (hidden <= 0 || top_k <= 0) return 0;
   return routesum_scratch_bytes(hidden, top_k);
@@ -470,20 +512,17 @@ int ervf_nvfp4_gemm_rows_b(const uint8_t* codes, const uint8_t* scales, const fl
 }
 
 int ervf_down_union(const uint8_t* bank, const float* acts, int n, const int32_t* dst, float* contrib,
-                    float global_scale, int hidden, int inter, int nchunks, uint32_t* masks,
-                    int32_t* plist, int32_t* pcount, int32_t* nz, int32_t* nzc, float* tmp,
-                    void* stream) {
-  if (!bank || !acts || !dst || !contrib || !masks || !plist || !pcount || !nz || !nzc || !tmp)
+                    float global_scale, int hidden, int inter, int nchunks, float* act_sum,
+                    uint32_t* masks, int32_t* plist, int32_t* pcount, int32_t* nz, int32_t* nzc,
+                    float* tmp, void* stream) {
+  if (!bank || !acts || !dst || !contrib || !act_sum || !masks || !plist || !pcount || !nz || !nzc || !tmp)
     return kErrNull;
   if (n < 1 || n > 64 || hidden <= 0 || (hidden & 1) || inter <= 0 || (inter & 15) || inter > 65536)
     return kErrShape;
   if (nchunks <= 0 || nchunks > 32) return kErrArg;
-  for (int b = 0; b < n; ++b) {
-    if (int e = launch_down_masked(bank, acts + (size_t)b * inter, masks, plist, pcount, nz, nzc,
-                                   global_scale, nullptr, nullptr, 0, tmp + (size_t)b * hidden, hidden,
-                                   inter, nchunks, S(stream)))
-      return e;
-  }
+  if (int e = launch_down_union(bank, acts, n, act_sum, masks, plist, pcount, nz, nzc, global_scale, tmp,
+                                hidden, inter, nchunks, S(stream)))
+    return e;
   return launch_scatter_rows(tmp, dst, n, hidden, contrib, S(stream));
 }
 

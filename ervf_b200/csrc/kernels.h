@@ -207,6 +207,25 @@ int read_aux_device_error(bool clear);
 int read_tc_device_error(bool clear);
 int read_ep_device_error(bool clear);
 int read_mma_device_error(bool clear);
+int read_token_device_error(bool clear);
+
+// One decode token through every routed MoE layer in one launch
+// (moe_token.cu).  layer_ptrs: device array [5][n_layers] of up code, up
+// scale, down code, down scale and globals (f32 [E][2]) bases per layer.
+struct MoeTokenArgs {
+  const unsigned long long* layer_ptrs;
+  size_t up_code_stride, up_scale_stride, dn_code_stride, dn_scale_stride;
+  const int* ids;        // [n_layers][top_k]
+  const float* route_w;  // [n_layers][top_k]
+  const float* x;        // [hidden]
+  float* out;            // [hidden]
+  int n_layers, top_k, n_experts, hidden, inter;
+  void* scratch;         // moe_token_scratch_bytes, counters zero
+  bool pdl;
+};
+
+size_t moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top_k);
+int launch_moe_token(const MoeTokenArgs& a, cudaStream_t stream);
 
 // Expert-parallel exchange over NVLink peer memory (ep_p2p.cu).  Region
 // layout of every rank: u64 flag[kEpMaxRanks] at 0, u64 seq at 512, f32

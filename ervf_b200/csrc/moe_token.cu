@@ -1,0 +1,700 @@
+// moe_token.cu -- one decode token through every routed MoE layer in ONE
+// launch (single GPU), bit-exact to the per-layer path (ervf_moe_layer: the
+// reference's per-layer up GEMV + relu^2, masked down GEMV and route-order
+// sum, kennydd001/ervf runtime.py:705-746 over fused_nvfp4.py:295-406).
+//
+// Work is a single ordered list of items, claimed one at a time from a global
+// counter by each CTA's producer warp:
+//   item 0                      PREP: x -> the layer-0 activation buffers
+//   per layer l, in order:      UP   items: slot-major, krt_u rows of up_e(x_l)
+//                               DOWN items: slot-major, krt_d rows of down_e(act)
+// An UP item needs x_l complete (every row group of layer l-1's route sum
+// written); a DOWN item needs its slot's act complete (all UP items of that
+// slot).  Dependencies point only at items with a SMALLER index, and every
+// CTA runs its claimed items in claim order, so the unfinished item with the
+// smallest index always has its inputs ready and its CTA running it: the
+// token completes whatever the number of co-resident CTAs (no grid-wide
+// residency assumption).  Every wait is bounded and ends with kErrTimeout.
+//
+// CTA = 8 consumer warps (the exact ERVF chain schedule of tma_core.cuh) +
+// one producer warp + one publisher warp, two CTAs per SM.
+//   producer  claims an item when a stage frees, writes the item header and
+//             the item's block-scale table RN(e4m3 * g) into the stage, bulk
+//             copies the weight rows (cp.async.bulk, no multicast) at once,
+//             then waits for the item's activation and bulk copies it (kept
+//             in global memory in the swizzled unit layout the consumers
+//             read, so no permutation pass) -- weights stream while the
+//             activation is still being produced elsewhere.
+//   consumers reduce the item's rows (chains -> shared chain buffer -> tree)
+//             and hand the row values to the publisher through shared memory.
+//   publisher stores them -- UP rows as relu^2 into the slot's swizzled act
+//             buffer, DOWN rows into contrib[slot][row] -- each lane fencing
+//             its own stores (a bulk copy on another SM reads them next), then
+//             makes the item visible: UP adds its rows to the slot's act
+//             counter (release); DOWN adds its rows to the 32-row groups it
+//             touches (acq_rel); the add that completes a group makes the
+//             warp sum the group in ROUTE order, acc = fmaf(y_s, w_s, acc)
+//             from 0, x_{l+1} = x_l + acc (the per-layer path's arithmetic),
+//             writes x_{l+1} (linear and swizzled, or `out` after the last
+//             layer) and adds the group's rows to the x counter of layer l+1.
+// The last CTA to leave zeroes every counter, so the scratch is ready for
+// the next token (also after a timeout, once all CTAs have left).
+#include <stdlib.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tma_core.cuh"
+
+namespace ervf {
+
+namespace {
+
+constexpr int kTokWarps = kCW + 2;  // consumers, producer, publisher
+constexpr int kTokThreads = kTokWarps * 32;
+constexpr int kProd = kCT;       // first thread of the producer warp
+constexpr int kPub = kCT + 32;   // first thread of the publisher warp
+constexpr int kTokMaxStages = 4;  // ring depth is chosen per launch (2..4)
+constexpr int kPubRing = 16;     // item descriptors between consumers and publisher
+constexpr int kLutOff = 64;      // stage: header [0, 64), block-scale table [64, 1088)
+constexpr int kXOff = kLutOff + 1024;
+constexpr int kYRingOff = 512;    // [kPubRing][32] row values handed to the publisher
+constexpr int kTabOff = kYRingOff + kPubRing * 32 * 4;  // per-token routing table, then the chain buffer
+constexpr unsigned kFull = 0xffffffffu;
+
+enum : int { kItemPrep = 0, kItemUp = 1, kItemDown = 2, kItemEnd = 3 };
+
+// One projection: up (rows = inter, cols = hidden) or down (rows = hidden,
+// cols = inter).
+struct TokPhase {
+  int rows, cols, n_u, n2, teams, krt, cb, sb, scale_off, n_items;
+};
+
+struct TokArgs {
+  const unsigned long long* layer_ptrs;  // [5][L]: up codes, up scales, dn codes, dn scales, globals
+  size_t up_cs, up_ss, dn_cs, dn_ss;     // per-expert record strides
+  const int* ids;                        // [L][K]
+  const float* route_w;                  // [L][K]
+  const float* x_in;                     // [hidden]
+  float* out;                            // [hidden]
+  int L, K, E, hidden, inter, G;         // G = 32-row groups of hidden
+  TokPhase up, dn;
+  int per_layer, total;
+  int stages, stage_bytes, codes_off, stage_base, part_off;
+  int prefetch;  // queue the next claimed item's weight rows into L2
+  unsigned* ctr;                         // claim, exited, xrows[L], actrows[L][K], grp[L][G]
+  int n_ctr;
+  float* xlin;     // [L][hidden]  x_l (x_0 = the input)
+  float* xsw;      // [L][hidden]  x_l in the swizzled unit layout
+  float* actsw;    // [2][K][inter] relu^2(up) per slot, swizzled
+  float* contrib;  // [2][K][hidden] down rows per slot
+};
+
+// Counter words.  The claim counter (hit by every claim), the exit counter
+// and every counter that producers poll sit on their own 128-byte line, so
+// that polling does not slow the atomics on a neighbour.
+constexpr int kCtrLine = 32;
+__device__ __forceinline__ unsigned* ctr_claim(const TokArgs& a) { return a.ctr; }
+__device__ __forceinline__ unsigned* ctr_exited(const TokArgs& a) { return a.ctr + kCtrLine; }
+__device__ __forceinline__ unsigned* ctr_xrows(const TokArgs& a, int l) {
+  return a.ctr + kCtrLine * (2 + l);
+}
+__device__ __forceinline__ unsigned* ctr_act(const TokArgs& a, int l, int s) {
+  return a.ctr + kCtrLine * (2 + a.L + l * a.K + s);
+}
+__device__ __forceinline__ unsigned* ctr_grp(const TokArgs& a, int l, int g) {
+  return a.ctr + kCtrLine * (2 + a.L + a.L * a.K) + l * a.G + g;
+}
+
+__host__ __device__ __forceinline__ size_t token_ctr_words(int L, int K, int G) {
+  return (size_t)kCtrLine * (2 + L + (size_t)L * K) + (size_t)L * G;
+}
+
+// Shared routing table of the token, loaded once per CTA: record bases of
+// every layer (up codes, up scales, down codes, down scales), the clamped
+// expert id of every (layer, slot) and its (down, up) global scales -- the
+// producer then forms an item's addresses without a global-memory round trip.
+__host__ __device__ __forceinline__ int token_tab_bytes(int L, int K) { return 32 * L + 12 * L * K; }
+
+// Float index of column j in the swizzled unit layout that x_slot / the
+// consumers use: unit t = j / 32 holds 8 float4 slots, slot k =
+// (x[c], x[c+8], x[c+1], x[c+9]) with c = 32t + 16(k>>2) + 2(k&3), stored at
+// float4 t*8 + (k ^ (t & 7)).
+__device__ __forceinline__ int sw_index(int j) {
+  const int t = j >> 5, o = j & 31;
+  const int k = 4 * (o >> 4) + ((o >> 1) & 3);
+  return ((t << 3) + (k ^ (t & 7))) * 4 + 2 * (o & 1) + ((o >> 3) & 1);
+}
+
+__device__ __forceinline__ void decode_item(const TokArgs& a, int idx, int& kind, int& l, int& slot,
+                                            int& r0, int& nrows) {
+  if (idx == 0) {
+    kind = kItemPrep;
+    l = slot = r0 = nrows = 0;
+    return;
+  }
+  const int i = idx - 1;
+  l = i / a.per_layer;
+  int j = i - l * a.per_layer;
+  const int nu = a.K * a.up.n_items;
+  const TokPhase* ph;
+  if (j < nu) {
+    kind = kItemUp;
+    ph = &a.up;
+  } else {
+    kind = kItemDown;
+    j -= nu;
+    ph = &a.dn;
+  }
+  slot = j / ph->n_items;
+  r0 = (j - slot * ph->n_items) * ph->krt;
+  nrows = min(ph->krt, ph->rows - r0);
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_gpu(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Orders this thread's generic-proxy view of global memory with its
+// async-proxy (bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// L2 prefetch of `bytes` (a multiple of 16, may be 0) at a 16-byte aligned
+// global address; a hint, no data moves into this SM.
+__device__ __forceinline__ void l2_prefetch(const void* p, uint32_t bytes) {
+  if (bytes) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Bounded wait until *p >= target (acquire); false after ~2 s.
+__device__ __forceinline__ bool wait_count(const unsigned* p, unsigned target) {
+  if (ld_acquire_gpu(p) >= target) return true;
+  const long long t0 = clock64();
+  while (ld_acquire_gpu(p) < target) {
+    if (clock64() - t0 > 4000000000LL) {
+      atomicExch(&g_device_error, kErrTimeout);
+      return false;
+    }
+    nanosleep_ns(128);
+  }
+  return true;
+}
+
+// Bounded wait until the shared counter *p > v (acquire at CTA scope).
+__device__ __forceinline__ bool wait_smem_gt(const int* p, int v) {
+  if (ld_acquire_cta(p) > v) return true;
+  const long long t0 = clock64();
+  while (ld_acquire_cta(p) <= v) {
+    if (clock64() - t0 > 4000000000LL) {
+      atomicExch(&g_device_error, kErrTimeout);
+      return false;
+    }
+    nanosleep_ns(32);
+  }
+  return true;
+}
+
+// Per-thread place in the consumer schedule of one projection (see the TMA
+// schedule in nvfp4_gemv.cu: teams of n_u threads, two segments per thread).
+struct SegPlace {
+  int team, par1, par2, u1, u2, grp;
+  bool active, cont;
+};
+
+__device__ __forceinline__ SegPlace seg_place(const TokPhase& ph, int tid) {
+  SegPlace s;
+  const int nu = ph.n_u, n2 = ph.n2;
+  s.team = tid / nu;
+  const int m = tid - s.team * nu;
+  s.active = s.team < ph.teams;
+  s.cont = m < 2 * n2;
+  s.grp = m < n2 ? m : m - n2;
+  s.u1 = s.grp;
+  s.u2 = s.cont ? s.grp + 64 : s.grp;
+  s.par1 = (m >= n2 && m < 2 * n2) ? 1 : 0;
+  s.par2 = s.cont ? s.par1 : 1;
+  return s;
+}
+
+template <int H>
+__global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_constant__ TokArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int s_last;
+  const int tid = threadIdx.x;
+  const int S = a.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [kTokMaxStages]
+  uint64_t* empty = full + kTokMaxStages;              // [kTokMaxStages]
+  int* done = reinterpret_cast<int*>(smem + 64);        // items stored by the consumers
+  int* pub_done = done + 1;                            // items published
+  int* pubq = reinterpret_cast<int*>(smem + 128);      // [kPubRing][4] kind, layer, slot, r0 | nrows << 16
+  float* yring = reinterpret_cast<float*>(smem + kYRingOff);
+  float* part = reinterpret_cast<float*>(smem + a.part_off);
+  // routing table: 8-byte entries first, so that every entry is aligned
+  unsigned long long* tab_base = reinterpret_cast<unsigned long long*>(smem + kTabOff);  // [4][L]
+  float2* tab_g = reinterpret_cast<float2*>(smem + kTabOff + 32 * a.L);                 // [L][K]
+  int* tab_id = reinterpret_cast<int*>(smem + kTabOff + 32 * a.L + 8 * a.L * a.K);       // [L][K]
+  uint8_t* stages = smem + a.stage_base;
+
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    *done = 0;
+    *pub_done = 0;
+    fence_mbar_init();
+  }
+  grid_dep_wait();  // ids, route weights and x come from the predecessor
+  for (int i = tid; i < 4 * a.L; i += kTokThreads) tab_base[i] = a.layer_ptrs[i];
+  for (int i = tid; i < a.L * a.K; i += kTokThreads) {
+    int e = a.ids[i];
+    e = e < 0 ? 0 : (e >= a.E ? a.E - 1 : e);  // a stale id cannot leave the bank
+    const float* gl = reinterpret_cast<const float*>(a.layer_ptrs[4 * a.L + i / a.K]);
+    tab_id[i] = e;
+    tab_g[i] = make_float2(gl[2 * e], gl[2 * e + 1]);
+  }
+  __syncthreads();
+
+  if (tid >= kProd && tid < kPub) {
+    // ------------------------------------------------------------ producer
+    const int lane = tid - kProd;
+    int it = 0;
+    bool ok = true;
+    // the next item is claimed while the current one streams, so the claim's
+    // round trip is off the path from a free stage to its copies
+    int next = 0;
+    if (lane == 0) next = (int)atomicAdd(ctr_claim(a), 1u);
+    for (;;) {
+      const int st = it % S;
+      uint8_t* sp = stages + (size_t)st * a.stage_bytes;
+      if (lane == 0) ok = mbar_wait(&empty[st], ((it / S) & 1) ^ 1);
+      ok = __shfl_sync(kFull, ok, 0);
+      if (!ok) break;
+      const int idx = __shfl_sync(kFull, next, 0);
+      if (idx >= a.total) break;
+      int kind, l, slot, r0, nrows;
+      decode_item(a, idx, kind, l, slot, r0, nrows);
+      int* hdr = reinterpret_cast<int*>(sp);
+      if (kind == kItemPrep) {
+        if (lane == 0) {
+          hdr[0] = kind;
+          mbar_arrive(&full[st]);
+          next = (int)atomicAdd(ctr_claim(a), 1u);
+        }
+        ++it;
+        continue;
+      }
+      const bool up = kind == kItemUp;
+      const TokPhase& ph = up ? a.up : a.dn;
+      const int e = tab_id[l * a.K + slot];
+      const uint8_t* cbase = reinterpret_cast<const uint8_t*>(tab_base[(up ? 0 : 2) * a.L + l]) +
+                             (size_t)e * (up ? a.up_cs : a.dn_cs);
+      const uint8_t* sbase = reinterpret_cast<const uint8_t*>(tab_base[(up ? 1 : 3) * a.L + l]) +
+                             (size_t)e * (up ? a.up_ss : a.dn_ss);
+      const float2 g2 = tab_g[l * a.K + slot];
+      const float g = up ? g2.y : g2.x;
+      float4* lut4 = reinterpret_cast<float4*>(sp + kLutOff);
+      for (int q4 = lane; q4 < 64; q4 += 32) {
+        const uint32_t v = 4u * (uint32_t)q4;
+        lut4[q4] = make_float4(e4m3_lut_value(v) * g, e4m3_lut_value(v + 1) * g,
+                               e4m3_lut_value(v + 2) * g, e4m3_lut_value(v + 3) * g);
+      }
+      if (lane == 0) {
+        reinterpret_cast<int4*>(hdr)[0] = make_int4(kind, l, slot, r0);
+        hdr[4] = nrows;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        uint8_t* codes = sp + a.codes_off;
+        const uint32_t code_bytes = (uint32_t)(nrows * ph.cb);
+        const uint32_t scale_bytes = (uint32_t)(nrows * ph.sb);
+        const uint32_t s16 = scale_bytes & ~15u;
+        const uint8_t* csrc = cbase + (size_t)r0 * ph.cb;
+        const uint8_t* ssrc = sbase + (size_t)r0 * ph.sb;
+        for (uint32_t i = s16; i < scale_bytes; ++i) codes[ph.scale_off + i] = ssrc[i];
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        const uint32_t x_bytes = (uint32_t)ph.cols * 4u;
+        mbar_arrive_expect_tx(&full[st], code_bytes + s16 + x_bytes);
+        for (uint32_t off = 0; off < code_bytes; off += 4096u) {
+          const uint32_t n = code_bytes - off < 4096u ? code_bytes - off : 4096u;
+          bulk_g2s(codes + off, csrc + off, n, &full[st]);
+        }
+        if (s16) bulk_g2s(codes + ph.scale_off, ssrc, s16, &full[st]);
+        next = (int)atomicAdd(ctr_claim(a), 1u);
+        if (a.prefetch && next < a.total) {
+          // its weight rows stream from HBM into L2 while this item waits
+          int k2, l2, s2, q0, n2;
+          decode_item(a, next, k2, l2, s2, q0, n2);
+          if (k2 != kItemPrep) {
+            const bool up2 = k2 == kItemUp;
+            const TokPhase& p2 = up2 ? a.up : a.dn;
+            const int e2 = tab_id[l2 * a.K + s2];
+            const uint8_t* c2 = reinterpret_cast<const uint8_t*>(tab_base[(up2 ? 0 : 2) * a.L + l2]) +
+                                (size_t)e2 * (up2 ? a.up_cs : a.dn_cs) + (size_t)q0 * p2.cb;
+            const uint8_t* sc2 = reinterpret_cast<const uint8_t*>(tab_base[(up2 ? 1 : 3) * a.L + l2]) +
+                                 (size_t)e2 * (up2 ? a.up_ss : a.dn_ss) + (size_t)q0 * p2.sb;
+            l2_prefetch(c2, (uint32_t)(n2 * p2.cb));
+            l2_prefetch(sc2, (uint32_t)(n2 * p2.sb) & ~15u);
+          }
+        }
+        // the item's activation: x_l (UP) or the slot's act (DOWN)
+        ok = up ? wait_count(ctr_xrows(a, l), (unsigned)a.hidden)
+                : wait_count(ctr_act(a, l, slot), (unsigned)a.inter);
+        fence_proxy_async_global();
+        // copied even after a timeout (in bounds), so that the stage completes
+        const float* xsrc = up ? a.xsw + (size_t)l * a.hidden
+                               : a.actsw + ((size_t)(l & 1) * a.K + slot) * a.inter;
+        bulk_g2s(sp + kXOff, xsrc, x_bytes, &full[st]);
+      }
+      ok = __shfl_sync(kFull, ok, 0);
+      ++it;
+      if (!ok) break;
+    }
+    // end marker for the consumers, then leave no bulk copy in flight
+    if (lane == 0) {
+      const int st = it % S;
+      if (mbar_wait(&empty[st], ((it / S) & 1) ^ 1)) {
+        *reinterpret_cast<int*>(stages + (size_t)st * a.stage_bytes) = kItemEnd;
+        mbar_arrive(&full[st]);
+      }
+      ++it;
+      for (int k = (it > S ? it - S : 0); k < it; ++k) mbar_wait(&full[k % S], (k / S) & 1);
+    }
+  } else if (tid >= kPub) {
+    // ----------------------------------------------------------- publisher
+    const int lane = tid - kPub;
+    for (int k = 0;; ++k) {
+      bool ok = true;
+      if (lane == 0) ok = wait_smem_gt(done, k);
+      ok = __shfl_sync(kFull, ok, 0);
+      __syncwarp();
+      if (!ok) break;
+      const int4 q = reinterpret_cast<const int4*>(pubq)[k % kPubRing];
+      const int kind = q.x, l = q.y, slot = q.z, rr = q.w;
+      const int r0 = rr & 0xFFFF, nrows = rr >> 16;
+      const float* yv = yring + (k % kPubRing) * 32;
+      if (kind == kItemEnd) break;
+      // Every lane stores its own row value; after the warp barrier lane 0's
+      // release (red / atom .release.gpu, cumulative over the stores ordered
+      // before it) publishes them.  All lanes work at once: the warp's path
+      // through shared memory and L2 stays a few round trips long even while
+      // the consumers keep the shared-memory pipe busy.  Readers acquire,
+      // then bulk copy (after a proxy fence) or load with __ldcg.
+      const float y = lane < nrows ? yv[lane] : 0.0f;
+      if (kind == kItemPrep) {
+        if (lane == 0) red_release_gpu(ctr_xrows(a, 0), (unsigned)a.hidden);  // stores fenced by the consumers
+      } else if (kind == kItemUp) {
+        if (lane < nrows) {
+          const float v = fmaxf(y, 0.0f);
+          a.actsw[((size_t)(l & 1) * a.K + slot) * a.inter + sw_index(r0 + lane)] = v * v;
+        }
+        __syncwarp();
+        if (lane == 0) red_release_gpu(ctr_act(a, l, slot), (unsigned)nrows);
+      } else {
+        if (lane < nrows) a.contrib[((size_t)(l & 1) * a.K + slot) * a.hidden + r0 + lane] = y;
+        __syncwarp();
+        const int g0 = r0 >> 5, g1 = (r0 + nrows - 1) >> 5;
+        int last = -1;
+        if (lane <= g1 - g0) {
+          const int g = g0 + lane;
+          const int lo = max(r0, g << 5), hi = min(r0 + nrows, (g << 5) + 32);
+          const int grows = min(a.hidden, (g << 5) + 32) - (g << 5);
+          const unsigned old = atom_add_acq_rel_gpu(ctr_grp(a, l, g), (unsigned)(hi - lo));
+          if ((int)old + (hi - lo) == a.K * grows) last = g;
+        }
+        __syncwarp();
+        unsigned m = __ballot_sync(kFull, last >= 0);
+        while (m) {
+          const int src = __ffs(m) - 1;
+          m &= m - 1;
+          const int g = __shfl_sync(kFull, last, src);
+          const int grows = min(a.hidden, (g << 5) + 32) - (g << 5);
+          const int r = (g << 5) + lane;
+          if (lane < grows) {
+            const float* cb = a.contrib + (size_t)(l & 1) * a.K * a.hidden;
+            float acc = 0.0f;
+            for (int s2 = 0; s2 < a.K; ++s2)
+              acc = fmaf(__ldcg(cb + (size_t)s2 * a.hidden + r), a.route_w[l * a.K + s2], acc);
+            const float xv = __ldcg(a.xlin + (size_t)l * a.hidden + r) + acc;
+            if (l + 1 < a.L) {
+              a.xlin[(size_t)(l + 1) * a.hidden + r] = xv;
+              a.xsw[(size_t)(l + 1) * a.hidden + sw_index(r)] = xv;
+            } else {
+              a.out[r] = xv;
+            }
+          }
+          __syncwarp();
+          if (lane == 0 && l + 1 < a.L) red_release_gpu(ctr_xrows(a, l + 1), (unsigned)grows);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) st_release_cta(pub_done, k + 1);
+    }
+  } else {
+    // ----------------------------------------------------------- consumers
+    const SegPlace pu = seg_place(a.up, tid), pd = seg_place(a.dn, tid);
+    const int tr = tid >> 3, tw = tid & 7;
+    float2 x[16];
+    int last_key = -1;
+    bool ring_fail = false;  // tid 0: the publisher stopped taking items
+    int it = 0;
+    for (;; ++it) {
+      const int st = it % S;
+      const bool to = !mbar_wait(&full[st], (it / S) & 1) || ring_fail;
+      const uint8_t* sp = stages + (size_t)st * a.stage_bytes;
+      const int* hdr = reinterpret_cast<const int*>(sp);
+      const int kind = to ? kItemEnd : hdr[0];
+      int l = 0, slot = 0, r0 = 0, nrows = 0;
+      if (kind == kItemPrep) {
+        const int nu = a.hidden >> 5;
+        float4* xs0 = reinterpret_cast<float4*>(a.xsw);
+        for (int f = tid; f < nu * 8; f += kCT) {
+          const int t = f >> 3, k = f & 7;
+          xs0[t * 8 + (k ^ (t & 7))] = x_slot(a.x_in, t, k);
+        }
+        for (int i = tid; i < a.hidden; i += kCT) a.xlin[i] = a.x_in[i];
+        fence_proxy_async_global();
+        __threadfence();
+      } else if (kind == kItemUp || kind == kItemDown) {
+        l = hdr[1];
+        slot = hdr[2];
+        r0 = hdr[3];
+        nrows = hdr[4];
+        const bool up = kind == kItemUp;
+        const TokPhase& ph = up ? a.up : a.dn;
+        const SegPlace& sp2 = up ? pu : pd;
+        const int key = (kind << 24) | (l << 8) | slot;
+        bool x_stale = key != last_key;
+        last_key = key;
+        // a row of fewer than 64 units leaves chains 4 n_u..255 unwritten:
+        // zero them (the other projection's item may have left values there)
+        const int nch = 4 * ph.n_u;
+        if (nch < 256) {
+          const int w = 256 - nch;
+          for (int i = tid; i < nrows * w; i += kCT) {
+            const int rr = i / w;
+            part[rr * kRowPitch + part_index(nch + (i - rr * w))] = 0.0f;
+          }
+        }
+        if (sp2.active) {
+          const uint32_t stage_off = (uint32_t)(a.stage_base + st * a.stage_bytes + a.codes_off);
+          const float* lut = reinterpret_cast<const float*>(sp + kLutOff);
+          const float4* xs = reinterpret_cast<const float4*>(sp + kXOff);
+          if (nrows == ph.krt) {
+            segments<H, true>(smem, stage_off, ph.scale_off, ph.cb, ph.sb, sp2.team, ph.teams, sp2.par1,
+                              sp2.par2, sp2.cont, sp2.u1, sp2.u2, sp2.grp, nrows, lut, xs, x, x_stale,
+                              part);
+          } else {
+            segments<H, false>(smem, stage_off, ph.scale_off, ph.cb, ph.sb, sp2.team, ph.teams, sp2.par1,
+                               sp2.par2, sp2.cont, sp2.u1, sp2.u2, sp2.grp, nrows, lut, xs, x, x_stale,
+                               part);
+          }
+        }
+      }
+      // tid 0: this item's publisher ring slot must be free (the publisher
+      // has taken item it - kPubRing); a wait that runs out stops everyone
+      if (tid == 0 && !to && kind != kItemEnd && !wait_smem_gt(pub_done, it - kPubRing)) ring_fail = true;
+      // every read of the stage is done; a timeout anywhere stops all consumers
+      const bool stop = named_bar_or(kBarC, kCT, to || ring_fail);
+      if (tid == 0 && !stop && kind != kItemEnd) mbar_arrive(&empty[st]);
+      if (stop || kind == kItemEnd) break;
+      if (kind != kItemPrep) {
+        float y = 0.0f;
+        if (tr < nrows) y = group_tree(part + tr * kRowPitch + tw * kGroupPitch);
+        y = combine8(y);
+        if (tw == 0 && tr < nrows) yring[(it % kPubRing) * 32 + tr] = y;
+      }
+      named_bar_sync(kBarC, kCT);  // the chain buffer is rewritten by the next item
+      if (tid == 0) {  // hand the item to the publisher
+        reinterpret_cast<int4*>(pubq)[it % kPubRing] = make_int4(kind, l, slot, r0 | (nrows << 16));
+        st_release_cta(done, it + 1);
+      }
+    }
+    // end marker for the publisher
+    if (tid == 0 && !ring_fail && wait_smem_gt(pub_done, it - kPubRing)) {
+      pubq[(it % kPubRing) * 4] = kItemEnd;
+      st_release_cta(done, it + 1);
+    }
+  }
+
+  // the last CTA to leave resets the counters for the next token
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(ctr_exited(a), 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (s_last) {
+    __threadfence();
+    for (int i = tid; i < a.n_ctr; i += kTokThreads) a.ctr[i] = 0u;
+  }
+}
+
+// ---------------------------------------------------------------- host
+
+int row_block_tok(int cols) {
+  int g = 256;
+  while (cols % g != 0) g >>= 1;
+  return 256 / g;
+}
+
+inline int align_up_tok(int v, int a) { return (v + a - 1) / a * a; }
+
+int env_int(const char* name, int dflt, int lo, int hi) {
+  const char* e = getenv(name);
+  int v = e ? atoi(e) : dflt;
+  return v < lo ? lo : (v > hi ? hi : v);
+}
+
+TokPhase make_phase(int rows, int cols) {
+  TokPhase p{};
+  p.rows = rows;
+  p.cols = cols;
+  p.n_u = cols / 32;
+  p.n2 = p.n_u > 64 ? p.n_u - 64 : 0;
+  p.teams = kCT / p.n_u;
+  if (p.teams > 16) p.teams = 16;
+  p.cb = cols / 2;
+  p.sb = cols / 16;
+  return p;
+}
+
+template <typename K>
+int set_smem_tok(K kernel, int bytes) {
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return kErrLaunch;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+    return kErrLaunch;
+  return kOk;
+}
+
+template <int H>
+int launch_token_h(const TokArgs& a, int smem, bool pdl, cudaStream_t stream) {
+  if (set_smem_tok(moe_token_kernel<H>, smem)) return kErrLaunch;
+  int dev = 0, sms = 0, occ = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, moe_token_kernel<H>, kTokThreads, smem) !=
+      cudaSuccess)
+    return kErrLaunch;
+  if (occ < 1) return kErrShape;
+  if (occ > 2) occ = 2;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(sms * occ);
+  cfg.blockDim = dim3(kTokThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, moe_token_kernel<H>, a) == cudaSuccess ? kOk : kErrLaunch;
+}
+
+}  // namespace
+
+size_t moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top_k) {
+  const size_t n_ctr = token_ctr_words(n_layers, top_k, (hidden + 31) / 32);
+  const size_t ctr = (n_ctr * 4 + 255) / 256 * 256;
+  return ctr + 4 * ((size_t)2 * n_layers * hidden + (size_t)2 * top_k * inter + (size_t)2 * top_k * hidden);
+}
+
+int launch_moe_token(const MoeTokenArgs& in, cudaStream_t stream) {
+  TokArgs a{};
+  a.layer_ptrs = in.layer_ptrs;
+  a.up_cs = in.up_code_stride;
+  a.up_ss = in.up_scale_stride;
+  a.dn_cs = in.dn_code_stride;
+  a.dn_ss = in.dn_scale_stride;
+  a.ids = in.ids;
+  a.route_w = in.route_w;
+  a.x_in = in.x;
+  a.out = in.out;
+  a.L = in.n_layers;
+  a.K = in.top_k;
+  a.E = in.n_experts;
+  a.hidden = in.hidden;
+  a.inter = in.inter;
+  a.G = (in.hidden + 31) / 32;
+  a.up = make_phase(in.inter, in.hidden);
+  a.dn = make_phase(in.hidden, in.inter);
+  const int blk_u = row_block_tok(in.hidden), blk_d = row_block_tok(in.inter);
+
+  int dev = 0, smem_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  const int budget = (smem_sm - 2 * 1024) / 2;  // two CTAs per SM
+  const int x_bytes = 4 * (in.hidden > in.inter ? in.hidden : in.inter);
+  // Largest rows-per-segment H whose ring of at least min_stages stages fits
+  // two CTAs per SM; the ring then takes every stage that fits (at most 4).
+  // ERVF_TOKEN_H / ERVF_TOKEN_STAGES (read once per process) cap H and raise
+  // the minimum depth for tuning; results are the same for every choice.
+  static const int max_h = env_int("ERVF_TOKEN_H", 4, 1, 4);
+  static const int min_stages = env_int("ERVF_TOKEN_STAGES", 2, 2, kTokMaxStages);
+  static const int prefetch = env_int("ERVF_TOKEN_PREFETCH", 1, 0, 1);
+  a.prefetch = prefetch;
+  int h = 0, smem = 0;
+  for (int cand = max_h; cand >= 1; --cand) {
+    const int ku = a.up.teams * 2 * cand, kd = a.dn.teams * 2 * cand;
+    if (ku > 32 || kd > 32 || ku % blk_u || kd % blk_d) continue;
+    const int codes_off = align_up_tok(kXOff + x_bytes, 128);
+    const int wu = ku * a.up.cb + align_up_tok(ku * a.up.sb, 16);
+    const int wd = kd * a.dn.cb + align_up_tok(kd * a.dn.sb, 16);
+    const int stage = align_up_tok(codes_off + (wu > wd ? wu : wd), 128);
+    const int kmax = ku > kd ? ku : kd;
+    const int part_off = align_up_tok(kTabOff + token_tab_bytes(in.n_layers, in.top_k), 128);
+    const int base = align_up_tok(part_off + kmax * kRowPitch * 4, 128);
+    int stages = (budget - base) / stage;
+    if (stages > kTokMaxStages) stages = kTokMaxStages;
+    if (stages >= min_stages) {
+      h = cand;
+      a.up.krt = ku;
+      a.dn.krt = kd;
+      a.codes_off = codes_off;
+      a.stage_bytes = stage;
+      a.stage_base = base;
+      a.part_off = part_off;
+      a.stages = stages;
+      smem = base + stages * stage;
+      break;
+    }
+  }
+  if (h == 0) return kErrShape;
+  a.up.scale_off = a.up.krt * a.up.cb;
+  a.dn.scale_off = a.dn.krt * a.dn.cb;
+  a.up.n_items = (a.up.rows + a.up.krt - 1) / a.up.krt;
+  a.dn.n_items = (a.dn.rows + a.dn.krt - 1) / a.dn.krt;
+  a.per_layer = a.K * (a.up.n_items + a.dn.n_items);
+  a.total = 1 + a.L * a.per_layer;
+
+  uint8_t* s = reinterpret_cast<uint8_t*>(in.scratch);
+  a.n_ctr = (int)token_ctr_words(a.L, a.K, a.G);
+  a.ctr = reinterpret_cast<unsigned*>(s);
+  s += ((size_t)a.n_ctr * 4 + 255) / 256 * 256;
+  a.xlin = reinterpret_cast<float*>(s);
+  s += (size_t)4 * a.L * a.hidden;
+  a.xsw = reinterpret_cast<float*>(s);
+  s += (size_t)4 * a.L * a.hidden;
+  a.actsw = reinterpret_cast<float*>(s);
+  s += (size_t)4 * 2 * a.K * a.inter;
+  a.contrib = reinterpret_cast<float*>(s);
+
+  switch (h) {
+    case 4: return launch_token_h<4>(a, smem, in.pdl, stream);
+    case 3: return launch_token_h<3>(a, smem, in.pdl, stream);
+    case 2: return launch_token_h<2>(a, smem, in.pdl, stream);
+    default: return launch_token_h<1>(a, smem, in.pdl, stream);
+  }
+}
+
+int read_token_device_error(bool clear) { return read_unit_error(clear); }
+
+}  // namespace ervf

@@ -24,6 +24,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tma_core.cuh"
 
 namespace ervf {
 
@@ -204,10 +205,6 @@ __global__ void __launch_bounds__(256) nvfp4_gemv_sched(GemvBatch p, int tiles_p
 // memories alive until all reads are done.  Same arithmetic, no atomics and
 // no contrib round trip through L2.
 
-constexpr int kCW = 8;          // consumer warps
-constexpr int kCT = kCW * 32;   // consumer threads
-constexpr int kBarC = 1;        // named barrier of the consumer threads
-
 struct TmaCfg {
   int stages;       // ring depth
   int stage_bytes;  // bytes per stage (128-aligned)
@@ -238,6 +235,10 @@ struct TmaCfg {
 constexpr int kPartOff = 576;
 
 constexpr int kYsmRows = 512;  // rows per cluster range (cluster mode)
+#ifndef ERVF_BULK_PIECE
+#define ERVF_BULK_PIECE 4096
+#endif
+constexpr uint32_t kBulkPiece = ERVF_BULK_PIECE;  // bytes per bulk copy of an item's code rows
 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -252,139 +253,6 @@ __device__ __forceinline__ float ld_dsmem(const float* p, uint32_t rank) {
   return v;
 }
 
-// One 16-byte code unit (4 chains x 8 codes) of one row, continuing the four
-// chain accumulators: acc[0] = (chain 0, chain 1), acc[1] = (chain 2, chain 3).
-// Chains 0,1 use the block scale s0 = s_2u, chains 2,3 use s1 = s_2u+1.  The
-// activation comes pre-paired: xp[m] = (x[m], x[8 + m]) and xp[8 + m] =
-// (x[16 + m], x[24 + m]) for code m of the chain pair, x[8j + m] being the
-// activation of chain j's m-th code.  Each step is one packed multiply
-// (w = RN(e2m1 * s) for two chains) and one packed FMA (acc = fmaf(w, x, acc)
-// for two chains): the same IEEE operations, in the same per-chain order, as
-// the scalar chain.
-__device__ __forceinline__ void unit_fma(const uint4 q, const float s0, const float s1,
-                                         const float2 (&xp)[16], float2 (&acc)[2]) {
-  uint32_t h0[4], h1[4], h2[4], h3[4];
-  e2m1x8_to_f16x2(q.x, h0);
-  e2m1x8_to_f16x2(q.y, h1);
-  e2m1x8_to_f16x2(q.z, h2);
-  e2m1x8_to_f16x2(q.w, h3);
-  const float2 sa = make_float2(s0, s0), sb = make_float2(s1, s1);
-  float2 a01 = acc[0], a23 = acc[1];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __half2 v0 = *reinterpret_cast<const __half2*>(&h0[i]);
-    const __half2 v1 = *reinterpret_cast<const __half2*>(&h1[i]);
-    const __half2 v2 = *reinterpret_cast<const __half2*>(&h2[i]);
-    const __half2 v3 = *reinterpret_cast<const __half2*>(&h3[i]);
-    a01 = fma2(mul2(make_float2(__low2float(v0), __low2float(v1)), sa), xp[2 * i], a01);
-    a23 = fma2(mul2(make_float2(__low2float(v2), __low2float(v3)), sb), xp[8 + 2 * i], a23);
-    a01 = fma2(mul2(make_float2(__high2float(v0), __high2float(v1)), sa), xp[2 * i + 1], a01);
-    a23 = fma2(mul2(make_float2(__high2float(v2), __high2float(v3)), sb), xp[9 + 2 * i], a23);
-  }
-  acc[0] = a01;
-  acc[1] = a23;
-}
-
-// SiLU of the gate row, v / (1 + e^-v) in binary32 (CUDA expf).
-__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
-
-// Shared copy of the activation: unit t (32 columns) holds 8 float4 slots;
-// slot k = (x[c], x[c + 8], x[c + 1], x[c + 9]) with c = 16 (k >> 2) + 2 (k & 3)
-// (column offsets inside the unit), stored at t * 8 + (k ^ (t & 7)) so that
-// the eight readers of one slot index hit different bank groups.  One slot
-// is two of the pairs unit_fma consumes.
-__device__ __forceinline__ float4 x_slot(const float* x, int t, int k) {
-  const int c = 32 * t + 16 * (k >> 2) + 2 * (k & 3);
-  const float2 a = *reinterpret_cast<const float2*>(x + c);
-  const float2 b = *reinterpret_cast<const float2*>(x + c + 8);
-  return make_float4(a.x, b.x, a.y, b.y);
-}
-
-__device__ __forceinline__ float4 x_slot_cg(const float* x, int t, int k) {
-  const int c = 32 * t + 16 * (k >> 2) + 2 * (k & 3);
-  const float2 a = __ldcg(reinterpret_cast<const float2*>(x + c));
-  const float2 b = __ldcg(reinterpret_cast<const float2*>(x + c + 8));
-  return make_float4(a.x, b.x, a.y, b.y);
-}
-
-// The activation pairs of unit u from the shared copy.
-__device__ __forceinline__ void load_unit_x(const float4* xs, int u, float2 (&xp)[16]) {
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const float4 v = xs[u * 8 + (k ^ (u & 7))];
-    xp[2 * k] = make_float2(v.x, v.y);
-    xp[2 * k + 1] = make_float2(v.z, v.w);
-  }
-}
-
-// The two segments of one consumer thread for one item (see the schedule
-// above).  FULL: every row of the item exists, so the H rows of a segment run
-// unconditionally and interleave.
-// H rows of one segment, unit fixed: code / scale byte offsets (into the
-// stage, relative to smem) advance by rstep / sstep per row; block scales come
-// from the job's table of RN(e4m3 * g).
-template <int H, bool FULL>
-__device__ __forceinline__ void seg_rows(const uint8_t* smem, uint32_t coff, uint32_t soff,
-                                         uint32_t rstep, uint32_t sstep, const float* lut,
-                                         const float2 (&x)[16], float2 (&acc)[H][2], int row0,
-                                         int rowstep, int nrows) {
-#pragma unroll
-  for (int h = 0; h < H; ++h) {
-    if (FULL || row0 + h * rowstep < nrows) {
-      const uint4 q = *reinterpret_cast<const uint4*>(smem + coff + h * rstep);
-      const uint32_t s2 = *reinterpret_cast<const uint16_t*>(smem + soff + h * sstep);
-      unit_fma(q, lut[s2 & 0xFFu], lut[s2 >> 8], x, acc[h]);
-    }
-  }
-}
-
-template <int H, bool FULL>
-__device__ __forceinline__ void seg_store(float* part, uint32_t poff, uint32_t pstep,
-                                          const float2 (&acc)[H][2], int row0, int rowstep,
-                                          int nrows) {
-#pragma unroll
-  for (int h = 0; h < H; ++h)
-    if (FULL || row0 + h * rowstep < nrows)
-      *reinterpret_cast<float4*>(part + poff + h * pstep) =
-          make_float4(acc[h][0].x, acc[h][0].y, acc[h][1].x, acc[h][1].y);
-}
-
-// The two segments of one consumer thread for one item (see the schedule
-// above).  FULL: every row of the item exists, so the H rows of a segment run
-// unconditionally and interleave.  stage_off: the stage's byte offset in smem.
-template <int H, bool FULL>
-__device__ __forceinline__ void segments(const uint8_t* smem, uint32_t stage_off, int scale_off,
-                                         int cb, int sb, int team, int T, int par1, int par2,
-                                         bool cont, int u1, int u2, int grp, int nrows,
-                                         const float* lut, const float4* xs, float2 (&x)[16],
-                                         bool& x_stale, float* part) {
-  float2 acc[H][2];
-#pragma unroll
-  for (int h = 0; h < H; ++h) acc[h][0] = acc[h][1] = make_float2(0.0f, 0.0f);
-  const int rowstep = 2 * T;
-  const uint32_t rstep = (uint32_t)(rowstep * cb), sstep = (uint32_t)(rowstep * sb);
-  const uint32_t pstep = (uint32_t)(rowstep * kRowPitch);
-  const int row1 = team + T * par1, row2 = team + T * par2;
-  if (cont || x_stale) load_unit_x(xs, u1, x);
-  x_stale = false;
-  seg_rows<H, FULL>(smem, stage_off + row1 * cb + 16 * u1, stage_off + scale_off + row1 * sb + 2 * u1,
-                    rstep, sstep, lut, x, acc, row1, rowstep, nrows);
-  if (!cont) {
-    seg_store<H, FULL>(part, row1 * kRowPitch + part_index(4 * grp), pstep, acc, row1, rowstep, nrows);
-#pragma unroll
-    for (int h = 0; h < H; ++h) acc[h][0] = acc[h][1] = make_float2(0.0f, 0.0f);
-  } else {
-    load_unit_x(xs, u2, x);
-  }
-  seg_rows<H, FULL>(smem, stage_off + row2 * cb + 16 * u2, stage_off + scale_off + row2 * sb + 2 * u2,
-                    rstep, sstep, lut, x, acc, row2, rowstep, nrows);
-  seg_store<H, FULL>(part, row2 * kRowPitch + part_index(4 * grp), pstep, acc, row2, rowstep, nrows);
-}
-
-__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void grid_dep_launch() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
 
 // The CTA's items: row blocks [blk, blk_end) of the flattened (active job,
 // block) space, cut at job ends and at kb blocks.
@@ -411,21 +279,6 @@ __device__ __forceinline__ bool next_item(ItemSeq& q, const TmaCfg& c, const int
   return true;
 }
 
-__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
-  unsigned old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
-
-__device__ __forceinline__ void st_release_cta(int* p, int v) {
-  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ int ld_acquire_cta(const int* p) {
-  int v;
-  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
-  return v;
-}
 
 // This CTA's slice of the L2 prefetch: the records are cut into 32 KB chunks,
 // numbered across records, and CTA b issues chunks b, b + grid, ...  Ids are
@@ -588,7 +441,14 @@ __global__ void __launch_bounds__(kCT + 32, 2) nvfp4_gemv_tma(GemvBatch p, TmaCf
         for (uint32_t i = s16; i < scale_bytes; ++i) dst[c.scale_off + i] = ssrc[i];
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_arrive_expect_tx(&full[st], code_bytes + s16);
-        bulk_g2s(dst, jc[job] + (size_t)r0 * cb, code_bytes, &full[st]);
+        // The code rows go as several bulk copies in flight at once: one
+        // copy streams at ~10 GB/s on B200 however large it is, so a whole
+        // item in one copy leaves HBM idle (measured: ~4 us for 36 KB)
+        const uint8_t* csrc = jc[job] + (size_t)r0 * cb;
+        for (uint32_t off = 0; off < code_bytes; off += kBulkPiece) {
+          const uint32_t n = code_bytes - off < kBulkPiece ? code_bytes - off : kBulkPiece;
+          bulk_g2s(dst + off, csrc + off, n, &full[st]);
+        }
         if (s16) bulk_g2s(dst + c.scale_off, ssrc, s16, &full[st]);
       }
       if (!prefetched) l2_prefetch_slice(p);
@@ -734,9 +594,15 @@ DevInfo& dev_info() {
 inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
 
+// Dynamic shared memory of a kernel, with the shared-memory carve-out at its
+// maximum: the driver otherwise may pick the smallest carve-out that fits
+// one CTA, and two ~113 KB CTAs of the TMA schedule then no longer share an SM.
 template <typename K>
 int set_smem(K kernel, int bytes) {
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return kErrLaunch;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared) != cudaSuccess)
     return kErrLaunch;
   return kOk;
 }

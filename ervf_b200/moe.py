@@ -167,6 +167,18 @@ class MoEDecoder:
         self.prefetch = True
         nb = _lib.load().ervf_routesum_scratch_bytes(bank.hidden, k)
         self.scratch = torch.zeros(nb, dtype=torch.uint8, device=d)
+        # One launch per token on one GPU (ervf_moe_token: every layer's up
+        # and down rows as one claimed work list, bit-identical to the
+        # per-layer launches); False runs the per-layer launches.
+        self.token = ep_ranks == 1
+        self.layer_ptrs = self.tok_scratch = None
+        if self.token:
+            addrs = ([ptr(t) for t in bank.up_codes] + [ptr(t) for t in bank.up_scales]
+                     + [ptr(t) for t in bank.dn_codes] + [ptr(t) for t in bank.dn_scales]
+                     + [ptr(t) for t in bank.globals])
+            self.layer_ptrs = torch.tensor(addrs, dtype=torch.int64, device=d)
+            nb = _lib.load().ervf_moe_token_scratch_bytes(L, bank.hidden, bank.inter, k)
+            self.tok_scratch = torch.zeros(nb, dtype=torch.uint8, device=d)
 
     def _s(self) -> int:
         return int(torch.cuda.current_stream(self.bank.device).cuda_stream)
@@ -325,9 +337,24 @@ class MoEDecoder:
         router logits of every layer.  Returns the buffer holding x after
         the last layer."""
         self.route(rlogs)
+        if self.token and self.ep_ranks == 1:
+            out = self.xs[(self.bank.n_layers - 1) & 1]
+            self.token_step(x_in, out)
+            return out
         cur = x_in
         for l in range(self.bank.n_layers):
             nxt = self.xs[l & 1]
             self.layer(l, cur, nxt, first=(l == 0))
             cur = nxt
         return cur
+
+    def token_step(self, x_in: torch.Tensor, out: torch.Tensor) -> None:
+        """Every layer of one token in one launch with the routes already in
+        self.ids / self.w: out = x_L, bit-identical to the per-layer chain
+        (out may be x_in)."""
+        b = self.bank
+        _lib.call("ervf_moe_token", ptr(self.layer_ptrs), b.n_layers, int(b.up_code_bytes),
+                  int(b.up_scale_bytes), int(b.dn_code_bytes), int(b.dn_scale_bytes), ptr(self.ids),
+                  ptr(self.w), self.top_k, b.n_experts, ptr(x_in), ptr(out), b.hidden, b.inter,
+                  ptr(self.tok_scratch), self.tok_scratch.numel(),
+                  _lib.LAUNCH_PDL if self.pdl else 0, self._s())

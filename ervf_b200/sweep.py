@@ -13,9 +13,11 @@ Numerics, per node (activation row):
     tree) on that node's row, which is what the reference's batched kernel
     computes per column (ervf_nvfp4_gemm_rows_b).
   * ``down_union`` returns the reference's ``down_union`` bit for bit: the
-    masked panel-major down projection per node (a column where a node is
-    zero adds fmaf(w, 0, acc) = acc, so the union mask the reference walks and
-    the node's own mask agree), scattered to ``contrib[dst[b]]``.
+    masked panel-major down projection of every node over the UNION panel
+    list and masks of the expert's nodes (ervf_down_union), scattered to
+    ``contrib[dst[b]]``.  The union matters: the masked path assigns panels
+    to its chunks by their position in the active list, so a node's bits
+    depend on the other nodes' zero pattern.
   * ``moe_block`` ends with ``reduce_slots``: out[b] = fmaf(w, contrib, out)
     over the route slots in order (the token-major path's order).
 
@@ -73,6 +75,7 @@ class SweepMoE:
         state = self.fused.alloc_masked_state(hidden, inter)
         state.update({
             "acts": z(nb * inter),
+            "act_sum": z(inter),
             "contrib": z(B * top_k * hidden),
             "weights": z(B * top_k),
             "xbuf": z(nb * max(hidden, inter)),
@@ -104,7 +107,7 @@ class SweepMoE:
         ``gather_from_host`` changes nothing in the result."""
         _lib.call("ervf_down_union", ptr(bank_ptr), ptr(state["acts"]), int(n), ptr(dst),
                   ptr(state["contrib"]), float(np.float32(global_scale)), int(hidden), int(inter),
-                  int(state["nchunks"]), ptr(state["masks"]), ptr(state["plist"]),
+                  int(state["nchunks"]), ptr(state["act_sum"]), ptr(state["masks"]), ptr(state["plist"]),
                   ptr(state["pcount"]), ptr(state["nz"]), ptr(state["nzc"]), ptr(state["tmp"]),
                   self.fused._s())
 

@@ -159,6 +159,34 @@ ERVF_API int ervf_moe_layer(const uint8_t* up_codes, const uint8_t* up_scales, s
                             const uint8_t* next_up_scales, const int32_t* next_ids, int flags,
                             void* stream);
 
+/* One decode token through EVERY routed MoE layer, one launch (single GPU):
+ * for l = 0..n_layers-1, x_{l+1} = ervf_moe_layer(layer l, x_l) bit for bit
+ * (same chains, tree, relu^2 and route-order sum; x_0 = x), out = x_L.  The
+ * CTAs claim row items of every layer's up and down projections in order
+ * from a device counter and wait (bounded) only on the activations an item
+ * needs, so expert weights stream while the previous projection finishes and
+ * no launch boundary separates the layers.  The reference runs the same
+ * layers as per-expert launches (runtime.py:705-746 over
+ * fused_nvfp4.py:970-984).
+ * layer_ptrs: device array of 5 * n_layers addresses: [0, L) up code bases,
+ * [L, 2L) up scale bases, [2L, 3L) down code bases, [3L, 4L) down scale
+ * bases, [4L, 5L) globals f32[n_experts][2] (down, up) of each layer; expert
+ * e of layer l sits at base + e * stride.  ids int32[L][top_k] and route_w
+ * f32[L][top_k] on the device (ids clamped into [0, n_experts)).  out may be
+ * x.  scratch: ervf_moe_token_scratch_bytes bytes, 256-byte aligned, zeroed
+ * once before first use; every launch leaves its counters zero again, also
+ * after a timeout (the last CTA to leave resets them).  Launches sharing a
+ * scratch must not overlap.  flags: ERVF_LAUNCH_PDL or 0.  Bases and strides
+ * 16-byte aligned; hidden, inter multiples of 32, <= 4096; top_k <= 16. */
+ERVF_API int ervf_moe_token(const uint64_t* layer_ptrs, int n_layers, size_t up_code_stride,
+                            size_t up_scale_stride, size_t dn_code_stride, size_t dn_scale_stride,
+                            const int32_t* ids, const float* route_w, int top_k, int n_experts,
+                            const float* x, float* out, int hidden, int inter, void* scratch,
+                            size_t scratch_bytes, int flags, void* stream);
+
+/* Bytes of scratch ervf_moe_token uses (counters and per-layer activations). */
+ERVF_API size_t ervf_moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top_k);
+
 /* ervf_moe_down_routesum without a scratch argument.  No counterpart in the
  * reference.  The scratch is a fixed device array inside the library, so the
  * call allocates nothing: hidden <= 8192 and top_k <= 8, else
@@ -331,15 +359,17 @@ ERVF_API int ervf_nvfp4_gemm_rows_b(const uint8_t* codes, const uint8_t* scales,
 
 /* ervf_down_union: contrib[dst[b]*hidden + r] = the masked panel-major down
  * projection of acts[b*inter ..] (the record at `bank`, runtime.py:34-52
- * layout), b < n <= 64 -- bit-identical to the reference's down_union
- * (gemm_down_masked_b over the union panel mask + reduce_partials_scatter,
- * sweepspec.py:143-216: a column where node b is zero adds fmaf(w, 0, acc) =
- * acc, so the union mask and b's own mask give the same bits).  masks ..
- * nzc: the masked-down state of ervf_down_masked; tmp: n*hidden floats. */
+ * layout), b < n <= 64, walking the UNION panel list and masks of the n nodes
+ * -- bit-identical to the reference's down_union (act_sum = sum of the
+ * nodes' rows, panel_scan of it, gemm_down_masked_b, reduce_partials_scatter;
+ * sweepspec.py:143-216, :331-360).  The union matters: panels go to chunks
+ * by their position in the active list, so a node's bits depend on the other
+ * nodes' zero pattern.  act_sum: inter floats; masks .. nzc: the masked-down
+ * state of ervf_down_masked; tmp: n*hidden floats. */
 ERVF_API int ervf_down_union(const uint8_t* bank, const float* acts, int n, const int32_t* dst,
                             float* contrib, float global_scale, int hidden, int inter, int nchunks,
-                            uint32_t* masks, int32_t* plist, int32_t* pcount, int32_t* nz,
-                            int32_t* nzc, float* tmp, void* stream);
+                            float* act_sum, uint32_t* masks, int32_t* plist, int32_t* pcount,
+                            int32_t* nz, int32_t* nzc, float* tmp, void* stream);
 
 /* ervf_reduce_slots: out[b*rows + r] = fmaf(weights[b*top_k + s],
  * contrib[(b*top_k + s)*rows + r], .) over s = 0..top_k-1 in route-slot

@@ -135,6 +135,36 @@ def test_decoder_step_pdl_chain_matches_oracle(fused, oracle, bank, cuda):
         assert bits_equal(y.cpu().numpy(), want), (use_graph, prefetch)
 
 
+@pytest.mark.parametrize("hidden,inter,E,k,L", [(2688, 1856, 8, 6, 3), (1024, 512, 8, 4, 2),
+                                                 (4096, 2048, 4, 2, 2), (512, 1024, 6, 1, 3)])
+def test_token_launch_equals_layer_chain(fused, cuda, hidden, inter, E, k, L):
+    """ervf_moe_token (every layer of a token in one launch) equals the
+    per-layer launches (ervf_moe_layer) bit for bit on the same routes, for
+    three tokens back to back on one scratch, whose counters the kernel
+    leaves zero."""
+    from ervf_b200.moe import ExpertBank, MoEDecoder
+
+    eb = ExpertBank.synthetic(L, E, hidden, inter, cuda, seed=5)
+    dec = MoEDecoder(eb, k)
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(9)
+    for t in range(3):
+        rl = torch.randn(L, E, generator=gen, device=cuda)
+        x = torch.randn(hidden, generator=gen, device=cuda) * 0.05
+        dec.token = True
+        y_tok = dec.step(x, rl).clone()
+        dec.token = False
+        y_ref = dec.step(x, rl).clone()
+        torch.cuda.synchronize()
+        assert np.isfinite(y_ref.cpu().numpy()).all()
+        assert bits_equal(y_tok.cpu().numpy(), y_ref.cpu().numpy()), f"token {t}"
+    n_ctr = 32 * (2 + L + L * k) + L * ((hidden + 31) // 32)
+    assert int(dec.tok_scratch[:4 * n_ctr].view(torch.int32).abs().sum()) == 0
+    from ervf_b200 import _lib
+
+    assert _lib.load().ervf_device_status() == 0
+
+
 def test_decoder_step_with_router_matches_oracle(fused, oracle, bank, cuda):
     """Three layers with the router on the device between them (router GEMV +
     top-k, up, down + routed sum per layer, PDL-chained, eager and in a CUDA

@@ -82,6 +82,8 @@ def test_down_union_equals_reference(ref, fused, sweep, oracle, cuda, n):
     r = np.random.default_rng(n)
     acts = np.maximum(r.standard_normal((n, INTER)), 0).astype(np.float32) ** 2  # ~50 % zeros
     acts[:, 100:300] = 0.0  # whole zero panels for every node
+    for b in range(n):  # and a panel that only node b leaves empty: the union list differs
+        acts[b, 16 * (30 + b):16 * (31 + b)] = 0.0
     top_k, B = 6, 8
     dst = _t(r.choice(B * top_k, n, replace=False).astype(np.int32), cuda)
     want = torch.zeros(B * top_k * HIDDEN, device=cuda)
