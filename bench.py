@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--no-extras", action="store_true",
                     help="only the decode-step line (no per-kernel, GEMV, batch-32 or router keys)")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--bank", choices=["quantized", "random"], default="quantized",
+                    help="random: expert records of seeded random bytes (same shapes and "
+                         "bytes, a few launches to build; for profiler runs)")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel exchange of the slot outputs (N > 1)")
     ap.add_argument("--gemv", type=int, nargs=2, metavar=("ROWS", "COLS"),
@@ -176,6 +179,25 @@ def time_graph(fn, steps, device):
     return a.elapsed_time(b) / steps
 
 
+def random_bank(L, device):
+    """A bank of seeded random code bytes and scale bytes 0x28..0x37 (E4M3
+    0.25..0.47) with global scale 1/64: the bench's shapes and bytes in a
+    handful of launches, for profiler runs whose time goes into every launch."""
+    from ervf_b200.moe import ExpertBank
+
+    bank = ExpertBank(L, N_EXPERTS, HIDDEN, INTER, device)
+    g = torch.Generator(device=device)
+    for l in range(L):
+        g.manual_seed(7000 + l)
+        for t in (bank.up_codes[l], bank.dn_codes[l]):
+            t.copy_(torch.randint(0, 256, t.shape, generator=g, device=device, dtype=torch.int32).to(torch.uint8))
+        for t in (bank.up_scales[l], bank.dn_scales[l]):
+            t.copy_(torch.randint(0x28, 0x38, t.shape, generator=g, device=device, dtype=torch.int32).to(torch.uint8))
+        bank.globals[l].fill_(1.0 / 64.0)
+    torch.cuda.synchronize(device)
+    return bank
+
+
 def kernel_roofline(dec, bank, device, hbm, iters=192):
     """Average device time of the two grouped expert kernels (a CUDA graph of
     `iters` launches each, timed with CUDA events), each launch on a
@@ -216,6 +238,22 @@ def kernel_roofline(dec, bank, device, hbm, iters=192):
         "moe_up_grouped": {"ms": t_up, "bytes": up_bytes, "gbs": up_bytes / t_up / 1e6},
         "moe_down_routesum": {"ms": t_dn, "bytes": dn_bytes, "gbs": dn_bytes / t_dn / 1e6},
     }
+    if dec.token:
+        # the one-launch token kernel (the decode step's kernel on one GPU):
+        # every launch on its own routing of all L layers
+        tok_ids = ids[: (iters // L) * L].view(-1, L, TOP_K)[:8]
+        tok_w = torch.full((L, TOP_K), 1.0 / TOP_K, device=device)
+        xt = (x * 0.0625).contiguous()
+        yt = torch.zeros(HIDDEN, device=device)
+
+        def token(i):
+            dec.token_step(xt, yt, tok_ids[i % tok_ids.shape[0]], tok_w)
+
+        for i in range(4):
+            token(i)
+        t_tok = time_graph(token, 16, device)
+        tok_bytes = L * (TOP_K * 2 * rec + 3 * HIDDEN * 4 + 2 * TOP_K * INTER * 4)
+        res["moe_token"] = {"ms": t_tok, "bytes": tok_bytes, "gbs": tok_bytes / t_tok / 1e6}
     for v in res.values():
         v["frac"] = v["gbs"] / hbm
     return res
@@ -511,7 +549,10 @@ def main():
     t0 = time.time()
     # every rank builds only the experts it owns (e % world == rank); seeds
     # 1000 * layer + expert (+500 for down), N(0, 0.02), quantised on the device
-    bank = ExpertBank.synthetic(L, N_EXPERTS, HIDDEN, INTER, device, rank=rank, world=world)
+    if args.bank == "random":
+        bank = random_bank(L, device)
+    else:
+        bank = ExpertBank.synthetic(L, N_EXPERTS, HIDDEN, INTER, device, rank=rank, world=world)
     torch.cuda.synchronize(device)
     build_s = time.time() - t0
 
@@ -607,6 +648,8 @@ def main():
     full = not args.no_extras
     kern = kernel_roofline(dec, bank, device, hbm) if (world == 1 and full) else None
     gemv0 = gemv_shape(device, hbm) if (world == 1 and rank == 0 and full) else None
+    # the lm_head shape (131072 x 2688, L2-cold replicas), one launch per call
+    lmhead = gemv_shape(device, hbm, 131072, HIDDEN) if (world == 1 and rank == 0 and full) else None
     batch32 = batched_decode(dec, device, hbm, world) if full else None
     routed = routed_decode(dec, device, hbm) if (world == 1 and full) else None
     extra = None
@@ -633,9 +676,10 @@ def main():
                        "exchange": args.exchange if world > 1 else None,
                        "l2": "inputs larger than L2 (17.2 GB bank, 808 MB streamed per token)",
                        "cuda_graph": graph is not None},
-            # router + per layer: up, down(+route sum) on one GPU; up, down,
-            # exchange(+route sum) or route sum after the all-gather with N > 1
-            "gpu_launches": (2 * L + 1 if world == 1 else 3 * L + 1) * args.steps,
+            # router + the one-launch token kernel on one GPU (router + per
+            # layer up, down(+route sum) without it); up, down, exchange(+route
+            # sum) or route sum after the all-gather with N > 1
+            "gpu_launches": ((2 if dec.token else 2 * L + 1) if world == 1 else 3 * L + 1) * args.steps,
             "token_bytes": token_bytes,
             "token_roofline_frac": (token_bytes / (ms / args.steps / 1e3) / 1e9) / (hbm * world),
             "clocks": clocks,
@@ -656,6 +700,8 @@ def main():
             line["kernels"] = kern
         if gemv0 is not None:
             line["gemv_config0"] = gemv0
+        if lmhead is not None:
+            line["gemv_lmhead_nvfp4"] = lmhead
         if extra is not None:
             line.update(extra)
         if batch32 is not None:

@@ -104,37 +104,6 @@ int launch_nvfp4_batch(const GemvBatch& b, int width, cudaStream_t stream);
 // cols <= 4096, 16-byte aligned bases and strides, routed-sum scratch).
 bool nvfp4_tma_ok(const GemvBatch& b);
 
-// Batched NVFP4 GEMM on the tensor cores (nvfp4_gemm_tc.cu):
-// out[n][r] = g * (W @ X[n])[r] for n < N <= 16, fp32 accumulate.
-int launch_nvfp4_gemm_tc(const uint8_t* codes, const uint8_t* scales, float g, const float* x,
-                         float* out, int rows, int cols, int n, cudaStream_t stream);
-
-// Expert-major grouped NVFP4 GEMM on the tensor cores (batched MoE block):
-// see TcArgs in nvfp4_gemm_tc.cu.
-struct GroupedTc {
-  const uint8_t* codes;   // expert bank base (expert e at e * code_stride)
-  const uint8_t* scales;
-  size_t code_stride, scale_stride;
-  const float* globals;   // [E][2]
-  int gsel;               // 1: up (g_up), 0: down (g_down)
-  const float* x;         // source rows
-  const int* b_idx;       // gather index per sorted pair (NULL: identity)
-  float* out;             // [pairs][rows]
-  int rows, cols;
-  const int* chunk_expert;
-  const int* chunk_off;
-  const int* chunk_n;
-  const int* n_chunks;
-  int max_chunks;
-  int relu2;
-  // K-split (1 or 2): part f32[ksplit][max_chunks][rows], ucnt u32[max_chunks *
-  // ceil(rows / 128)] zero before and left zero; results depend on ksplit
-  // (association of the partial sums), not on the grid or the arrival order
-  int ksplit;
-  float* part;
-  unsigned* ucnt;
-};
-int launch_grouped_tc(const GroupedTc& g, cudaStream_t stream);
 
 // Warp-specialised NVFP4 GEMM on the tensor cores (nvfp4_mma.cu).  The
 // activations come as f16 panels in the MMA's layout: panel[c][kb] = 8 KB

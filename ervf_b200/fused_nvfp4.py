@@ -256,6 +256,20 @@ class FusedNVFP4:
                   ptr(act), ptr(base), ptr(resid), ptr(out), int(hidden), int(inter),
                   ptr(scratch), int(_numel(scratch) or 0), self._width(), int(flags), self._s())
 
+    def device_status(self) -> int:
+        """Read and clear the library's device error words (waits for the
+        device: ervf_device_status).  After a bounded device wait ran out
+        (``_lib.ERR_TIMEOUT``) the counters in this object's cached scratch
+        buffers can be left non-zero, so they are zeroed again here and the
+        next call starts clean.  Returns the status (0 = no error)."""
+        st = int(_lib.load().ervf_device_status())
+        if st == _lib.ERR_TIMEOUT:
+            for buf in self.__dict__.get("_scratch_cache", {}).values():
+                buf.zero_()
+            if getattr(self, "_bscratch", None) is not None:
+                self._bscratch.zero_()
+        return st
+
     def routesum_scratch_bytes(self, hidden: int, top_k: int) -> int:
         return int(_lib.load().ervf_routesum_scratch_bytes(int(hidden), int(top_k)))
 

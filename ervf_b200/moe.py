@@ -348,13 +348,27 @@ class MoEDecoder:
             cur = nxt
         return cur
 
-    def token_step(self, x_in: torch.Tensor, out: torch.Tensor) -> None:
-        """Every layer of one token in one launch with the routes already in
-        self.ids / self.w: out = x_L, bit-identical to the per-layer chain
-        (out may be x_in)."""
+    def device_status(self) -> int:
+        """Read and clear the library's device error words; after a timeout
+        zero this decoder's scratch buffers (and the FusedNVFP4 caches) so the
+        next step starts from clean counters.  Returns the status."""
+        st = self.fused.device_status()
+        if st == _lib.ERR_TIMEOUT:
+            self.scratch.zero_()
+            if self.tok_scratch is not None:
+                self.tok_scratch.zero_()
+        return st
+
+    def token_step(self, x_in: torch.Tensor, out: torch.Tensor, ids: torch.Tensor | None = None,
+                   w: torch.Tensor | None = None) -> None:
+        """Every layer of one token in one launch with the routes in
+        self.ids / self.w (or the given int32 [L][top_k] ids and f32 weights):
+        out = x_L, bit-identical to the per-layer chain (out may be x_in)."""
         b = self.bank
+        ids = self.ids if ids is None else ids
+        w = self.w if w is None else w
         _lib.call("ervf_moe_token", ptr(self.layer_ptrs), b.n_layers, int(b.up_code_bytes),
-                  int(b.up_scale_bytes), int(b.dn_code_bytes), int(b.dn_scale_bytes), ptr(self.ids),
-                  ptr(self.w), self.top_k, b.n_experts, ptr(x_in), ptr(out), b.hidden, b.inter,
+                  int(b.up_scale_bytes), int(b.dn_code_bytes), int(b.dn_scale_bytes), ptr(ids),
+                  ptr(w), self.top_k, b.n_experts, ptr(x_in), ptr(out), b.hidden, b.inter,
                   ptr(self.tok_scratch), self.tok_scratch.numel(),
                   _lib.LAUNCH_PDL if self.pdl else 0, self._s())

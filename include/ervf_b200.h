@@ -401,7 +401,10 @@ ERVF_API size_t ervf_nvfp4_gemm_tc_scratch_bytes(int rows, int cols, int n);
  * accumulate; x is split into bf16 high and low halves (16 MMA columns), so
  * the result is held to rel-L2 <= 1e-3, not to gemv_bf16's chain order (the
  * reference has no batched BF16 kernel; ervf_bf16_gemv keeps that order).
- * cols % 32 == 0; W and x 16-byte aligned. */
+ * When a matrix has fewer 128-row tiles than the GPU has CTA slots, K is split
+ * over several CTAs whose fp32 partial sums are added atomically into out: the
+ * last bits then vary with the arrival order from call to call (always within
+ * the tolerance).  cols % 32 == 0; W and x 16-byte aligned. */
 ERVF_API int ervf_bf16_gemm_tc(const uint16_t* W, const float* x, float* out, int rows, int cols,
                                int batch, void* stream);
 
