@@ -437,9 +437,17 @@ def routed_decode(dec, device, hbm, steps=50):
     ms = time_graph(lambda i: dec.step_with_router(x, gate_w), steps, device)
     router_bytes = E * HIDDEN * 4 + HIDDEN * 4
     token_bytes = L * (TOP_K * dec.bank.expert_bytes() + router_bytes)
-    return {"ms_per_token": round(ms, 4), "tok_s": round(1e3 / ms, 1),
-            "launches_per_token": 3 * L, "token_bytes": token_bytes,
-            "frac": round(token_bytes / ms / 1e6 / hbm, 4)}
+    res = {"ms_per_token": round(ms, 4), "tok_s": round(1e3 / ms, 1),
+           "launches_per_token": 1 if (dec.token and dec.token_router) else 3 * L,
+           "token_bytes": token_bytes,
+           "frac": round(token_bytes / ms / 1e6 / hbm, 4)}
+    if dec.token and not dec.token_router:
+        # the same step with the routers inside the one-launch token kernel
+        dec.token_router = True
+        ms1 = time_graph(lambda i: dec.step_with_router(x, gate_w), steps, device)
+        dec.token_router = False
+        res["one_launch_ms_per_token"] = round(ms1, 4)
+    return res
 
 
 def cpu_sample(bank, layers_sampled=4, tokens=2):

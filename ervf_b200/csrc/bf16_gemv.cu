@@ -25,27 +25,6 @@ namespace {
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-// Reduce the 8 chain values of this lane (chains 8c+j) of one row to the
-// row sum, valid in lane 0.
-__device__ __forceinline__ float row_tree(float (&a)[8]) {
-  // chain offset 16 -> lane xor 2; offset 8 -> lane xor 1
-#pragma unroll
-  for (int j = 0; j < 8; ++j) a[j] += __shfl_xor_sync(0xffffffffu, a[j], 2);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) a[j] += __shfl_xor_sync(0xffffffffu, a[j], 1);
-  // offsets 4, 2, 1 inside the lane
-  const float2 l4a = add2(make_float2(a[0], a[1]), make_float2(a[4], a[5]));
-  const float2 l4b = add2(make_float2(a[2], a[3]), make_float2(a[6], a[7]));
-  const float2 l2 = add2(l4a, l4b);
-  float s = l2.x + l2.y;
-  // legacy combine: group sum + 0.0, then (w,w+4),(w,w+2),(w,w+1) = lanes xor 16, 8, 4
-  s = s + 0.0f;
-  s += __shfl_xor_sync(0xffffffffu, s, 16);
-  s += __shfl_xor_sync(0xffffffffu, s, 8);
-  s += __shfl_xor_sync(0xffffffffu, s, 4);
-  return s;
-}
-
 template <int B>
 __global__ void __launch_bounds__(256) bf16_gemv_kernel(const uint16_t* __restrict__ W,
                                                         const float* __restrict__ x,
@@ -97,38 +76,6 @@ __global__ void __launch_bounds__(256) bf16_gemv_kernel(const uint16_t* __restri
     const float s = row_tree(acc[b]);
     if (lane == 0) out[(size_t)b * rows + row] = s;
   }
-}
-
-// gemv_f32 (gpu_kernels.py:51-74): the same 256-chain walk, warp butterfly
-// and legacy combine as gemv_bf16 with fp32 weights.  One warp per row; lane
-// c owns chains 8c..8c+7 (two 128-bit loads per round).  Row sum in lane 0.
-__device__ __forceinline__ float f32_row(const float* __restrict__ wr, const float* __restrict__ x,
-                                         int cols, int lane) {
-  float acc[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-  const int nfull = cols >> 8;
-#pragma unroll 4
-  for (int i = 0; i < nfull; ++i) {
-    const int k = 256 * i + 8 * lane;
-    const float4 w0 = __ldcs(reinterpret_cast<const float4*>(wr + k));
-    const float4 w1 = __ldcs(reinterpret_cast<const float4*>(wr + k + 4));
-    const float4 x0 = __ldcg(reinterpret_cast<const float4*>(x + k));
-    const float4 x1 = __ldcg(reinterpret_cast<const float4*>(x + k + 4));
-    const float2 a01 = fma2(make_float2(w0.x, w0.y), make_float2(x0.x, x0.y), make_float2(acc[0], acc[1]));
-    const float2 a23 = fma2(make_float2(w0.z, w0.w), make_float2(x0.z, x0.w), make_float2(acc[2], acc[3]));
-    const float2 a45 = fma2(make_float2(w1.x, w1.y), make_float2(x1.x, x1.y), make_float2(acc[4], acc[5]));
-    const float2 a67 = fma2(make_float2(w1.z, w1.w), make_float2(x1.z, x1.w), make_float2(acc[6], acc[7]));
-    acc[0] = a01.x; acc[1] = a01.y; acc[2] = a23.x; acc[3] = a23.y;
-    acc[4] = a45.x; acc[5] = a45.y; acc[6] = a67.x; acc[7] = a67.y;
-  }
-  {
-    const int k = 256 * nfull + 8 * lane;
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (k + j < cols) acc[j] = fmaf(wr[k + j], __ldcg(x + k + j), acc[j]);
-  }
-  return row_tree(acc);
 }
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

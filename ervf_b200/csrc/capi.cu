@@ -362,6 +362,49 @@ int ervf_moe_token(const uint64_t* layer_ptrs, int n_layers, size_t up_code_stri
   return launch_moe_token(a, S(stream));
 }
 
+int ervf_moe_token_router(const uint64_t* layer_ptrs, int n_layers, size_t up_code_stride,
+                          size_t up_scale_stride, size_t dn_code_stride, size_t dn_scale_stride,
+                          int32_t* ids, float* route_w, int top_k, int n_experts, float scaling,
+                          int bad_pick, const float* x, float* out, int hidden, int inter, void* scratch,
+                          size_t scratch_bytes, int flags, void* stream) {
+  if (!layer_ptrs || !ids || !route_w || !x || !out || !scratch) return kErrNull;
+  if (flags & ~ERVF_LAUNCH_PDL) return kErrArg;
+  if (n_layers <= 0 || top_k <= 0 || top_k > kMaxJobs || n_experts <= 0 || n_experts > 256 ||
+      top_k > n_experts)
+    return kErrShape;
+  if (bad_pick != 0 && bad_pick != 1) return kErrArg;
+  if (hidden <= 0 || inter <= 0 || hidden % 32 || inter % 32 || hidden > 4096 || inter > 4096)
+    return kErrShape;
+  if (scratch_bytes < moe_token_scratch_bytes(n_layers, hidden, inter, top_k)) return kErrArg;
+  if (!al(scratch, 256) || !al(x, 16) || !al(out, 4) || !al(layer_ptrs, 8) || !al(ids, 4) ||
+      !al(route_w, 4) || ((up_code_stride | up_scale_stride | dn_code_stride | dn_scale_stride) & 15u))
+    return kErrAlign;
+  const size_t cb = (size_t)inter * hidden / 2, sb = (size_t)inter * hidden / 16;
+  if (up_code_stride < cb || up_scale_stride < sb || dn_code_stride < cb || dn_scale_stride < sb)
+    return kErrArg;
+  MoeTokenArgs a{};
+  a.layer_ptrs = reinterpret_cast<const unsigned long long*>(layer_ptrs);
+  a.up_code_stride = up_code_stride;
+  a.up_scale_stride = up_scale_stride;
+  a.dn_code_stride = dn_code_stride;
+  a.dn_scale_stride = dn_scale_stride;
+  a.ids = ids;
+  a.route_w = route_w;
+  a.x = x;
+  a.out = out;
+  a.n_layers = n_layers;
+  a.top_k = top_k;
+  a.n_experts = n_experts;
+  a.hidden = hidden;
+  a.inter = inter;
+  a.scratch = scratch;
+  a.pdl = (flags & ERVF_LAUNCH_PDL) != 0;
+  a.route = true;
+  a.scaling = scaling;
+  a.bad_pick = bad_pick;
+  return launch_moe_token(a, S(stream));
+}
+
 size_t ervf_moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top_k) {
   if (n_layers <= 0 || hidden <= 0 || inter <= 0 || top_k <= 0) return 0;
   return moe_token_scratch_bytes(n_layers, hidden, inter, top_k);

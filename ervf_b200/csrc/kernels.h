@@ -179,8 +179,9 @@ int read_mma_device_error(bool clear);
 int read_token_device_error(bool clear);
 
 // One decode token through every routed MoE layer in one launch
-// (moe_token.cu).  layer_ptrs: device array [5][n_layers] of up code, up
-// scale, down code, down scale and globals (f32 [E][2]) bases per layer.
+// (moe_token.cu).  layer_ptrs: device array [5][n_layers] (+2 rows with the
+// router) of up code, up scale, down code, down scale and globals (f32
+// [E][2]) bases per layer.
 struct MoeTokenArgs {
   const unsigned long long* layer_ptrs;
   size_t up_code_stride, up_scale_stride, dn_code_stride, dn_scale_stride;
@@ -191,6 +192,11 @@ struct MoeTokenArgs {
   int n_layers, top_k, n_experts, hidden, inter;
   void* scratch;         // moe_token_scratch_bytes, counters zero
   bool pdl;
+  // router on the device: layer_ptrs has two more rows (router weights
+  // f32 [E][hidden], router bias f32 [E] or 0); ids / route_w are outputs
+  bool route;
+  float scaling;
+  int bad_pick;
 };
 
 size_t moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top_k);

@@ -43,6 +43,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "route.cuh"
 #include "tma_core.cuh"
 
 namespace ervf {
@@ -61,7 +62,9 @@ constexpr int kYRingOff = 512;    // [kPubRing][32] row values handed to the pub
 constexpr int kTabOff = kYRingOff + kPubRing * 32 * 4;  // per-token routing table, then the chain buffer
 constexpr unsigned kFull = 0xffffffffu;
 
-enum : int { kItemPrep = 0, kItemUp = 1, kItemDown = 2, kItemEnd = 3 };
+enum : int { kItemPrep = 0, kItemUp = 1, kItemDown = 2, kItemEnd = 3, kItemRoute = 4 };
+constexpr int kRouteRows = kCW;  // router rows per item: one per consumer warp
+constexpr int kTokMaxRouteExperts = 256;  // experts a layer's router items can route
 
 // One projection: up (rows = inter, cols = hidden) or down (rows = hidden,
 // cols = inter).
@@ -70,10 +73,18 @@ struct TokPhase {
 };
 
 struct TokArgs {
-  const unsigned long long* layer_ptrs;  // [5][L]: up codes, up scales, dn codes, dn scales, globals
+  // [5][L]: up codes, up scales, dn codes, dn scales, globals; with the
+  // router two more rows: router weights f32 [E][hidden], router bias f32 [E]
+  // (0 = none)
+  const unsigned long long* layer_ptrs;
   size_t up_cs, up_ss, dn_cs, dn_ss;     // per-expert record strides
-  const int* ids;                        // [L][K]
+  const int* ids;                        // [L][K] (written by the router items when route)
   const float* route_w;                  // [L][K]
+  int route;                             // router items compute ids / route_w per layer
+  float scaling;
+  int bad_pick;
+  int n_route;                           // router items per layer
+  float* rlog;                           // [L][E] router logits (route)
   const float* x_in;                     // [hidden]
   float* out;                            // [hidden]
   int L, K, E, hidden, inter, G;         // G = 32-row groups of hidden
@@ -101,19 +112,32 @@ __device__ __forceinline__ unsigned* ctr_xrows(const TokArgs& a, int l) {
 __device__ __forceinline__ unsigned* ctr_act(const TokArgs& a, int l, int s) {
   return a.ctr + kCtrLine * (2 + a.L + l * a.K + s);
 }
+__device__ __forceinline__ unsigned* ctr_route_ready(const TokArgs& a, int l) {
+  return a.ctr + kCtrLine * (2 + a.L + a.L * a.K + l);
+}
+// router rows done per layer, then the route-sum groups: atomics only
+__host__ __device__ __forceinline__ size_t token_rows_base(int L, int K) {
+  return (size_t)kCtrLine * (2 + 2 * L + (size_t)L * K);
+}
+__host__ __device__ __forceinline__ size_t token_grp_base(int L, int K) {
+  return token_rows_base(L, K) + (size_t)(L + kCtrLine - 1) / kCtrLine * kCtrLine;
+}
+__device__ __forceinline__ unsigned* ctr_route_rows(const TokArgs& a, int l) {
+  return a.ctr + token_rows_base(a.L, a.K) + l;
+}
 __device__ __forceinline__ unsigned* ctr_grp(const TokArgs& a, int l, int g) {
-  return a.ctr + kCtrLine * (2 + a.L + a.L * a.K) + l * a.G + g;
+  return a.ctr + token_grp_base(a.L, a.K) + (size_t)l * a.G + g;
 }
 
 __host__ __device__ __forceinline__ size_t token_ctr_words(int L, int K, int G) {
-  return (size_t)kCtrLine * (2 + L + (size_t)L * K) + (size_t)L * G;
+  return token_grp_base(L, K) + (size_t)L * G;
 }
 
 // Shared routing table of the token, loaded once per CTA: record bases of
 // every layer (up codes, up scales, down codes, down scales), the clamped
 // expert id of every (layer, slot) and its (down, up) global scales -- the
 // producer then forms an item's addresses without a global-memory round trip.
-__host__ __device__ __forceinline__ int token_tab_bytes(int L, int K) { return 32 * L + 12 * L * K; }
+__host__ __device__ __forceinline__ int token_tab_bytes(int L, int K) { return 36 * L + 12 * L * K; }
 
 // Float index of column j in the swizzled unit layout that x_slot / the
 // consumers use: unit t = j / 32 holds 8 float4 slots, slot k =
@@ -135,6 +159,14 @@ __device__ __forceinline__ void decode_item(const TokArgs& a, int idx, int& kind
   const int i = idx - 1;
   l = i / a.per_layer;
   int j = i - l * a.per_layer;
+  if (j < a.n_route) {  // router rows kRouteRows * j .. (before the layer's up items)
+    kind = kItemRoute;
+    slot = 0;
+    r0 = kRouteRows * j;
+    nrows = min(kRouteRows, a.E - r0);
+    return;
+  }
+  j -= a.n_route;
   const int nu = a.K * a.up.n_items;
   const TokPhase* ph;
   if (j < nu) {
@@ -200,6 +232,21 @@ __device__ __forceinline__ bool wait_smem_gt(const int* p, int v) {
   return true;
 }
 
+// Router logit of one expert row (one warp; lane 0 holds it).  Kept out of
+// line so that the router's registers do not weigh on the expert paths.
+__device__ __noinline__ float router_row(const float* gw, const float* x, int cols, int lane) {
+  return f32_row(gw, x, cols, lane);
+}
+
+// route_topk_f32 of one layer on the calling (full) warp.
+__device__ __noinline__ void router_topk(const float* lg, const float* gb, int* io, float* wo, int n,
+                                         int top_k, float scaling, int bad_pick) {
+  if (n <= 128)
+    route_topk_warp<4>(lg, gb, io, wo, n, top_k, scaling, bad_pick);
+  else
+    route_topk_warp<8>(lg, gb, io, wo, n, top_k, scaling, bad_pick);
+}
+
 // Per-thread place in the consumer schedule of one projection (see the TMA
 // schedule in nvfp4_gemv.cu: teams of n_u threads, two segments per thread).
 struct SegPlace {
@@ -222,7 +269,9 @@ __device__ __forceinline__ SegPlace seg_place(const TokPhase& ph, int tid) {
   return s;
 }
 
-template <int H>
+// ROUTE: the launch has router items (ervf_moe_token_router); the plain
+// instantiation carries no router code at all.
+template <int H, bool ROUTE>
 __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_constant__ TokArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_last;
@@ -239,6 +288,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
   unsigned long long* tab_base = reinterpret_cast<unsigned long long*>(smem + kTabOff);  // [4][L]
   float2* tab_g = reinterpret_cast<float2*>(smem + kTabOff + 32 * a.L);                 // [L][K]
   int* tab_id = reinterpret_cast<int*>(smem + kTabOff + 32 * a.L + 8 * a.L * a.K);       // [L][K]
+  int* tab_ok = tab_id + a.L * a.K;  // [L]: the layer's (id, g) entries are filled
   uint8_t* stages = smem + a.stage_base;
 
   if (tid == 0) {
@@ -252,7 +302,8 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
   }
   grid_dep_wait();  // ids, route weights and x come from the predecessor
   for (int i = tid; i < 4 * a.L; i += kTokThreads) tab_base[i] = a.layer_ptrs[i];
-  for (int i = tid; i < a.L * a.K; i += kTokThreads) {
+  for (int i = tid; i < a.L; i += kTokThreads) tab_ok[i] = a.route ? 0 : 1;
+  for (int i = tid; i < (a.route ? 0 : a.L * a.K); i += kTokThreads) {
     int e = a.ids[i];
     e = e < 0 ? 0 : (e >= a.E ? a.E - 1 : e);  // a stale id cannot leave the bank
     const float* gl = reinterpret_cast<const float*>(a.layer_ptrs[4 * a.L + i / a.K]);
@@ -281,6 +332,29 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
       int kind, l, slot, r0, nrows;
       decode_item(a, idx, kind, l, slot, r0, nrows);
       int* hdr = reinterpret_cast<int*>(sp);
+      if (ROUTE && kind == kItemRoute) {
+        // router rows: no weights to stage (the consumer warps read them
+        // directly); the stage completes once x_l is complete
+        bool okx = true;
+        if (lane == 0) {
+          reinterpret_cast<int4*>(hdr)[0] = make_int4(kind, l, slot, r0);
+          hdr[4] = nrows;
+          // the item's router rows do not depend on x: queue them into L2
+          // now, so that the warps read them from L2 once x_l is complete
+          const uint8_t* gw = reinterpret_cast<const uint8_t*>(a.layer_ptrs[5 * a.L + l]) +
+                              (size_t)r0 * a.hidden * 4;
+          const uint32_t gbytes = (uint32_t)nrows * (uint32_t)a.hidden * 4u;
+          for (uint32_t off = 0; off < gbytes; off += 32768u)
+            l2_prefetch(gw + off, gbytes - off < 32768u ? gbytes - off : 32768u);
+          okx = wait_count(ctr_xrows(a, l), (unsigned)a.hidden);
+          mbar_arrive(&full[st]);
+          next = (int)atomicAdd(ctr_claim(a), 1u);
+        }
+        ok = __shfl_sync(kFull, okx, 0);
+        ++it;
+        if (!ok) break;
+        continue;
+      }
       if (kind == kItemPrep) {
         if (lane == 0) {
           hdr[0] = kind;
@@ -289,6 +363,25 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
         }
         ++it;
         continue;
+      }
+      if (ROUTE && !tab_ok[l]) {
+        // routed on the device: this layer's ids exist once its router
+        // items are published
+        bool okr = true;
+        if (lane == 0) okr = wait_count(ctr_route_ready(a, l), 1u);
+        __syncwarp();
+        if (lane < a.K) {
+          int e = __ldcg(a.ids + l * a.K + lane);
+          e = e < 0 ? 0 : (e >= a.E ? a.E - 1 : e);
+          const float* gl = reinterpret_cast<const float*>(a.layer_ptrs[4 * a.L + l]);
+          tab_id[l * a.K + lane] = e;
+          tab_g[l * a.K + lane] = make_float2(gl[2 * e], gl[2 * e + 1]);
+        }
+        __syncwarp();
+        if (lane == 0) tab_ok[l] = 1;
+        __syncwarp();
+        ok = __shfl_sync(kFull, okr, 0);
+        if (!ok) break;
       }
       const bool up = kind == kItemUp;
       const TokPhase& ph = up ? a.up : a.dn;
@@ -331,7 +424,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
           // its weight rows stream from HBM into L2 while this item waits
           int k2, l2, s2, q0, n2;
           decode_item(a, next, k2, l2, s2, q0, n2);
-          if (k2 != kItemPrep) {
+          if ((k2 == kItemUp || k2 == kItemDown) && (!ROUTE || tab_ok[l2])) {
             const bool up2 = k2 == kItemUp;
             const TokPhase& p2 = up2 ? a.up : a.dn;
             const int e2 = tab_id[l2 * a.K + s2];
@@ -389,6 +482,24 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
       const float y = lane < nrows ? yv[lane] : 0.0f;
       if (kind == kItemPrep) {
         if (lane == 0) red_release_gpu(ctr_xrows(a, 0), (unsigned)a.hidden);  // stores fenced by the consumers
+      } else if (ROUTE && kind == kItemRoute) {
+        // router logits; the item that completes the layer routes it (the
+        // reference's route_topk_f32 on one warp) and releases the layer's ids
+        float* lg = a.rlog + (size_t)l * a.E;
+        if (lane < nrows) lg[r0 + lane] = y;
+        __syncwarp();
+        unsigned last = 0;
+        if (lane == 0) last = atom_add_acq_rel_gpu(ctr_route_rows(a, l), (unsigned)nrows) + nrows == (unsigned)a.E;
+        last = __shfl_sync(kFull, last, 0);
+        if (last) {
+          __syncwarp();
+          const float* gb = reinterpret_cast<const float*>(a.layer_ptrs[6 * a.L + l]);
+          int* io = const_cast<int*>(a.ids) + l * a.K;
+          float* wo = const_cast<float*>(a.route_w) + l * a.K;
+          router_topk(lg, gb, io, wo, a.E, a.K, a.scaling, a.bad_pick);
+          __syncwarp();
+          if (lane == 0) red_release_gpu(ctr_route_ready(a, l), 1u);
+        }
       } else if (kind == kItemUp) {
         if (lane < nrows) {
           const float v = fmaxf(y, 0.0f);
@@ -420,7 +531,8 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
             const float* cb = a.contrib + (size_t)(l & 1) * a.K * a.hidden;
             float acc = 0.0f;
             for (int s2 = 0; s2 < a.K; ++s2)
-              acc = fmaf(__ldcg(cb + (size_t)s2 * a.hidden + r), a.route_w[l * a.K + s2], acc);
+              acc = fmaf(__ldcg(cb + (size_t)s2 * a.hidden + r),
+                         ROUTE ? __ldcg(a.route_w + l * a.K + s2) : a.route_w[l * a.K + s2], acc);
             const float xv = __ldcg(a.xlin + (size_t)l * a.hidden + r) + acc;
             if (l + 1 < a.L) {
               a.xlin[(size_t)(l + 1) * a.hidden + r] = xv;
@@ -451,7 +563,18 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
       const int* hdr = reinterpret_cast<const int*>(sp);
       const int kind = to ? kItemEnd : hdr[0];
       int l = 0, slot = 0, r0 = 0, nrows = 0;
-      if (kind == kItemPrep) {
+      float route_v = 0.0f;  // kItemRoute: this warp's router logit (lane 0)
+      if (ROUTE && kind == kItemRoute) {
+        l = hdr[1];
+        r0 = hdr[3];
+        nrows = hdr[4];
+        const int w = tid >> 5;
+        if (w < nrows) {
+          const float* gw = reinterpret_cast<const float*>(a.layer_ptrs[5 * a.L + l]) +
+                            (size_t)(r0 + w) * a.hidden;
+          route_v = router_row(gw, a.xlin + (size_t)l * a.hidden, a.hidden, tid & 31);
+        }
+      } else if (kind == kItemPrep) {
         const int nu = a.hidden >> 5;
         float4* xs0 = reinterpret_cast<float4*>(a.xsw);
         for (int f = tid; f < nu * 8; f += kCT) {
@@ -504,7 +627,9 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
       const bool stop = named_bar_or(kBarC, kCT, to || ring_fail);
       if (tid == 0 && !stop && kind != kItemEnd) mbar_arrive(&empty[st]);
       if (stop || kind == kItemEnd) break;
-      if (kind != kItemPrep) {
+      if (ROUTE && kind == kItemRoute) {
+        if ((tid & 31) == 0 && (tid >> 5) < nrows) yring[(it % kPubRing) * 32 + (tid >> 5)] = route_v;
+      } else if (kind != kItemPrep) {
         float y = 0.0f;
         if (tr < nrows) y = group_tree(part + tr * kRowPitch + tw * kGroupPitch);
         y = combine8(y);
@@ -575,13 +700,13 @@ int set_smem_tok(K kernel, int bytes) {
   return kOk;
 }
 
-template <int H>
+template <int H, bool ROUTE>
 int launch_token_h(const TokArgs& a, int smem, bool pdl, cudaStream_t stream) {
-  if (set_smem_tok(moe_token_kernel<H>, smem)) return kErrLaunch;
+  if (set_smem_tok(moe_token_kernel<H, ROUTE>, smem)) return kErrLaunch;
   int dev = 0, sms = 0, occ = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, moe_token_kernel<H>, kTokThreads, smem) !=
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, moe_token_kernel<H, ROUTE>, kTokThreads, smem) !=
       cudaSuccess)
     return kErrLaunch;
   if (occ < 1) return kErrShape;
@@ -596,7 +721,7 @@ int launch_token_h(const TokArgs& a, int smem, bool pdl, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, moe_token_kernel<H>, a) == cudaSuccess ? kOk : kErrLaunch;
+  return cudaLaunchKernelEx(&cfg, moe_token_kernel<H, ROUTE>, a) == cudaSuccess ? kOk : kErrLaunch;
 }
 
 }  // namespace
@@ -604,7 +729,8 @@ int launch_token_h(const TokArgs& a, int smem, bool pdl, cudaStream_t stream) {
 size_t moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top_k) {
   const size_t n_ctr = token_ctr_words(n_layers, top_k, (hidden + 31) / 32);
   const size_t ctr = (n_ctr * 4 + 255) / 256 * 256;
-  return ctr + 4 * ((size_t)2 * n_layers * hidden + (size_t)2 * top_k * inter + (size_t)2 * top_k * hidden);
+  return ctr + 4 * ((size_t)2 * n_layers * hidden + (size_t)2 * top_k * inter + (size_t)2 * top_k * hidden +
+                    (size_t)n_layers * kTokMaxRouteExperts);
 }
 
 int launch_moe_token(const MoeTokenArgs& in, cudaStream_t stream) {
@@ -616,6 +742,10 @@ int launch_moe_token(const MoeTokenArgs& in, cudaStream_t stream) {
   a.dn_ss = in.dn_scale_stride;
   a.ids = in.ids;
   a.route_w = in.route_w;
+  a.route = in.route ? 1 : 0;
+  a.scaling = in.scaling;
+  a.bad_pick = in.bad_pick;
+  if (a.route && in.n_experts > kTokMaxRouteExperts) return kErrShape;
   a.x_in = in.x;
   a.out = in.out;
   a.L = in.n_layers;
@@ -672,7 +802,8 @@ int launch_moe_token(const MoeTokenArgs& in, cudaStream_t stream) {
   a.dn.scale_off = a.dn.krt * a.dn.cb;
   a.up.n_items = (a.up.rows + a.up.krt - 1) / a.up.krt;
   a.dn.n_items = (a.dn.rows + a.dn.krt - 1) / a.dn.krt;
-  a.per_layer = a.K * (a.up.n_items + a.dn.n_items);
+  a.n_route = a.route ? (a.E + kRouteRows - 1) / kRouteRows : 0;
+  a.per_layer = a.n_route + a.K * (a.up.n_items + a.dn.n_items);
   a.total = 1 + a.L * a.per_layer;
 
   uint8_t* s = reinterpret_cast<uint8_t*>(in.scratch);
@@ -686,12 +817,22 @@ int launch_moe_token(const MoeTokenArgs& in, cudaStream_t stream) {
   a.actsw = reinterpret_cast<float*>(s);
   s += (size_t)4 * 2 * a.K * a.inter;
   a.contrib = reinterpret_cast<float*>(s);
+  s += (size_t)4 * 2 * a.K * a.hidden;
+  a.rlog = reinterpret_cast<float*>(s);
 
+  if (a.route) {
+    switch (h) {
+      case 4: return launch_token_h<4, true>(a, smem, in.pdl, stream);
+      case 3: return launch_token_h<3, true>(a, smem, in.pdl, stream);
+      case 2: return launch_token_h<2, true>(a, smem, in.pdl, stream);
+      default: return launch_token_h<1, true>(a, smem, in.pdl, stream);
+    }
+  }
   switch (h) {
-    case 4: return launch_token_h<4>(a, smem, in.pdl, stream);
-    case 3: return launch_token_h<3>(a, smem, in.pdl, stream);
-    case 2: return launch_token_h<2>(a, smem, in.pdl, stream);
-    default: return launch_token_h<1>(a, smem, in.pdl, stream);
+    case 4: return launch_token_h<4, false>(a, smem, in.pdl, stream);
+    case 3: return launch_token_h<3, false>(a, smem, in.pdl, stream);
+    case 2: return launch_token_h<2, false>(a, smem, in.pdl, stream);
+    default: return launch_token_h<1, false>(a, smem, in.pdl, stream);
   }
 }
 

@@ -59,16 +59,24 @@ constexpr int kMmaThreads = kMmaWarps * 32;
 constexpr int kM = 128;               // rows per unit (UMMA M)
 constexpr int kN = 16;                // batch columns (UMMA N)
 constexpr int kKB = 256;              // columns per k-block
-constexpr int kStages = 4;            // smem ring depth
+#ifndef ERVF_MMA_STAGES
+#define ERVF_MMA_STAGES 4
+#endif
+constexpr int kStages = ERVF_MMA_STAGES;  // smem ring depth
 constexpr int kAStages = 3;           // tensor-memory A stages
 constexpr int kCodeTile = kM * kKB / 2;       // 16 KB
 constexpr int kBTile = kN * kKB * 2;          // 8 KB
 constexpr int kStageBytes = kCodeTile + kBTile;
 constexpr int kScaleBuf = kM * 256;           // scale rows of a tile, cols <= 4096
 constexpr int kTmemCols = 512;
-constexpr int kDCol = 0;                      // accumulators: columns 0..15, 16..31
-constexpr int kACol = 64;                     // A stages: 64 + 128 a
+// Accumulators: kDAcc independent chains per buffer (the 16 MMAs of a
+// k-block go round-robin over them, so that consecutive MMAs do not wait on
+// each other's result), two buffers: columns (d * kDAcc + c) * 16 .. + 15.
+constexpr int kDAcc = 4;
+constexpr int kDCol = 0;
+constexpr int kACol = 2 * kDAcc * kN;          // A stages: 128 + 128 a
 constexpr int kAStageCols = kKB / 2;          // 128 (two f16 per 32-bit column)
+static_assert(kACol + kAStages * kAStageCols <= kTmemCols, "tensor-memory columns");
 constexpr int kDecodeWarp0 = 2, kEpiWarp0 = 10;
 
 // shared memory: [0, 1024) barriers and slots, then the ring (1024-aligned
@@ -113,6 +121,15 @@ struct MmaArgs {
   unsigned* ucnt;
   int part_cols;
 };
+
+// 16 consecutive 32-bit tensor-memory columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+}
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
@@ -338,11 +355,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
 #pragma unroll
           for (int j = 0; j < kKB / 16; ++j) {
             const uint64_t db = umma_desc(b0 + 256 * j, 128, 4096);
-            const uint32_t acc = (kb > un.kb0 || j > 0) ? 1u : 0u;
+            const uint32_t acc = (kb > un.kb0 || j >= kDAcc) ? 1u : 0u;
             asm volatile(
                 "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                 " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
-                ::"r"(tmem + kDCol + 16 * d), "r"(tmem + kACol + as * kAStageCols + 8 * j), "l"(db),
+                ::"r"(tmem + kDCol + (d * kDAcc + (j % kDAcc)) * kN),
+                  "r"(tmem + kACol + as * kAStageCols + 8 * j), "l"(db),
                   "r"(kIdesc), "r"(acc) : "memory");
           }
           umma_commit(&empty[s]);
@@ -438,14 +456,19 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       const bool w_ok = wait_or_dead(&dfull[d], (nu >> 1) & 1, dead);
       if (named_bar_or(2, 128, !w_ok)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      uint32_t v[16];
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-            "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-            "=r"(v[14]), "=r"(v[15])
-          : "r"(tmem + ((uint32_t)(32 * q) << 16) + kDCol + 16 * d));
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      // the kDAcc chains of buffer d, added ((c0 + c1) + (c2 + c3))
+      float y[16];
+      {
+        uint32_t v[kDAcc][16];
+#pragma unroll
+        for (int c = 0; c < kDAcc; ++c)
+          tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + kDCol + (d * kDAcc + c) * kN, v[c]);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          y[j] = (__uint_as_float(v[0][j]) + __uint_as_float(v[1][j])) +
+                 (__uint_as_float(v[2][j]) + __uint_as_float(v[3][j]));
+      }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&dempty[d]);  // the accumulator may be rewritten
@@ -453,9 +476,6 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       const int row = un.tile * kM + r;
       const bool row_ok = row < a.rows;
       const float g = a.mode == kSingle ? a.g : __ldg(&a.globals[unit_expert(a, un) * 2 + a.gsel]);
-      float y[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) y[j] = __uint_as_float(v[j]);
       if (a.splits > 1) {
         // partial of this split; the last split of the unit adds them in split order
         const int ct = un.chunk * a.tiles + un.tile;

@@ -184,6 +184,27 @@ ERVF_API int ervf_moe_token(const uint64_t* layer_ptrs, int n_layers, size_t up_
                             const float* x, float* out, int hidden, int inter, void* scratch,
                             size_t scratch_bytes, int flags, void* stream);
 
+/* ervf_moe_token with the router on the device: before each layer's experts,
+ * router items compute rlog = gemv_f32(gate_w[l], x_l) (the reference's
+ * mv_f32, gpu_kernels.py:51-74, one warp per expert) and the item that
+ * completes the layer routes it with route_topk_f32 (fused_nvfp4.py:433-465;
+ * sigmoid + bias, ties to the lowest index, scaling, bad_pick) into
+ * ids[l] / route_w[l]; the layer's expert items wait for those ids before
+ * streaming their weights.  Bit-identical to ervf_route_gemv_topk followed
+ * by ervf_moe_layer, layer after layer (the reference's per-layer mv_f32 +
+ * route_topk + experts, runtime.py:705-746).  layer_ptrs: 7 * n_layers
+ * addresses: the five rows of ervf_moe_token, then [5L, 6L) router weights
+ * f32[n_experts][hidden] and [6L, 7L) router bias f32[n_experts] (0 = no
+ * bias) of each layer.  ids int32[L][top_k], route_w f32[L][top_k]: outputs.
+ * n_experts <= 256, top_k <= min(16, n_experts), bad_pick 0 or 1; scratch
+ * and the other arguments as for ervf_moe_token. */
+ERVF_API int ervf_moe_token_router(const uint64_t* layer_ptrs, int n_layers, size_t up_code_stride,
+                                   size_t up_scale_stride, size_t dn_code_stride,
+                                   size_t dn_scale_stride, int32_t* ids, float* route_w, int top_k,
+                                   int n_experts, float scaling, int bad_pick, const float* x,
+                                   float* out, int hidden, int inter, void* scratch,
+                                   size_t scratch_bytes, int flags, void* stream);
+
 /* Bytes of scratch ervf_moe_token uses (counters and per-layer activations). */
 ERVF_API size_t ervf_moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top_k);
 

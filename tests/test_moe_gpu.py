@@ -197,7 +197,9 @@ def test_decoder_step_with_router_matches_oracle(fused, oracle, bank, cuda):
         assert np.array_equal(ids, oid)
         experts = {e: (*bank["ups"][(e + l) % E], *bank["dns"][(e + 2 * l) % E]) for e in range(E)}
         want = (want + oracle.moe_block(want, experts, ids, w, HIDDEN, INTER)).astype(np.float32)
-    for use_graph in (False, True):
+    # one launch for every router and expert (token), or the per-layer launches
+    for token, use_graph in ((True, False), (True, True), (False, False), (False, True)):
+        dec.token = dec.token_router = token
         dec.xbuf.fill_(float("nan"))
         if use_graph:
             g = torch.cuda.CUDAGraph()
@@ -212,7 +214,38 @@ def test_decoder_step_with_router_matches_oracle(fused, oracle, bank, cuda):
         else:
             y = dec.step_with_router(xd, gwd, gbd)
         torch.cuda.synchronize()
-        assert bits_equal(y.cpu().numpy(), want), use_graph
+        assert bits_equal(y.cpu().numpy(), want), (token, use_graph)
+
+
+@pytest.mark.parametrize("E,with_bias", [(128, True), (256, False), (44, True)])
+def test_token_router_equals_layer_router(fused, cuda, E, with_bias):
+    """The routed token launch (router items inside ervf_moe_token_router)
+    gives the same ids, weights and output bits as the per-layer router +
+    expert launches, for three tokens back to back."""
+    from ervf_b200.moe import ExpertBank, MoEDecoder
+
+    L, k = 3, 6
+    eb = ExpertBank.synthetic(L, E, HIDDEN, INTER, cuda, seed=11)
+    dec = MoEDecoder(eb, k, scaling=2.5)
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(31)
+    gw = torch.randn(L, E, HIDDEN, generator=gen, device=cuda) * 0.05
+    gb = torch.randn(L, E, generator=gen, device=cuda) * 0.1 if with_bias else None
+    for t in range(3):
+        x = torch.randn(HIDDEN, generator=gen, device=cuda) * 0.05
+        dec.token = dec.token_router = True
+        y_tok = dec.step_with_router(x, gw, gb).clone()
+        ids_tok, w_tok = dec.ids.clone(), dec.w.clone()
+        dec.token = dec.token_router = False
+        y_ref = dec.step_with_router(x, gw, gb).clone()
+        torch.cuda.synchronize()
+        assert torch.equal(ids_tok, dec.ids), t
+        assert bits_equal(w_tok.cpu().numpy(), dec.w.cpu().numpy()), t
+        assert np.isfinite(y_ref.cpu().numpy()).all()
+        assert bits_equal(y_tok.cpu().numpy(), y_ref.cpu().numpy()), t
+    from ervf_b200 import _lib
+
+    assert _lib.load().ervf_device_status() == 0
 
 
 def test_routesum_residual_matches_f64(fused, oracle, bank, cuda):
