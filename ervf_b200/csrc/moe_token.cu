@@ -28,15 +28,19 @@
 //   consumers reduce the item's rows (chains -> shared chain buffer -> tree)
 //             and hand the row values to the publisher through shared memory.
 //   publisher stores them -- UP rows as relu^2 into the slot's swizzled act
-//             buffer, DOWN rows into contrib[slot][row] -- each lane fencing
-//             its own stores (a bulk copy on another SM reads them next), then
-//             makes the item visible: UP adds its rows to the slot's act
-//             counter (release); DOWN adds its rows to the 32-row groups it
+//             buffer, DOWN rows into contrib[slot][row], one row per lane --
+//             and after a warp barrier lane 0's release (cumulative over
+//             the lanes' stores) makes the item visible: UP adds its rows to
+//             the slot's act counter (release); DOWN adds its rows to the 32-row groups it
 //             touches (acq_rel); the add that completes a group makes the
 //             warp sum the group in ROUTE order, acc = fmaf(y_s, w_s, acc)
 //             from 0, x_{l+1} = x_l + acc (the per-layer path's arithmetic),
 //             writes x_{l+1} (linear and swizzled, or `out` after the last
 //             layer) and adds the group's rows to the x counter of layer l+1.
+// With the router on the device (ROUTE instantiation) each layer starts with
+// router items: one consumer warp per expert row computes the reference's
+// gemv_f32 row, the item that completes the layer runs route_topk_f32 and
+// releases the layer's ids; expert items of that layer wait for them.
 // The last CTA to leave zeroes every counter, so the scratch is ready for
 // the next token (also after a timeout, once all CTAs have left).
 #include <stdlib.h>
