@@ -56,3 +56,24 @@ def test_null_and_shape_checks_need_no_device():
 def test_python_shim_raises_value_error():
     with pytest.raises(ValueError):
         _lib.call("ervf_nvfp4_gemv", None, None, None, None, 1.0, 8, 16, 0, 1.0, 0, 0, None)
+
+
+def test_token_entries_check_arguments_without_a_device():
+    lib = _lib.load()
+    nb = lib.ervf_moe_token_scratch_bytes(24, 2688, 1856, 6)
+    assert nb > 0 and lib.ervf_moe_token_scratch_bytes(0, 2688, 1856, 6) == 0
+    buf = ctypes.create_string_buffer(4096)
+    p = ctypes.addressof(buf)
+    args = (p, 24, 2688 * 1856 // 2, 2688 * 1856 // 16, 2688 * 1856 // 2, 2688 * 1856 // 16, p, p, 6, 128,
+            p, p, 2688, 1856, p)
+    assert lib.ervf_moe_token(None, *args[1:], nb, 0, None) == _lib.ERR_NULL
+    bad_shape = list(args)
+    bad_shape[12] = 100  # hidden not a multiple of 32
+    assert lib.ervf_moe_token(*bad_shape, nb, 0, None) == _lib.ERR_SHAPE
+    assert lib.ervf_moe_token(*args, nb - 1, 0, None) == _lib.ERR_ARG  # scratch too small
+    assert lib.ervf_moe_token(*args, nb, 0x40, None) == _lib.ERR_ARG   # unknown flag
+    r = (p, 24, 2688 * 1856 // 2, 2688 * 1856 // 16, 2688 * 1856 // 2, 2688 * 1856 // 16, p, p, 6)
+    tail = (p, p, 2688, 1856, p, nb, 0, None)
+    assert lib.ervf_moe_token_router(*r, 512, 1.0, 0, *tail) == _lib.ERR_SHAPE   # > 256 experts
+    assert lib.ervf_moe_token_router(*r, 128, 1.0, 2, *tail) == _lib.ERR_ARG     # bad_pick
+    assert lib.ervf_moe_token_router(*r, 4, 1.0, 0, *tail) == _lib.ERR_SHAPE     # top_k > experts
