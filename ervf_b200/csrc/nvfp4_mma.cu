@@ -11,7 +11,7 @@
 // significant bits, E4M3 four: a 6-bit product in 2^-10 .. 2688), X is
 // rounded to f16, the global scale g is applied to the fp32 accumulator.
 //
-// One CTA per SM, 14 warps, persistent over work units: 128 weight rows x one
+// One CTA per SM, 17 warps, persistent over work units: 128 weight rows x one
 // K range (grouped mode: unit = (expert chunk, 128-row tile, K range)).  The
 // K range walks k-blocks of 256 columns through a ring of shared-memory
 // stages and tensor-memory A stages:
@@ -25,22 +25,25 @@
 //                      K-major core-matrix layout, 8 KB, prepared once per
 //                      call by pack_panel_kernel) into ring stage s.  This
 //                      GPU's own memory only; no multicast anywhere.
-//   warps 2..9         decoders.  Warp w owns tensor-memory lanes 32 (w % 4)
-//                      .. +31 (= tile rows) and half (w - 2) / 4 of the
+//   warps 1..4, lane 0 MMA.  Issuer c issues MMAs c, c+4, c+8, c+12 of the
+//                      16 tcgen05.mma.cta_group::1.kind::f16 of a k-block
+//                      (M128 N16 K16, A from tensor memory, B from the
+//                      stage) into its own fp32 accumulator chain c of
+//                      buffer d; each issuer's tcgen05.commit counts once on
+//                      the barriers that free the smem stage and the A stage,
+//                      and, after the unit's last k-block, fill buffer d.
+//   warps 5..12        decoders.  Warp w owns tensor-memory lanes 32 (w % 4)
+//                      .. +31 (= tile rows) and half (w - 5) / 4 of the
 //                      k-block's 256 columns: codes from the swizzled tile,
 //                      e2m1 pairs -> f16x2 (hardware converter) times the
 //                      f16x2 block scale, tcgen05.st into A stage a.
-//   warp 1, one lane   MMA.  16 x tcgen05.mma.cta_group::1.kind::f16 per
-//                      k-block (M128 N16 K16, A from tensor memory, B from
-//                      the stage, fp32 accumulator in tensor memory buffer
-//                      d); tcgen05.commit frees the smem stage and the A
-//                      stage, the unit's last commit fills buffer d.
-//   warps 10..13       epilogue.  tcgen05.ld of buffer d (warp w: lanes
-//                      32 (w % 4) ..), times g, then the mode's store, and
-//                      frees d.  With a K split, each split stores its fp32
-//                      partial; the last split of a unit (counter) adds them
-//                      in split order -- deterministic, the same bits
-//                      whatever the arrival order or the grid.
+//   warps 13..16       epilogue.  tcgen05.ld of the four chains of buffer d
+//                      (warp w: lanes 32 (w % 4) ..), added in a fixed order,
+//                      times g, then the mode's store, and frees d.  With a
+//                      K split, each split stores its fp32 partial; the last
+//                      split of a unit (counter) adds them in split order --
+//                      deterministic, the same bits whatever the arrival
+//                      order or the grid.
 //
 // Every wait is bounded (%clock64); a wait that runs out records
 // kErrTimeout, marks the CTA dead, and every role drains: no copy or MMA is
@@ -54,7 +57,12 @@ namespace ervf {
 
 namespace {
 
-constexpr int kMmaWarps = 14;
+// MMA issue: one tcgen05.mma takes its issuing thread ~95 cycles whatever the
+// shape (measured on B200 for M128 / M64 x N16..N128), while issuers in
+// different warps overlap (4 issuers: ~30 cycles per MMA in aggregate).  So
+// kMmaIssuers warps issue a k-block's MMAs, each its own accumulator chain.
+constexpr int kMmaIssuers = 4;
+constexpr int kMmaWarps = 1 + kMmaIssuers + 8 + 4;
 constexpr int kMmaThreads = kMmaWarps * 32;
 constexpr int kM = 128;               // rows per unit (UMMA M)
 constexpr int kN = 16;                // batch columns (UMMA N)
@@ -73,11 +81,12 @@ constexpr int kTmemCols = 512;
 // k-block go round-robin over them, so that consecutive MMAs do not wait on
 // each other's result), two buffers: columns (d * kDAcc + c) * 16 .. + 15.
 constexpr int kDAcc = 4;
+static_assert(kMmaIssuers == kDAcc, "one accumulator chain per MMA issuer");
 constexpr int kDCol = 0;
 constexpr int kACol = 2 * kDAcc * kN;          // A stages: 128 + 128 a
 constexpr int kAStageCols = kKB / 2;          // 128 (two f16 per 32-bit column)
 static_assert(kACol + kAStages * kAStageCols <= kTmemCols, "tensor-memory columns");
-constexpr int kDecodeWarp0 = 2, kEpiWarp0 = 10;
+constexpr int kDecodeWarp0 = 1 + kMmaIssuers, kEpiWarp0 = kDecodeWarp0 + 8;
 
 // shared memory: [0, 1024) barriers and slots, then the ring (1024-aligned
 // stages: the 128-byte swizzle repeats every 1024 bytes), then two scale buffers
@@ -263,19 +272,19 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
+      mbar_init(&empty[i], kMmaIssuers);
     }
     for (int i = 0; i < kAStages; ++i) {
       mbar_init(&afull[i], 8);
-      mbar_init(&aempty[i], 1);
+      mbar_init(&aempty[i], kMmaIssuers);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&dfull[i], 1);
+      mbar_init(&dfull[i], kMmaIssuers);
       mbar_init(&dempty[i], 4);
       mbar_init(&sfull[i], 1);
       mbar_init(&sempty[i], 8);
     }
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, kMmaIssuers);
     *dead = 0;
     fence_mbar_init();
   }
@@ -330,8 +339,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       for (uint32_t k = gk > (uint32_t)kStages ? gk - kStages : 0; k < gk; ++k)
         mbar_wait(&full[k % kStages], (k / kStages) & 1, 2000000000LL);
     }
-  } else if (warp == 1) {
-    // --------------------------------------------------------------- MMA
+  } else if (warp <= kMmaIssuers) {
+    // ----------------------------------------------------------- MMA issue
+    // issuer c = warp - 1: MMAs c, c + 4, ... of every k-block, accumulator
+    // chain c; every stage / buffer barrier counts one commit per issuer
+    const int c = warp - 1;
     if (lane == 0) {
       uint32_t gk = 0;
       int nu = 0;
@@ -353,13 +365,14 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t b0 = smem_u32(ring + s * kStageBytes + kCodeTile);
 #pragma unroll
-          for (int j = 0; j < kKB / 16; ++j) {
+          for (int jj = 0; jj < kKB / 16 / kMmaIssuers; ++jj) {
+            const int j = c + kMmaIssuers * jj;
             const uint64_t db = umma_desc(b0 + 256 * j, 128, 4096);
-            const uint32_t acc = (kb > un.kb0 || j >= kDAcc) ? 1u : 0u;
+            const uint32_t acc = (kb > un.kb0 || jj > 0) ? 1u : 0u;
             asm volatile(
                 "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                 " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
-                ::"r"(tmem + kDCol + (d * kDAcc + (j % kDAcc)) * kN),
+                ::"r"(tmem + kDCol + (d * kDAcc + c) * kN),
                   "r"(tmem + kACol + as * kAStageCols + 8 * j), "l"(db),
                   "r"(kIdesc), "r"(acc) : "memory");
           }
