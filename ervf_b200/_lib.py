@@ -60,7 +60,6 @@ SIGNATURES: dict[str, list] = {
     "ervf_moe_token": [_vp, _i, _sz, _sz, _sz, _sz, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _vp, _sz, _i,
                        _vp],
     "ervf_moe_token_scratch_bytes": [_i, _i, _i, _i],
-    "ervf_moe_token_scratch_init": [_vp, _sz, _i, _i, _i, _i, _vp],
     "ervf_moe_token_router": [_vp, _i, _sz, _sz, _sz, _sz, _vp, _vp, _i, _i, _f, _i, _vp, _vp, _i, _i,
                               _vp, _sz, _i, _vp],
     "ervf_moe_down_routesum_static": [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp,

@@ -410,17 +410,6 @@ size_t ervf_moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top
   return moe_token_scratch_bytes(n_layers, hidden, inter, top_k);
 }
 
-int ervf_moe_token_scratch_init(void* scratch, size_t scratch_bytes, int n_layers, int hidden, int inter,
-                                int top_k, void* stream) {
-  if (!scratch) return kErrNull;
-  if (n_layers <= 0 || top_k <= 0 || top_k > kMaxJobs || hidden <= 0 || inter <= 0 || hidden % 32 ||
-      inter % 32 || hidden > 4096 || inter > 4096)
-    return kErrShape;
-  if (scratch_bytes < moe_token_scratch_bytes(n_layers, hidden, inter, top_k)) return kErrArg;
-  if (!al(scratch, 256)) return kErrAlign;
-  return init_moe_token_scratch(scratch, n_layers, hidden, inter, top_k, S(stream));
-}
-
 size_t ervf_routesum_scratch_bytes(int hidden, int top_k) {
   if (hidden <= 0 || top_k <= 0) return 0;
   return routesum_scratch_bytes(hidden, top_k);

@@ -190,7 +190,7 @@ struct MoeTokenArgs {
   const float* x;        // [hidden]
   float* out;            // [hidden]
   int n_layers, top_k, n_experts, hidden, inter;
-  void* scratch;         // moe_token_scratch_bytes, set up by init_moe_token_scratch
+  void* scratch;         // moe_token_scratch_bytes, counters zero
   bool pdl;
   // router on the device: layer_ptrs has two more rows (router weights
   // f32 [E][hidden], router bias f32 [E] or 0); ids / route_w are outputs
@@ -200,9 +200,6 @@ struct MoeTokenArgs {
 };
 
 size_t moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top_k);
-// Counters zero, hand-off words unwritten (stream-ordered memsets).
-int init_moe_token_scratch(void* scratch, int n_layers, int hidden, int inter, int top_k,
-                           cudaStream_t stream);
 int launch_moe_token(const MoeTokenArgs& a, cudaStream_t stream);
 
 // Expert-parallel exchange over NVLink peer memory (ep_p2p.cu).  Region

@@ -8,56 +8,41 @@
 //   item 0                      PREP: x -> the layer-0 activation buffers
 //   per layer l, in order:      UP   items: slot-major, krt_u rows of up_e(x_l)
 //                               DOWN items: slot-major, krt_d rows of down_e(act)
-// An UP item needs x_l complete (every row of layer l-1's route sum
+// An UP item needs x_l complete (every row group of layer l-1's route sum
 // written); a DOWN item needs its slot's act complete (all UP items of that
-// slot); the DOWN items of the last slot also need the other slots' rows of
-// the same block.  Dependencies point only at items with a SMALLER index, and
-// every CTA runs its claimed items in claim order, so the unfinished item
-// with the smallest index always has its inputs ready and its CTA running
-// it: the token completes whatever the number of co-resident CTAs (no
-// grid-wide residency assumption).  Every wait is bounded and ends with
-// kErrTimeout.
-//
-// Hand-off without counters or fences: every word passed between CTAs (x_l,
-// act, the down rows) is written once per token as ~bits(value), so 0 means
-// "not written yet" (no value encodes to 0: the one float that would, the
-// NaN 0xFFFFFFFF, is stored as the canonical NaN, which arithmetic never
-// makes differently).  A reader polls the words themselves.  The buffers are
-// double-buffered by token parity (an epoch word the last CTA advances); each
-// launch first zeroes the other parity's words, which the previous launch
-// used, so the next launch finds them unwritten.  A release/acquire pair per
-// hand-off would wait for the writer's stores to be acknowledged while the
-// weight streams load L2 (~2.5 us a layer, measured).
+// slot).  Dependencies point only at items with a SMALLER index, and every
+// CTA runs its claimed items in claim order, so the unfinished item with the
+// smallest index always has its inputs ready and its CTA running it: the
+// token completes whatever the number of co-resident CTAs (no grid-wide
+// residency assumption).  Every wait is bounded and ends with kErrTimeout.
 //
 // CTA = 8 consumer warps (the exact ERVF chain schedule of tma_core.cuh) +
 // one producer warp + one publisher warp, two CTAs per SM.
 //   producer  claims an item when a stage frees, writes the item header and
 //             the item's block-scale table RN(e4m3 * g) into the stage, bulk
 //             copies the weight rows (cp.async.bulk, no multicast) at once,
-//             then polls one word of every block its activation's writers
-//             store and bulk copies the activation (kept in global memory in
-//             the swizzled unit layout the consumers read, so no permutation
-//             pass) -- weights stream while the activation is still being
-//             produced elsewhere.
-//   consumers decode the activation copy in place (a word the copy read
-//             before its store landed is polled again from global memory),
-//             reduce the item's rows (chains -> shared chain buffer -> tree)
+//             then waits for the item's activation and bulk copies it (kept
+//             in global memory in the swizzled unit layout the consumers
+//             read, so no permutation pass) -- weights stream while the
+//             activation is still being produced elsewhere.
+//   consumers reduce the item's rows (chains -> shared chain buffer -> tree)
 //             and hand the row values to the publisher through shared memory.
 //   publisher stores them -- UP rows as relu^2 into the slot's swizzled act
-//             buffer, DOWN rows of every slot but the last into
-//             contrib[slot][row], one row per lane.  A DOWN item of the last
-//             slot instead sums its rows in ROUTE order, acc = fmaf(y_s, w_s,
-//             acc) from 0 over the slots' rows (polled), x_{l+1} = x_l + acc
-//             (the per-layer path's arithmetic), and writes x_{l+1} (linear
-//             and swizzled, or `out` after the last layer).
+//             buffer, DOWN rows into contrib[slot][row], one row per lane --
+//             and after a warp barrier lane 0's release (cumulative over
+//             the lanes' stores) makes the item visible: UP adds its rows to
+//             the slot's act counter (release); DOWN adds its rows to the 32-row groups it
+//             touches (acq_rel); the add that completes a group makes the
+//             warp sum the group in ROUTE order, acc = fmaf(y_s, w_s, acc)
+//             from 0, x_{l+1} = x_l + acc (the per-layer path's arithmetic),
+//             writes x_{l+1} (linear and swizzled, or `out` after the last
+//             layer) and adds the group's rows to the x counter of layer l+1.
 // With the router on the device (ROUTE instantiation) each layer starts with
 // router items: one consumer warp per expert row computes the reference's
-// gemv_f32 row over the decoded copy of x_l, the item that completes the
-// layer runs route_topk_f32 and releases the layer's ids (release/acquire
-// counters); expert items of that layer wait for them.
-// The last CTA to leave zeroes every counter and advances the epoch, so the
-// scratch is ready for the next token (also after a timeout, once all CTAs
-// have left).
+// gemv_f32 row, the item that completes the layer runs route_topk_f32 and
+// releases the layer's ids; expert items of that layer wait for them.
+// The last CTA to leave zeroes every counter, so the scratch is ready for
+// the next token (also after a timeout, once all CTAs have left).
 #include <stdlib.h>
 
 #include "common.cuh"
@@ -77,17 +62,13 @@ constexpr int kTokMaxStages = 4;  // ring depth is chosen per launch (2..4)
 constexpr int kPubRing = 16;     // item descriptors between consumers and publisher
 constexpr int kLutOff = 64;      // stage: header [0, 64), block-scale table [64, 1088)
 constexpr int kXOff = kLutOff + 1024;
-constexpr int kPubFullOff = 384;  // [kPubRing] mbarriers: ring slot filled (pubq at 128 .. 384)
 constexpr int kYRingOff = 512;    // [kPubRing][32] row values handed to the publisher
 constexpr int kTabOff = kYRingOff + kPubRing * 32 * 4;  // per-token routing table, then the chain buffer
-static_assert(128 + 16 * kPubRing <= kPubFullOff && kPubFullOff + 8 * kPubRing <= kYRingOff,
-              "publisher ring layout");
 constexpr unsigned kFull = 0xffffffffu;
 
 enum : int { kItemPrep = 0, kItemUp = 1, kItemDown = 2, kItemEnd = 3, kItemRoute = 4 };
 constexpr int kRouteRows = kCW;  // router rows per item: one per consumer warp
 constexpr int kTokMaxRouteExperts = 256;  // experts a layer's router items can route
-constexpr int kTokMaxK = 16;              // route slots per layer
 
 // One projection: up (rows = inter, cols = hidden) or down (rows = hidden,
 // cols = inter).
@@ -110,92 +91,50 @@ struct TokArgs {
   float* rlog;                           // [L][E] router logits (route)
   const float* x_in;                     // [hidden]
   float* out;                            // [hidden]
-  int L, K, E, hidden, inter;
+  int L, K, E, hidden, inter, G;         // G = 32-row groups of hidden
   TokPhase up, dn;
   int per_layer, total;
   int stages, stage_bytes, codes_off, stage_base, part_off;
   int prefetch;  // queue the next claimed item's weight rows into L2
-  unsigned* ctr;                         // claim, exited, epoch, xrows[L], act[L][K], route_ready[L], route_rows[L]
+  unsigned* ctr;                         // claim, exited, xrows[L], actrows[L][K], grp[L][G]
   int n_ctr;
-  // Hand-off words, [2] token parities of hand_words each, laid out per
-  // parity as xlin [L][hidden] (x_l; x_0 = the input), xsw [L][hidden] (x_l
-  // in the swizzled unit layout), act [L][K][inter] (relu^2(up) per slot,
-  // swizzled), contrib [L][K][hidden] (down rows per slot).  Stored ~bits.
-  uint32_t* hand;
-  size_t hand_words;
+  float* xlin;     // [L][hidden]  x_l (x_0 = the input)
+  float* xsw;      // [L][hidden]  x_l in the swizzled unit layout
+  float* actsw;    // [2][K][inter] relu^2(up) per slot, swizzled
+  float* contrib;  // [2][K][hidden] down rows per slot
 };
 
-// Counter words.  The claim counter (hit by every claim), the exit counter,
-// the epoch and every counter that producers poll sit on their own 128-byte
-// line, so that polling does not slow the atomics on a neighbour.
+// Counter words.  The claim counter (hit by every claim), the exit counter
+// and every counter that producers poll sit on their own 128-byte line, so
+// that polling does not slow the atomics on a neighbour.
 constexpr int kCtrLine = 32;
-constexpr int kEpochWord = 2 * kCtrLine;
 __device__ __forceinline__ unsigned* ctr_claim(const TokArgs& a) { return a.ctr; }
 __device__ __forceinline__ unsigned* ctr_exited(const TokArgs& a) { return a.ctr + kCtrLine; }
-// Rows of x_l / of a slot's act whose stores were issued (relaxed adds
-// after the stores, no fence): the producers' wake-up hint.  The data words
-// themselves say whether they are written.
-__device__ __forceinline__ unsigned* ctr_xrows(const TokArgs& a, int l) { return a.ctr + kCtrLine * (3 + l); }
+__device__ __forceinline__ unsigned* ctr_xrows(const TokArgs& a, int l) {
+  return a.ctr + kCtrLine * (2 + l);
+}
 __device__ __forceinline__ unsigned* ctr_act(const TokArgs& a, int l, int s) {
-  return a.ctr + kCtrLine * (3 + a.L + l * a.K + s);
+  return a.ctr + kCtrLine * (2 + a.L + l * a.K + s);
 }
 __device__ __forceinline__ unsigned* ctr_route_ready(const TokArgs& a, int l) {
-  return a.ctr + kCtrLine * (3 + a.L + a.L * a.K + l);
+  return a.ctr + kCtrLine * (2 + a.L + a.L * a.K + l);
 }
-// router rows done per layer: atomics only
+// router rows done per layer, then the route-sum groups: atomics only
 __host__ __device__ __forceinline__ size_t token_rows_base(int L, int K) {
-  return (size_t)kCtrLine * (3 + 2 * (size_t)L + (size_t)L * K);
+  return (size_t)kCtrLine * (2 + 2 * L + (size_t)L * K);
+}
+__host__ __device__ __forceinline__ size_t token_grp_base(int L, int K) {
+  return token_rows_base(L, K) + (size_t)(L + kCtrLine - 1) / kCtrLine * kCtrLine;
 }
 __device__ __forceinline__ unsigned* ctr_route_rows(const TokArgs& a, int l) {
   return a.ctr + token_rows_base(a.L, a.K) + l;
 }
-__host__ __device__ __forceinline__ size_t token_ctr_words(int L, int K) {
-  return token_rows_base(L, K) + (size_t)(L + kCtrLine - 1) / kCtrLine * kCtrLine;
+__device__ __forceinline__ unsigned* ctr_grp(const TokArgs& a, int l, int g) {
+  return a.ctr + token_grp_base(a.L, a.K) + (size_t)l * a.G + g;
 }
 
-// Hand-off words of one token parity.
-__host__ __device__ __forceinline__ size_t token_hand_words(int L, int K, int hidden, int inter) {
-  return (size_t)L * (2 * (size_t)hidden + (size_t)K * inter + (size_t)K * hidden);
-}
-
-struct Hand {
-  uint32_t *xlin, *xsw, *act, *contrib;
-};
-
-__device__ __forceinline__ Hand hand_of(const TokArgs& a, int parity) {
-  Hand h;
-  h.xlin = a.hand + (size_t)parity * a.hand_words;
-  h.xsw = h.xlin + (size_t)a.L * a.hidden;
-  h.act = h.xsw + (size_t)a.L * a.hidden;
-  h.contrib = h.act + (size_t)a.L * a.K * a.inter;
-  return h;
-}
-
-// A hand-off word: the value's bits; kUnwritten (all ones, a NaN that
-// arithmetic never makes) = not written.  A value with those bits is stored
-// as the canonical NaN.
-constexpr uint32_t kUnwritten = 0xFFFFFFFFu;
-__device__ __forceinline__ uint32_t hand_enc(float v) {
-  const uint32_t b = __float_as_uint(v);
-  return b == kUnwritten ? 0x7FFFFFFFu : b;
-}
-__device__ __forceinline__ float hand_dec(uint32_t w) { return __uint_as_float(w); }
-
-__device__ __forceinline__ void st_relaxed_gpu(uint32_t* p, uint32_t v) {
-  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ uint4 ld_relaxed_gpu4(const uint4* p) {
-  uint4 v;
-  asm volatile("ld.relaxed.gpu.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p)
-               : "memory");
-  return v;
+__host__ __device__ __forceinline__ size_t token_ctr_words(int L, int K, int G) {
+  return token_grp_base(L, K) + (size_t)L * G;
 }
 
 // Shared routing table of the token, loaded once per CTA: record bases of
@@ -257,6 +196,12 @@ __device__ __forceinline__ void red_release_gpu(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Orders this thread's generic-proxy view of global memory with its
+// async-proxy (bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // L2 prefetch of `bytes` (a multiple of 16, may be 0) at a 16-byte aligned
 // global address; a hint, no data moves into this SM.
 __device__ __forceinline__ void l2_prefetch(const void* p, uint32_t bytes) {
@@ -291,109 +236,10 @@ __device__ __forceinline__ bool wait_smem_gt(const int* p, int v) {
   return true;
 }
 
-// True once a wait gave up (kErrTimeout recorded and not yet read): the
-// hand-off polls then stop at once instead of each running out its budget.
-__device__ __forceinline__ bool token_failed() {
-  return *reinterpret_cast<volatile int*>(&g_device_error) == kErrTimeout;
-}
-
-__device__ __forceinline__ void red_relaxed_gpu(unsigned* p, unsigned v) {
-  asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Bounded wait (one thread) until the hint counter *p >= target.
-__device__ __forceinline__ bool wait_hint(const unsigned* p, unsigned target) {
-  if (ld_relaxed_gpu(p) >= target) return true;
-  const long long t0 = clock64();
-  while (ld_relaxed_gpu(p) < target) {
-    if (token_failed() || clock64() - t0 > 4000000000LL) {
-      atomicExch(&g_device_error, kErrTimeout);
-      return false;
-    }
-    nanosleep_ns(128);
-  }
-  return true;
-}
-
-// Bounded poll of one hand-off word; decodes it.  After a timeout: 0.0f.
-__device__ __forceinline__ float hand_wait(const uint32_t* p, bool& ok) {
-  uint32_t w = ld_relaxed_gpu(p);
-  if (w == kUnwritten) {
-    const long long t0 = clock64();
-    while ((w = ld_relaxed_gpu(p)) == kUnwritten) {
-      if (token_failed() || clock64() - t0 > 4000000000LL) {
-        atomicExch(&g_device_error, kErrTimeout);
-        ok = false;
-        return 0.0f;
-      }
-      nanosleep_ns(64);
-    }
-  }
-  return hand_dec(w);
-}
-
-constexpr int kHandVec = 4;  // uint4 per consumer thread: n <= 4 * kCT * kHandVec = 4096 words
-
-__device__ __forceinline__ bool any_unwritten(const uint4& w) {
-  return (w.x == kUnwritten) | (w.y == kUnwritten) | (w.z == kUnwritten) | (w.w == kUnwritten);
-}
-
-// Completes a stage's copy of n hand-off words (n a multiple of 4, <= 4096),
-// all consumer threads: a word the bulk copy read before its store landed is
-// read again from src (same layout) until written, and put in place.  Ends
-// with a proxy fence, since the stage is later refilled by bulk copies.
-// False after a timeout (the words left unwritten become 0.0f).
-__device__ __forceinline__ bool take_handoff(uint32_t* sx, const uint32_t* src, int n, int tid) {
-  uint4* s4 = reinterpret_cast<uint4*>(sx);
-  const uint4* g4 = reinterpret_cast<const uint4*>(src);
-  const int n4 = n >> 2;
-  uint4 w[kHandVec];
-  unsigned need = 0;
-#pragma unroll
-  for (int j = 0; j < kHandVec; ++j) {
-    const int v = tid + j * kCT;
-    w[j] = v < n4 ? s4[v] : make_uint4(0u, 0u, 0u, 0u);
-    if (any_unwritten(w[j])) need |= 1u << j;
-  }
-  bool ok = true;
-  if (need) {
-    const unsigned fixed = need;
-    const long long t0 = clock64();
-    for (;;) {
-#pragma unroll
-      for (int j = 0; j < kHandVec; ++j) {
-        if (need & (1u << j)) {
-          w[j] = ld_relaxed_gpu4(g4 + tid + j * kCT);
-          if (!any_unwritten(w[j])) need &= ~(1u << j);
-        }
-      }
-      if (!need) break;
-      if (token_failed() || clock64() - t0 > 4000000000LL) {
-        atomicExch(&g_device_error, kErrTimeout);
-        ok = false;
-#pragma unroll
-        for (int j = 0; j < kHandVec; ++j) {
-          w[j].x = w[j].x == kUnwritten ? 0u : w[j].x;
-          w[j].y = w[j].y == kUnwritten ? 0u : w[j].y;
-          w[j].z = w[j].z == kUnwritten ? 0u : w[j].z;
-          w[j].w = w[j].w == kUnwritten ? 0u : w[j].w;
-        }
-        break;
-      }
-      nanosleep_ns(64);
-    }
-#pragma unroll
-    for (int j = 0; j < kHandVec; ++j)
-      if (fixed & (1u << j)) s4[tid + j * kCT] = w[j];
-  }
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  return ok;
-}
-
-// Router logit of one expert row (one warp; lane 0 holds it), x in shared memory.  Kept out of
+// Router logit of one expert row (one warp; lane 0 holds it).  Kept out of
 // line so that the router's registers do not weigh on the expert paths.
 __device__ __noinline__ float router_row(const float* gw, const float* x, int cols, int lane) {
-  return f32_row<true>(gw, x, cols, lane);
+  return f32_row(gw, x, cols, lane);
 }
 
 // route_topk_f32 of one layer on the calling (full) warp.
@@ -427,48 +273,18 @@ __device__ __forceinline__ SegPlace seg_place(const TokPhase& ph, int tid) {
   return s;
 }
 
-// The rows of one UP / DOWN item into the shared chain buffer (consumer
-// threads): chains past a short row are zeroed (the other projection's item
-// may have left values there), then each thread's two segments.
-template <int H>
-__device__ __forceinline__ void item_rows(const uint8_t* smem, uint32_t stage_off, const uint8_t* sp,
-                                          const TokPhase& ph, const SegPlace& sp2, int nrows, int tid,
-                                          float2 (&x)[16], bool x_stale, float* part) {
-  const int nch = 4 * ph.n_u;
-  if (nch < 256) {
-    const int w = 256 - nch;
-    for (int i = tid; i < nrows * w; i += kCT) {
-      const int rr = i / w;
-      part[rr * kRowPitch + part_index(nch + (i - rr * w))] = 0.0f;
-    }
-  }
-  if (sp2.active) {
-    const float* lut = reinterpret_cast<const float*>(sp + kLutOff);
-    const float4* xs = reinterpret_cast<const float4*>(sp + kXOff);
-    if (nrows == ph.krt)
-      segments<H, true>(smem, stage_off, ph.scale_off, ph.cb, ph.sb, sp2.team, ph.teams, sp2.par1, sp2.par2,
-                        sp2.cont, sp2.u1, sp2.u2, sp2.grp, nrows, lut, xs, x, x_stale, part);
-    else
-      segments<H, false>(smem, stage_off, ph.scale_off, ph.cb, ph.sb, sp2.team, ph.teams, sp2.par1, sp2.par2,
-                         sp2.cont, sp2.u1, sp2.u2, sp2.grp, nrows, lut, xs, x, x_stale, part);
-  }
-}
-
 // ROUTE: the launch has router items (ervf_moe_token_router); the plain
 // instantiation carries no router code at all.
 template <int H, bool ROUTE>
 __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_constant__ TokArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_last;
-  __shared__ unsigned s_epoch;
   const int tid = threadIdx.x;
   const int S = a.stages;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [kTokMaxStages]
   uint64_t* empty = full + kTokMaxStages;              // [kTokMaxStages]
-  int* pub_done = reinterpret_cast<int*>(smem + 64);    // items published
-  // consumers -> publisher: one mbarrier per ring slot (the publisher waits
-  // suspended, taking no issue slots from the consumer warps)
-  uint64_t* pub_full = reinterpret_cast<uint64_t*>(smem + kPubFullOff);  // [kPubRing]
+  int* done = reinterpret_cast<int*>(smem + 64);        // items stored by the consumers
+  int* pub_done = done + 1;                            // items published
   int* pubq = reinterpret_cast<int*>(smem + 128);      // [kPubRing][4] kind, layer, slot, r0 | nrows << 16
   float* yring = reinterpret_cast<float*>(smem + kYRingOff);
   float* part = reinterpret_cast<float*>(smem + a.part_off);
@@ -484,7 +300,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    for (int i = 0; i < kPubRing; ++i) mbar_init(&pub_full[i], 1);
+    *done = 0;
     *pub_done = 0;
     fence_mbar_init();
   }
@@ -498,19 +314,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
     tab_id[i] = e;
     tab_g[i] = make_float2(gl[2 * e], gl[2 * e + 1]);
   }
-  if (tid == 0) s_epoch = ld_relaxed_gpu(a.ctr + kEpochWord);
   __syncthreads();
-  const unsigned epoch = s_epoch;
-  const Hand hd = hand_of(a, (int)(epoch & 1u));
-  {
-    // this CTA's share of the other parity's words (the previous token's)
-    // back to "not written"
-    uint4* o4 = reinterpret_cast<uint4*>(a.hand + (size_t)((epoch & 1u) ^ 1u) * a.hand_words);
-    const size_t n4 = a.hand_words >> 2, per = (n4 + gridDim.x - 1) / gridDim.x;
-    const size_t i1 = min(n4, per * (blockIdx.x + 1));
-    const uint4 un = make_uint4(kUnwritten, kUnwritten, kUnwritten, kUnwritten);
-    for (size_t i = per * blockIdx.x + tid; i < i1; i += kTokThreads) o4[i] = un;
-  }
 
   if (tid >= kProd && tid < kPub) {
     // ------------------------------------------------------------ producer
@@ -535,12 +339,10 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
       if (ROUTE && kind == kItemRoute) {
         // router rows: no weights to stage (the consumer warps read them
         // directly); the stage completes once x_l is complete
-        const uint32_t* xsrc = hd.xlin + (size_t)l * a.hidden;
+        bool okx = true;
         if (lane == 0) {
           reinterpret_cast<int4*>(hdr)[0] = make_int4(kind, l, slot, r0);
           hdr[4] = nrows;
-          hdr[5] = a.hidden;
-          *reinterpret_cast<const uint32_t**>(hdr + 8) = xsrc;
           // the item's router rows do not depend on x: queue them into L2
           // now, so that the warps read them from L2 once x_l is complete
           const uint8_t* gw = reinterpret_cast<const uint8_t*>(a.layer_ptrs[5 * a.L + l]) +
@@ -548,16 +350,11 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
           const uint32_t gbytes = (uint32_t)nrows * (uint32_t)a.hidden * 4u;
           for (uint32_t off = 0; off < gbytes; off += 32768u)
             l2_prefetch(gw + off, gbytes - off < 32768u ? gbytes - off : 32768u);
+          okx = wait_count(ctr_xrows(a, l), (unsigned)a.hidden);
+          mbar_arrive(&full[st]);
           next = (int)atomicAdd(ctr_claim(a), 1u);
         }
-        // x_l (linear) once its rows' stores are issued, then the copy (made
-        // even after a timeout, in bounds, so the stage completes)
-        if (lane == 0) {
-          ok = wait_hint(ctr_xrows(a, l), (unsigned)a.hidden);
-          mbar_arrive_expect_tx(&full[st], (uint32_t)a.hidden * 4u);
-          bulk_g2s(sp + kXOff, xsrc, (uint32_t)a.hidden * 4u, &full[st]);
-        }
-        ok = __shfl_sync(kFull, ok, 0);
+        ok = __shfl_sync(kFull, okx, 0);
         ++it;
         if (!ok) break;
         continue;
@@ -605,14 +402,9 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
         lut4[q4] = make_float4(e4m3_lut_value(v) * g, e4m3_lut_value(v + 1) * g,
                                e4m3_lut_value(v + 2) * g, e4m3_lut_value(v + 3) * g);
       }
-      // the item's activation: x_l (UP) or the slot's act (DOWN)
-      const uint32_t* xsrc = up ? hd.xsw + (size_t)l * a.hidden
-                                : hd.act + ((size_t)l * a.K + slot) * a.inter;
       if (lane == 0) {
         reinterpret_cast<int4*>(hdr)[0] = make_int4(kind, l, slot, r0);
         hdr[4] = nrows;
-        hdr[5] = ph.cols;
-        *reinterpret_cast<const uint32_t**>(hdr + 8) = xsrc;
       }
       __syncwarp();
       if (lane == 0) {
@@ -648,14 +440,14 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
             l2_prefetch(sc2, (uint32_t)(n2 * p2.sb) & ~15u);
           }
         }
-      }
-      // the activation once all its rows' stores are issued (x_l: the last
-      // slot's DOWN items of layer l-1, or PREP; act: the slot's UP items),
-      // then the copy, made even after a timeout (in bounds) so that the
-      // stage completes
-      if (lane == 0) {
-        ok = up ? wait_hint(ctr_xrows(a, l), (unsigned)a.hidden) : wait_hint(ctr_act(a, l, slot), (unsigned)a.inter);
-        bulk_g2s(sp + kXOff, xsrc, (uint32_t)ph.cols * 4u, &full[st]);
+        // the item's activation: x_l (UP) or the slot's act (DOWN)
+        ok = up ? wait_count(ctr_xrows(a, l), (unsigned)a.hidden)
+                : wait_count(ctr_act(a, l, slot), (unsigned)a.inter);
+        fence_proxy_async_global();
+        // copied even after a timeout (in bounds), so that the stage completes
+        const float* xsrc = up ? a.xsw + (size_t)l * a.hidden
+                               : a.actsw + ((size_t)(l & 1) * a.K + slot) * a.inter;
+        bulk_g2s(sp + kXOff, xsrc, x_bytes, &full[st]);
       }
       ok = __shfl_sync(kFull, ok, 0);
       ++it;
@@ -676,7 +468,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
     const int lane = tid - kPub;
     for (int k = 0;; ++k) {
       bool ok = true;
-      if (lane == 0) ok = mbar_wait(&pub_full[k % kPubRing], (k / kPubRing) & 1);
+      if (lane == 0) ok = wait_smem_gt(done, k);
       ok = __shfl_sync(kFull, ok, 0);
       __syncwarp();
       if (!ok) break;
@@ -685,11 +477,15 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
       const int r0 = rr & 0xFFFF, nrows = rr >> 16;
       const float* yv = yring + (k % kPubRing) * 32;
       if (kind == kItemEnd) break;
-      // Every lane stores its own row value as a hand-off word; readers poll
-      // the words, so nothing here waits for the stores to land.
+      // Every lane stores its own row value; after the warp barrier lane 0's
+      // release (red / atom .release.gpu, cumulative over the stores ordered
+      // before it) publishes them.  All lanes work at once: the warp's path
+      // through shared memory and L2 stays a few round trips long even while
+      // the consumers keep the shared-memory pipe busy.  Readers acquire,
+      // then bulk copy (after a proxy fence) or load with __ldcg.
       const float y = lane < nrows ? yv[lane] : 0.0f;
       if (kind == kItemPrep) {
-        if (lane == 0) red_relaxed_gpu(ctr_xrows(a, 0), (unsigned)a.hidden);
+        if (lane == 0) red_release_gpu(ctr_xrows(a, 0), (unsigned)a.hidden);  // stores fenced by the consumers
       } else if (ROUTE && kind == kItemRoute) {
         // router logits; the item that completes the layer routes it (the
         // reference's route_topk_f32 on one warp) and releases the layer's ids
@@ -711,45 +507,47 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
       } else if (kind == kItemUp) {
         if (lane < nrows) {
           const float v = fmaxf(y, 0.0f);
-          st_relaxed_gpu(hd.act + ((size_t)l * a.K + slot) * a.inter + sw_index(r0 + lane), hand_enc(v * v));
+          a.actsw[((size_t)(l & 1) * a.K + slot) * a.inter + sw_index(r0 + lane)] = v * v;
         }
         __syncwarp();
-        if (lane == 0) red_relaxed_gpu(ctr_act(a, l, slot), (unsigned)nrows);
-      } else if (kind == kItemDown) {
-        uint32_t* cb = hd.contrib + (size_t)l * a.K * a.hidden;
-        if (slot + 1 < a.K) {
-          if (lane < nrows) st_relaxed_gpu(cb + (size_t)slot * a.hidden + r0 + lane, hand_enc(y));
-        } else if (lane < nrows) {
-          // the last slot's block: the route sum of its rows in ROUTE order
-          // over every slot's row (loaded at once, then polled where a store
-          // has not landed yet), then x_{l+1} = x_l + acc
-          const int r = r0 + lane;
-          uint32_t w[kTokMaxK - 1];
-#pragma unroll
-          for (int s2 = 0; s2 < kTokMaxK - 1; ++s2)
-            if (s2 < a.K - 1) w[s2] = ld_relaxed_gpu(cb + (size_t)s2 * a.hidden + r);
-          const uint32_t wx = ld_relaxed_gpu(hd.xlin + (size_t)l * a.hidden + r);
-          bool vok = true;
-          float acc = 0.0f;
-#pragma unroll
-          for (int s2 = 0; s2 < kTokMaxK - 1; ++s2) {
-            if (s2 < a.K - 1) {
-              const float c = w[s2] != kUnwritten ? hand_dec(w[s2]) : hand_wait(cb + (size_t)s2 * a.hidden + r, vok);
-              acc = fmaf(c, ROUTE ? __ldcg(a.route_w + l * a.K + s2) : a.route_w[l * a.K + s2], acc);
+        if (lane == 0) red_release_gpu(ctr_act(a, l, slot), (unsigned)nrows);
+      } else {
+        if (lane < nrows) a.contrib[((size_t)(l & 1) * a.K + slot) * a.hidden + r0 + lane] = y;
+        __syncwarp();
+        const int g0 = r0 >> 5, g1 = (r0 + nrows - 1) >> 5;
+        int last = -1;
+        if (lane <= g1 - g0) {
+          const int g = g0 + lane;
+          const int lo = max(r0, g << 5), hi = min(r0 + nrows, (g << 5) + 32);
+          const int grows = min(a.hidden, (g << 5) + 32) - (g << 5);
+          const unsigned old = atom_add_acq_rel_gpu(ctr_grp(a, l, g), (unsigned)(hi - lo));
+          if ((int)old + (hi - lo) == a.K * grows) last = g;
+        }
+        __syncwarp();
+        unsigned m = __ballot_sync(kFull, last >= 0);
+        while (m) {
+          const int src = __ffs(m) - 1;
+          m &= m - 1;
+          const int g = __shfl_sync(kFull, last, src);
+          const int grows = min(a.hidden, (g << 5) + 32) - (g << 5);
+          const int r = (g << 5) + lane;
+          if (lane < grows) {
+            const float* cb = a.contrib + (size_t)(l & 1) * a.K * a.hidden;
+            float acc = 0.0f;
+            for (int s2 = 0; s2 < a.K; ++s2)
+              acc = fmaf(__ldcg(cb + (size_t)s2 * a.hidden + r),
+                         ROUTE ? __ldcg(a.route_w + l * a.K + s2) : a.route_w[l * a.K + s2], acc);
+            const float xv = __ldcg(a.xlin + (size_t)l * a.hidden + r) + acc;
+            if (l + 1 < a.L) {
+              a.xlin[(size_t)(l + 1) * a.hidden + r] = xv;
+              a.xsw[(size_t)(l + 1) * a.hidden + sw_index(r)] = xv;
+            } else {
+              a.out[r] = xv;
             }
           }
-          acc = fmaf(y, ROUTE ? __ldcg(a.route_w + l * a.K + a.K - 1) : a.route_w[l * a.K + a.K - 1], acc);
-          const float xv = (wx != kUnwritten ? hand_dec(wx) : hand_wait(hd.xlin + (size_t)l * a.hidden + r, vok)) + acc;
-          if (l + 1 < a.L) {
-            const uint32_t e = hand_enc(xv);
-            st_relaxed_gpu(hd.xlin + (size_t)(l + 1) * a.hidden + r, e);
-            st_relaxed_gpu(hd.xsw + (size_t)(l + 1) * a.hidden + sw_index(r), e);
-          } else {
-            a.out[r] = xv;
-          }
+          __syncwarp();
+          if (lane == 0 && l + 1 < a.L) red_release_gpu(ctr_xrows(a, l + 1), (unsigned)grows);
         }
-        __syncwarp();
-        if (slot + 1 == a.K && lane == 0 && l + 1 < a.L) red_relaxed_gpu(ctr_xrows(a, l + 1), (unsigned)nrows);
       }
       __syncwarp();
       if (lane == 0) st_release_cta(pub_done, k + 1);
@@ -762,31 +560,14 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
     int last_key = -1;
     bool ring_fail = false;  // tid 0: the publisher stopped taking items
     int it = 0;
-    bool retry = false;  // the item's rows came out NaN: complete its copy, compute again
-    for (;;) {
+    for (;; ++it) {
       const int st = it % S;
       const bool to = !mbar_wait(&full[st], (it / S) & 1) || ring_fail;
-      uint8_t* sp = stages + (size_t)st * a.stage_bytes;
+      const uint8_t* sp = stages + (size_t)st * a.stage_bytes;
       const int* hdr = reinterpret_cast<const int*>(sp);
-      int kind = to ? kItemEnd : hdr[0];
-      // Router items complete their copy of x_l before use (words the copy
-      // read before their store landed are polled from global memory).  UP /
-      // DOWN items use their copy as it is: an unwritten word (a NaN) turns
-      // every row of the item into a NaN, which the check after the rows'
-      // trees catches; the item then runs again (same stage, `retry`) after
-      // completing its copy, and a NaN then is the data's.  Every consumer
-      // thread takes each barrier on every item (`to` differs between
-      // threads); a timeout stops everyone.
-      bool vok = true;
-      if ((ROUTE && kind == kItemRoute) || retry) {
-        const uint32_t* src = *reinterpret_cast<const uint32_t* const*>(hdr + 8);
-        vok = take_handoff(reinterpret_cast<uint32_t*>(sp + kXOff), src, hdr[5], tid);
-      }
-      bool vfail = (ROUTE || retry) ? named_bar_or(kBarC, kCT, !vok) : false;
-      if (vfail) kind = kItemEnd;
+      const int kind = to ? kItemEnd : hdr[0];
       int l = 0, slot = 0, r0 = 0, nrows = 0;
       float route_v = 0.0f;  // kItemRoute: this warp's router logit (lane 0)
-      const bool rows_item = kind == kItemUp || kind == kItemDown;
       if (ROUTE && kind == kItemRoute) {
         l = hdr[1];
         r0 = hdr[3];
@@ -795,65 +576,79 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
         if (w < nrows) {
           const float* gw = reinterpret_cast<const float*>(a.layer_ptrs[5 * a.L + l]) +
                             (size_t)(r0 + w) * a.hidden;
-          route_v = router_row(gw, reinterpret_cast<const float*>(sp + kXOff), a.hidden, tid & 31);
+          route_v = router_row(gw, a.xlin + (size_t)l * a.hidden, a.hidden, tid & 31);
         }
       } else if (kind == kItemPrep) {
-        // x_0, linear and swizzled
-        const Hand h0 = hand_of(a, (int)(s_epoch & 1u));
-        for (int i = tid; i < a.hidden; i += kCT) {
-          const uint32_t w = hand_enc(a.x_in[i]);
-          st_relaxed_gpu(h0.xlin + i, w);
-          st_relaxed_gpu(h0.xsw + sw_index(i), w);
+        const int nu = a.hidden >> 5;
+        float4* xs0 = reinterpret_cast<float4*>(a.xsw);
+        for (int f = tid; f < nu * 8; f += kCT) {
+          const int t = f >> 3, k = f & 7;
+          xs0[t * 8 + (k ^ (t & 7))] = x_slot(a.x_in, t, k);
         }
-      } else if (rows_item) {
+        for (int i = tid; i < a.hidden; i += kCT) a.xlin[i] = a.x_in[i];
+        fence_proxy_async_global();
+        __threadfence();
+      } else if (kind == kItemUp || kind == kItemDown) {
         l = hdr[1];
         slot = hdr[2];
         r0 = hdr[3];
         nrows = hdr[4];
-      }
-      const uint32_t stage_off = (uint32_t)(a.stage_base + st * a.stage_bytes + a.codes_off);
-      if (rows_item) {
         const bool up = kind == kItemUp;
+        const TokPhase& ph = up ? a.up : a.dn;
+        const SegPlace& sp2 = up ? pu : pd;
         const int key = (kind << 24) | (l << 8) | slot;
-        bool x_stale = retry || key != last_key;
+        bool x_stale = key != last_key;
         last_key = key;
-        item_rows<H>(smem, stage_off, sp, up ? a.up : a.dn, up ? pu : pd, nrows, tid, x, x_stale, part);
+        // a row of fewer than 64 units leaves chains 4 n_u..255 unwritten:
+        // zero them (the other projection's item may have left values there)
+        const int nch = 4 * ph.n_u;
+        if (nch < 256) {
+          const int w = 256 - nch;
+          for (int i = tid; i < nrows * w; i += kCT) {
+            const int rr = i / w;
+            part[rr * kRowPitch + part_index(nch + (i - rr * w))] = 0.0f;
+          }
+        }
+        if (sp2.active) {
+          const uint32_t stage_off = (uint32_t)(a.stage_base + st * a.stage_bytes + a.codes_off);
+          const float* lut = reinterpret_cast<const float*>(sp + kLutOff);
+          const float4* xs = reinterpret_cast<const float4*>(sp + kXOff);
+          if (nrows == ph.krt) {
+            segments<H, true>(smem, stage_off, ph.scale_off, ph.cb, ph.sb, sp2.team, ph.teams, sp2.par1,
+                              sp2.par2, sp2.cont, sp2.u1, sp2.u2, sp2.grp, nrows, lut, xs, x, x_stale,
+                              part);
+          } else {
+            segments<H, false>(smem, stage_off, ph.scale_off, ph.cb, ph.sb, sp2.team, ph.teams, sp2.par1,
+                               sp2.par2, sp2.cont, sp2.u1, sp2.u2, sp2.grp, nrows, lut, xs, x, x_stale,
+                               part);
+          }
+        }
       }
       // tid 0: this item's publisher ring slot must be free (the publisher
       // has taken item it - kPubRing); a wait that runs out stops everyone
       if (tid == 0 && !to && kind != kItemEnd && !wait_smem_gt(pub_done, it - kPubRing)) ring_fail = true;
-      // the rows' partials are complete; a timeout anywhere stops all consumers
-      if (named_bar_or(kBarC, kCT, to || ring_fail || vfail)) vfail = true;
-      float y = 0.0f;
-      if (!vfail && rows_item) {
-        if (tr < nrows) y = group_tree(part + tr * kRowPitch + tw * kGroupPitch);
-        y = combine8(y);
-        // a NaN row on the first run: the copy may have read an unwritten word
-        if (named_bar_or(kBarC, kCT, !retry && tw == 0 && tr < nrows && y != y)) {
-          retry = true;
-          continue;  // the same item, same stage
-        }
-      }
-      retry = false;
-      // every read of the stage is done
-      if (tid == 0 && !vfail && kind != kItemEnd) mbar_arrive(&empty[st]);
-      if (vfail || kind == kItemEnd) break;
+      // every read of the stage is done; a timeout anywhere stops all consumers
+      const bool stop = named_bar_or(kBarC, kCT, to || ring_fail);
+      if (tid == 0 && !stop && kind != kItemEnd) mbar_arrive(&empty[st]);
+      if (stop || kind == kItemEnd) break;
       if (ROUTE && kind == kItemRoute) {
         if ((tid & 31) == 0 && (tid >> 5) < nrows) yring[(it % kPubRing) * 32 + (tid >> 5)] = route_v;
-      } else if (rows_item) {
+      } else if (kind != kItemPrep) {
+        float y = 0.0f;
+        if (tr < nrows) y = group_tree(part + tr * kRowPitch + tw * kGroupPitch);
+        y = combine8(y);
         if (tw == 0 && tr < nrows) yring[(it % kPubRing) * 32 + tr] = y;
       }
       named_bar_sync(kBarC, kCT);  // the chain buffer is rewritten by the next item
       if (tid == 0) {  // hand the item to the publisher
         reinterpret_cast<int4*>(pubq)[it % kPubRing] = make_int4(kind, l, slot, r0 | (nrows << 16));
-        mbar_arrive(&pub_full[it % kPubRing]);
+        st_release_cta(done, it + 1);
       }
-      ++it;
     }
     // end marker for the publisher
     if (tid == 0 && !ring_fail && wait_smem_gt(pub_done, it - kPubRing)) {
       pubq[(it % kPubRing) * 4] = kItemEnd;
-      mbar_arrive(&pub_full[it % kPubRing]);
+      st_release_cta(done, it + 1);
     }
   }
 
@@ -866,9 +661,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
   __syncthreads();
   if (s_last) {
     __threadfence();
-    for (int i = tid; i < a.n_ctr; i += kTokThreads)
-      if (i != kEpochWord) a.ctr[i] = 0u;
-    if (tid == 0) a.ctr[kEpochWord] = s_epoch + 1u;  // the next token takes the other parity
+    for (int i = tid; i < a.n_ctr; i += kTokThreads) a.ctr[i] = 0u;
   }
 }
 
@@ -938,20 +731,10 @@ int launch_token_h(const TokArgs& a, int smem, bool pdl, cudaStream_t stream) {
 }  // namespace
 
 size_t moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top_k) {
-  const size_t n_ctr = token_ctr_words(n_layers, top_k);
+  const size_t n_ctr = token_ctr_words(n_layers, top_k, (hidden + 31) / 32);
   const size_t ctr = (n_ctr * 4 + 255) / 256 * 256;
-  return ctr + 4 * (2 * token_hand_words(n_layers, top_k, hidden, inter) +
+  return ctr + 4 * ((size_t)2 * n_layers * hidden + (size_t)2 * top_k * inter + (size_t)2 * top_k * hidden +
                     (size_t)n_layers * kTokMaxRouteExperts);
-}
-
-int init_moe_token_scratch(void* scratch, int n_layers, int hidden, int inter, int top_k,
-                           cudaStream_t stream) {
-  uint8_t* s = reinterpret_cast<uint8_t*>(scratch);
-  const size_t ctr = (token_ctr_words(n_layers, top_k) * 4 + 255) / 256 * 256;
-  const size_t hand = (size_t)4 * 2 * token_hand_words(n_layers, top_k, hidden, inter);
-  if (cudaMemsetAsync(s, 0, ctr, stream) != cudaSuccess) return kErrLaunch;
-  if (cudaMemsetAsync(s + ctr, 0xFF, hand, stream) != cudaSuccess) return kErrLaunch;
-  return kOk;
 }
 
 int launch_moe_token(const MoeTokenArgs& in, cudaStream_t stream) {
@@ -974,6 +757,7 @@ int launch_moe_token(const MoeTokenArgs& in, cudaStream_t stream) {
   a.E = in.n_experts;
   a.hidden = in.hidden;
   a.inter = in.inter;
+  a.G = (in.hidden + 31) / 32;
   a.up = make_phase(in.inter, in.hidden);
   a.dn = make_phase(in.hidden, in.inter);
   const int blk_u = row_block_tok(in.hidden), blk_d = row_block_tok(in.inter);
@@ -1027,12 +811,17 @@ int launch_moe_token(const MoeTokenArgs& in, cudaStream_t stream) {
   a.total = 1 + a.L * a.per_layer;
 
   uint8_t* s = reinterpret_cast<uint8_t*>(in.scratch);
-  a.n_ctr = (int)token_ctr_words(a.L, a.K);
+  a.n_ctr = (int)token_ctr_words(a.L, a.K, a.G);
   a.ctr = reinterpret_cast<unsigned*>(s);
   s += ((size_t)a.n_ctr * 4 + 255) / 256 * 256;
-  a.hand = reinterpret_cast<uint32_t*>(s);
-  a.hand_words = token_hand_words(a.L, a.K, a.hidden, a.inter);
-  s += (size_t)4 * 2 * a.hand_words;
+  a.xlin = reinterpret_cast<float*>(s);
+  s += (size_t)4 * a.L * a.hidden;
+  a.xsw = reinterpret_cast<float*>(s);
+  s += (size_t)4 * a.L * a.hidden;
+  a.actsw = reinterpret_cast<float*>(s);
+  s += (size_t)4 * 2 * a.K * a.inter;
+  a.contrib = reinterpret_cast<float*>(s);
+  s += (size_t)4 * 2 * a.K * a.hidden;
   a.rlog = reinterpret_cast<float*>(s);
 
   if (a.route) {

@@ -184,8 +184,7 @@ class MoEDecoder:
                      + [ptr(t) for t in bank.globals])
             self.layer_ptrs = torch.tensor(addrs, dtype=torch.int64, device=d)
             nb = _lib.load().ervf_moe_token_scratch_bytes(L, bank.hidden, bank.inter, k)
-            self.tok_scratch = torch.empty(nb, dtype=torch.uint8, device=d)
-            self._init_tok_scratch()
+            self.tok_scratch = torch.zeros(nb, dtype=torch.uint8, device=d)
 
     def _s(self) -> int:
         return int(torch.cuda.current_stream(self.bank.device).cuda_stream)
@@ -360,13 +359,6 @@ class MoEDecoder:
             cur = nxt
         return cur
 
-    def _init_tok_scratch(self) -> None:
-        """Token scratch ready for its first launch: counters zero, every
-        hand-off word unwritten (stream-ordered)."""
-        b = self.bank
-        _lib.call("ervf_moe_token_scratch_init", ptr(self.tok_scratch), self.tok_scratch.numel(),
-                  b.n_layers, b.hidden, b.inter, self.top_k, self._s())
-
     def device_status(self) -> int:
         """Read and clear the library's device error words; after a timeout
         zero this decoder's scratch buffers (and the FusedNVFP4 caches) so the
@@ -375,7 +367,7 @@ class MoEDecoder:
         if st == _lib.ERR_TIMEOUT:
             self.scratch.zero_()
             if self.tok_scratch is not None:
-                self._init_tok_scratch()
+                self.tok_scratch.zero_()
         return st
 
     def token_step_router(self, x_in: torch.Tensor, out: torch.Tensor, gate_w: torch.Tensor,

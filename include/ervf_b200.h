@@ -173,13 +173,11 @@ ERVF_API int ervf_moe_layer(const uint8_t* up_codes, const uint8_t* up_scales, s
  * bases, [4L, 5L) globals f32[n_experts][2] (down, up) of each layer; expert
  * e of layer l sits at base + e * stride.  ids int32[L][top_k] and route_w
  * f32[L][top_k] on the device (ids clamped into [0, n_experts)).  out may be
- * x.  scratch: ervf_moe_token_scratch_bytes bytes, 256-byte aligned, set up
- * once with ervf_moe_token_scratch_init before first use (and again before
- * it serves another shape); every launch leaves it ready for the next, also
- * after a timeout (the last CTA to leave resets the counters).  Launches
- * sharing a scratch must not overlap.  flags: ERVF_LAUNCH_PDL or 0.  Bases
- * and strides 16-byte aligned; hidden, inter multiples of 32, <= 4096;
- * top_k <= 16. */
+ * x.  scratch: ervf_moe_token_scratch_bytes bytes, 256-byte aligned, zeroed
+ * once before first use; every launch leaves its counters zero again, also
+ * after a timeout (the last CTA to leave resets them).  Launches sharing a
+ * scratch must not overlap.  flags: ERVF_LAUNCH_PDL or 0.  Bases and strides
+ * 16-byte aligned; hidden, inter multiples of 32, <= 4096; top_k <= 16. */
 ERVF_API int ervf_moe_token(const uint64_t* layer_ptrs, int n_layers, size_t up_code_stride,
                             size_t up_scale_stride, size_t dn_code_stride, size_t dn_scale_stride,
                             const int32_t* ids, const float* route_w, int top_k, int n_experts,
@@ -209,13 +207,6 @@ ERVF_API int ervf_moe_token_router(const uint64_t* layer_ptrs, int n_layers, siz
 
 /* Bytes of scratch ervf_moe_token uses (counters and per-layer activations). */
 ERVF_API size_t ervf_moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top_k);
-
-/* Prepares a token scratch for ervf_moe_token / ervf_moe_token_router of this
- * shape: zeroes the counters and marks every activation word unwritten
- * (all-ones bytes), as memsets on `stream`.  No counterpart in the
- * reference.  Arguments are checked as for ervf_moe_token. */
-ERVF_API int ervf_moe_token_scratch_init(void* scratch, size_t scratch_bytes, int n_layers, int hidden,
-                                         int inter, int top_k, void* stream);
 
 /* ervf_moe_down_routesum without a scratch argument.  No counterpart in the
  * reference.  The scratch is a fixed device array inside the library, so the

@@ -77,10 +77,3 @@ def test_token_entries_check_arguments_without_a_device():
     assert lib.ervf_moe_token_router(*r, 512, 1.0, 0, *tail) == _lib.ERR_SHAPE   # > 256 experts
     assert lib.ervf_moe_token_router(*r, 128, 1.0, 2, *tail) == _lib.ERR_ARG     # bad_pick
     assert lib.ervf_moe_token_router(*r, 4, 1.0, 0, *tail) == _lib.ERR_SHAPE     # top_k > experts
-    init = lib.ervf_moe_token_scratch_init
-    assert init(None, nb, 24, 2688, 1856, 6, None) == _lib.ERR_NULL
-    assert init(p, nb, 24, 2688, 1856, 17, None) == _lib.ERR_SHAPE        # top_k > 16
-    assert init(p, nb, 24, 2700, 1856, 6, None) == _lib.ERR_SHAPE         # hidden % 32
-    assert init(p, nb - 1, 24, 2688, 1856, 6, None) == _lib.ERR_ARG       # scratch too small
-    q = (p + 255) // 256 * 256 + 16
-    assert init(q, nb, 24, 2688, 1856, 6, None) == _lib.ERR_ALIGN          # not 256-byte aligned

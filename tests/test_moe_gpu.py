@@ -158,40 +158,8 @@ def test_token_launch_equals_layer_chain(fused, cuda, hidden, inter, E, k, L):
         torch.cuda.synchronize()
         assert np.isfinite(y_ref.cpu().numpy()).all()
         assert bits_equal(y_tok.cpu().numpy(), y_ref.cpu().numpy()), f"token {t}"
-    # counters: claim, exit, epoch (one advance per launch), x / act / router lines
-    n_ctr = 32 * (3 + 2 * L + L * k) + (L + 31) // 32 * 32
-    ctr = dec.tok_scratch[:4 * n_ctr].view(torch.int32).cpu()
-    assert int(ctr[:64].abs().sum()) == 0 and int(ctr[96:].abs().sum()) == 0
-    assert int(ctr[64]) == 3
-    from ervf_b200 import _lib
-
-    assert _lib.load().ervf_device_status() == 0
-
-
-def test_token_launch_with_nan_input_equals_layer_chain(fused, cuda):
-    """A NaN in x makes every up row of every layer a NaN, which sends each up
-    item of the one-launch token kernel through its check-and-recompute path
-    (the path that catches a copy made before every activation word landed);
-    the result still equals the per-layer launches bit for bit, for three
-    tokens on one scratch."""
-    from ervf_b200.moe import ExpertBank, MoEDecoder
-
-    L, E, k, hidden, inter = 3, 8, 6, 1024, 512
-    eb = ExpertBank.synthetic(L, E, hidden, inter, cuda, seed=7)
-    dec = MoEDecoder(eb, k)
-    gen = torch.Generator(device=cuda)
-    gen.manual_seed(11)
-    for t in range(3):
-        rl = torch.randn(L, E, generator=gen, device=cuda)
-        x = torch.randn(hidden, generator=gen, device=cuda) * 0.05
-        x[37 * (t + 1)] = float("nan")
-        dec.token = True
-        y_tok = dec.step(x, rl).clone()
-        dec.token = False
-        y_ref = dec.step(x, rl).clone()
-        torch.cuda.synchronize()
-        assert np.isnan(y_ref.cpu().numpy()).sum() >= 1
-        assert bits_equal(y_tok.cpu().numpy(), y_ref.cpu().numpy()), f"token {t}"
+    n_ctr = 32 * (2 + L + L * k) + L * ((hidden + 31) // 32)
+    assert int(dec.tok_scratch[:4 * n_ctr].view(torch.int32).abs().sum()) == 0
     from ervf_b200 import _lib
 
     assert _lib.load().ervf_device_status() == 0
