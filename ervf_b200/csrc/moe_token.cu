@@ -62,8 +62,11 @@ constexpr int kTokMaxStages = 4;  // ring depth is chosen per launch (2..4)
 constexpr int kPubRing = 16;     // item descriptors between consumers and publisher
 constexpr int kLutOff = 64;      // stage: header [0, 64), block-scale table [64, 1088)
 constexpr int kXOff = kLutOff + 1024;
+constexpr int kPubFullOff = 384;  // [kPubRing] mbarriers: ring slot filled (pubq at 128 .. 384)
 constexpr int kYRingOff = 512;    // [kPubRing][32] row values handed to the publisher
 constexpr int kTabOff = kYRingOff + kPubRing * 32 * 4;  // per-token routing table, then the chain buffer
+static_assert(128 + 16 * kPubRing <= kPubFullOff && kPubFullOff + 8 * kPubRing <= kYRingOff,
+              "publisher ring layout");
 constexpr unsigned kFull = 0xffffffffu;
 
 enum : int { kItemPrep = 0, kItemUp = 1, kItemDown = 2, kItemEnd = 3, kItemRoute = 4 };
@@ -283,8 +286,11 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
   const int S = a.stages;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [kTokMaxStages]
   uint64_t* empty = full + kTokMaxStages;              // [kTokMaxStages]
-  int* done = reinterpret_cast<int*>(smem + 64);        // items stored by the consumers
-  int* pub_done = done + 1;                            // items published
+  int* pub_done = reinterpret_cast<int*>(smem + 64);    // items published
+  // consumers -> publisher: one mbarrier per ring slot, so that the idle
+  // publisher waits suspended instead of taking issue slots from the
+  // consumer warps
+  uint64_t* pub_full = reinterpret_cast<uint64_t*>(smem + kPubFullOff);  // [kPubRing]
   int* pubq = reinterpret_cast<int*>(smem + 128);      // [kPubRing][4] kind, layer, slot, r0 | nrows << 16
   float* yring = reinterpret_cast<float*>(smem + kYRingOff);
   float* part = reinterpret_cast<float*>(smem + a.part_off);
@@ -300,7 +306,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    *done = 0;
+    for (int i = 0; i < kPubRing; ++i) mbar_init(&pub_full[i], 1);
     *pub_done = 0;
     fence_mbar_init();
   }
@@ -468,7 +474,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
     const int lane = tid - kPub;
     for (int k = 0;; ++k) {
       bool ok = true;
-      if (lane == 0) ok = wait_smem_gt(done, k);
+      if (lane == 0) ok = mbar_wait(&pub_full[k % kPubRing], (k / kPubRing) & 1);
       ok = __shfl_sync(kFull, ok, 0);
       __syncwarp();
       if (!ok) break;
@@ -642,13 +648,13 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
       named_bar_sync(kBarC, kCT);  // the chain buffer is rewritten by the next item
       if (tid == 0) {  // hand the item to the publisher
         reinterpret_cast<int4*>(pubq)[it % kPubRing] = make_int4(kind, l, slot, r0 | (nrows << 16));
-        st_release_cta(done, it + 1);
+        mbar_arrive(&pub_full[it % kPubRing]);
       }
     }
     // end marker for the publisher
     if (tid == 0 && !ring_fail && wait_smem_gt(pub_done, it - kPubRing)) {
       pubq[(it % kPubRing) * 4] = kItemEnd;
-      st_release_cta(done, it + 1);
+      mbar_arrive(&pub_full[it % kPubRing]);
     }
   }
 
