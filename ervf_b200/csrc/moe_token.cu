@@ -94,7 +94,8 @@ struct TokArgs {
   float* rlog;                           // [L][E] router logits (route)
   const float* x_in;                     // [hidden]
   float* out;                            // [hidden]
-  int L, K, E, hidden, inter, G;         // G = 32-row groups of hidden
+  int L, K, E, hidden, inter;
+  int B;                                 // down row blocks per slot (the block counters' stride)
   TokPhase up, dn;
   int per_layer, total;
   int stages, stage_bytes, codes_off, stage_base, part_off;
@@ -122,22 +123,25 @@ __device__ __forceinline__ unsigned* ctr_act(const TokArgs& a, int l, int s) {
 __device__ __forceinline__ unsigned* ctr_route_ready(const TokArgs& a, int l) {
   return a.ctr + kCtrLine * (2 + a.L + a.L * a.K + l);
 }
-// router rows done per layer, then the route-sum groups: atomics only
+// router rows done per layer, then per (layer, down row block) the slots
+// 0..K-2 whose rows of the block are stored: atomics and one poller each
 __host__ __device__ __forceinline__ size_t token_rows_base(int L, int K) {
   return (size_t)kCtrLine * (2 + 2 * L + (size_t)L * K);
 }
-__host__ __device__ __forceinline__ size_t token_grp_base(int L, int K) {
+__host__ __device__ __forceinline__ size_t token_blk_base(int L, int K) {
   return token_rows_base(L, K) + (size_t)(L + kCtrLine - 1) / kCtrLine * kCtrLine;
 }
 __device__ __forceinline__ unsigned* ctr_route_rows(const TokArgs& a, int l) {
   return a.ctr + token_rows_base(a.L, a.K) + l;
 }
-__device__ __forceinline__ unsigned* ctr_grp(const TokArgs& a, int l, int g) {
-  return a.ctr + token_grp_base(a.L, a.K) + (size_t)l * a.G + g;
+__device__ __forceinline__ unsigned* ctr_blk(const TokArgs& a, int l, int b) {
+  return a.ctr + token_blk_base(a.L, a.K) + (size_t)l * a.B + b;
 }
 
-__host__ __device__ __forceinline__ size_t token_ctr_words(int L, int K, int G) {
-  return token_grp_base(L, K) + (size_t)L * G;
+// Counter words for B down row blocks per slot (B <= hidden / 2: a down item
+// has at least two rows).
+__host__ __device__ __forceinline__ size_t token_ctr_words(int L, int K, int B) {
+  return token_blk_base(L, K) + (size_t)L * B;
 }
 
 // Shared routing table of the token, loaded once per CTA: record bases of
@@ -517,43 +521,37 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
         }
         __syncwarp();
         if (lane == 0) red_release_gpu(ctr_act(a, l, slot), (unsigned)nrows);
-      } else {
+      } else if (slot + 1 < a.K) {
+        // a down block of slots 0..K-2: its rows, then the block's count
         if (lane < nrows) a.contrib[((size_t)(l & 1) * a.K + slot) * a.hidden + r0 + lane] = y;
         __syncwarp();
-        const int g0 = r0 >> 5, g1 = (r0 + nrows - 1) >> 5;
-        int last = -1;
-        if (lane <= g1 - g0) {
-          const int g = g0 + lane;
-          const int lo = max(r0, g << 5), hi = min(r0 + nrows, (g << 5) + 32);
-          const int grows = min(a.hidden, (g << 5) + 32) - (g << 5);
-          const unsigned old = atom_add_acq_rel_gpu(ctr_grp(a, l, g), (unsigned)(hi - lo));
-          if ((int)old + (hi - lo) == a.K * grows) last = g;
+        if (lane == 0) red_release_gpu(ctr_blk(a, l, r0 / a.dn.krt), 1u);
+      } else {
+        // the block of the last slot: once the other slots' rows of the block
+        // are in (their items were claimed earlier, so the wait is usually
+        // over), the route sum of its rows in ROUTE order, acc = fmaf(y_s,
+        // w_s, acc) from 0, and x_{l+1} = x_l + acc
+        // (a wait that runs out records kErrTimeout; the sum then goes on)
+        if (lane == 0 && a.K > 1) wait_count(ctr_blk(a, l, r0 / a.dn.krt), (unsigned)(a.K - 1));
+        __syncwarp();
+        const int r = r0 + lane;
+        if (lane < nrows) {
+          const float* cb = a.contrib + (size_t)(l & 1) * a.K * a.hidden;
+          float acc = 0.0f;
+          for (int s2 = 0; s2 + 1 < a.K; ++s2)
+            acc = fmaf(__ldcg(cb + (size_t)s2 * a.hidden + r),
+                       ROUTE ? __ldcg(a.route_w + l * a.K + s2) : a.route_w[l * a.K + s2], acc);
+          acc = fmaf(y, ROUTE ? __ldcg(a.route_w + l * a.K + a.K - 1) : a.route_w[l * a.K + a.K - 1], acc);
+          const float xv = __ldcg(a.xlin + (size_t)l * a.hidden + r) + acc;
+          if (l + 1 < a.L) {
+            a.xlin[(size_t)(l + 1) * a.hidden + r] = xv;
+            a.xsw[(size_t)(l + 1) * a.hidden + sw_index(r)] = xv;
+          } else {
+            a.out[r] = xv;
+          }
         }
         __syncwarp();
-        unsigned m = __ballot_sync(kFull, last >= 0);
-        while (m) {
-          const int src = __ffs(m) - 1;
-          m &= m - 1;
-          const int g = __shfl_sync(kFull, last, src);
-          const int grows = min(a.hidden, (g << 5) + 32) - (g << 5);
-          const int r = (g << 5) + lane;
-          if (lane < grows) {
-            const float* cb = a.contrib + (size_t)(l & 1) * a.K * a.hidden;
-            float acc = 0.0f;
-            for (int s2 = 0; s2 < a.K; ++s2)
-              acc = fmaf(__ldcg(cb + (size_t)s2 * a.hidden + r),
-                         ROUTE ? __ldcg(a.route_w + l * a.K + s2) : a.route_w[l * a.K + s2], acc);
-            const float xv = __ldcg(a.xlin + (size_t)l * a.hidden + r) + acc;
-            if (l + 1 < a.L) {
-              a.xlin[(size_t)(l + 1) * a.hidden + r] = xv;
-              a.xsw[(size_t)(l + 1) * a.hidden + sw_index(r)] = xv;
-            } else {
-              a.out[r] = xv;
-            }
-          }
-          __syncwarp();
-          if (lane == 0 && l + 1 < a.L) red_release_gpu(ctr_xrows(a, l + 1), (unsigned)grows);
-        }
+        if (lane == 0 && l + 1 < a.L) red_release_gpu(ctr_xrows(a, l + 1), (unsigned)nrows);
       }
       __syncwarp();
       if (lane == 0) st_release_cta(pub_done, k + 1);
@@ -737,7 +735,7 @@ int launch_token_h(const TokArgs& a, int smem, bool pdl, cudaStream_t stream) {
 }  // namespace
 
 size_t moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top_k) {
-  const size_t n_ctr = token_ctr_words(n_layers, top_k, (hidden + 31) / 32);
+  const size_t n_ctr = token_ctr_words(n_layers, top_k, hidden / 2);
   const size_t ctr = (n_ctr * 4 + 255) / 256 * 256;
   return ctr + 4 * ((size_t)2 * n_layers * hidden + (size_t)2 * top_k * inter + (size_t)2 * top_k * hidden +
                     (size_t)n_layers * kTokMaxRouteExperts);
@@ -763,7 +761,6 @@ int launch_moe_token(const MoeTokenArgs& in, cudaStream_t stream) {
   a.E = in.n_experts;
   a.hidden = in.hidden;
   a.inter = in.inter;
-  a.G = (in.hidden + 31) / 32;
   a.up = make_phase(in.inter, in.hidden);
   a.dn = make_phase(in.hidden, in.inter);
   const int blk_u = row_block_tok(in.hidden), blk_d = row_block_tok(in.inter);
@@ -817,9 +814,12 @@ int launch_moe_token(const MoeTokenArgs& in, cudaStream_t stream) {
   a.total = 1 + a.L * a.per_layer;
 
   uint8_t* s = reinterpret_cast<uint8_t*>(in.scratch);
-  a.n_ctr = (int)token_ctr_words(a.L, a.K, a.G);
+  // counters of this launch's row blocks; the area is laid out for the
+  // most blocks any H gives, so that the vectors after it do not move
+  a.B = a.dn.n_items;
+  a.n_ctr = (int)token_ctr_words(a.L, a.K, a.B);
   a.ctr = reinterpret_cast<unsigned*>(s);
-  s += ((size_t)a.n_ctr * 4 + 255) / 256 * 256;
+  s += (token_ctr_words(a.L, a.K, a.hidden / 2) * 4 + 255) / 256 * 256;
   a.xlin = reinterpret_cast<float*>(s);
   s += (size_t)4 * a.L * a.hidden;
   a.xsw = reinterpret_cast<float*>(s);
