@@ -437,16 +437,18 @@ def routed_decode(dec, device, hbm, steps=50):
     ms = time_graph(lambda i: dec.step_with_router(x, gate_w), steps, device)
     router_bytes = E * HIDDEN * 4 + HIDDEN * 4
     token_bytes = L * (TOP_K * dec.bank.expert_bytes() + router_bytes)
+    one = dec.token and dec.token_router and E <= 256
     res = {"ms_per_token": round(ms, 4), "tok_s": round(1e3 / ms, 1),
-           "launches_per_token": 1 if (dec.token and dec.token_router) else 3 * L,
+           "launches_per_token": 1 if one else 3 * L,
+           "path": "one launch (router items in the token kernel)" if one else "per-layer launches",
            "token_bytes": token_bytes,
            "frac": round(token_bytes / ms / 1e6 / hbm, 4)}
-    if dec.token and not dec.token_router:
-        # the same step with the routers inside the one-launch token kernel
-        dec.token_router = True
+    if dec.token:
+        # the same step on the other path
+        dec.token_router = not one
         ms1 = time_graph(lambda i: dec.step_with_router(x, gate_w), steps, device)
-        dec.token_router = False
-        res["one_launch_ms_per_token"] = round(ms1, 4)
+        dec.token_router = one
+        res["per_layer_ms_per_token" if one else "one_launch_ms_per_token"] = round(ms1, 4)
     return res
 
 

@@ -243,10 +243,11 @@ __device__ __forceinline__ bool wait_smem_gt(const int* p, int v) {
   return true;
 }
 
-// Router logit of one expert row (one warp; lane 0 holds it).  Kept out of
-// line so that the router's registers do not weigh on the expert paths.
+// Router logit of one expert row (one warp; lane 0 holds it; x in shared
+// memory).  Kept out of line so that the router's registers do not weigh on
+// the expert paths.
 __device__ __noinline__ float router_row(const float* gw, const float* x, int cols, int lane) {
-  return f32_row(gw, x, cols, lane);
+  return f32_row<true>(gw, x, cols, lane);
 }
 
 // route_topk_f32 of one layer on the calling (full) warp.
@@ -348,7 +349,8 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
       int* hdr = reinterpret_cast<int*>(sp);
       if (ROUTE && kind == kItemRoute) {
         // router rows: no weights to stage (the consumer warps read them
-        // directly); the stage completes once x_l is complete
+        // directly); the stage completes with a copy of x_l (linear), made
+        // once x_l is complete (and after a timeout, in bounds)
         bool okx = true;
         if (lane == 0) {
           reinterpret_cast<int4*>(hdr)[0] = make_int4(kind, l, slot, r0);
@@ -361,7 +363,9 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
           for (uint32_t off = 0; off < gbytes; off += 32768u)
             l2_prefetch(gw + off, gbytes - off < 32768u ? gbytes - off : 32768u);
           okx = wait_count(ctr_xrows(a, l), (unsigned)a.hidden);
-          mbar_arrive(&full[st]);
+          fence_proxy_async_global();
+          mbar_arrive_expect_tx(&full[st], (uint32_t)a.hidden * 4u);
+          bulk_g2s(sp + kXOff, a.xlin + (size_t)l * a.hidden, (uint32_t)a.hidden * 4u, &full[st]);
           next = (int)atomicAdd(ctr_claim(a), 1u);
         }
         ok = __shfl_sync(kFull, okx, 0);
@@ -497,15 +501,19 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
       if (kind == kItemPrep) {
         if (lane == 0) red_release_gpu(ctr_xrows(a, 0), (unsigned)a.hidden);  // stores fenced by the consumers
       } else if (ROUTE && kind == kItemRoute) {
-        // router logits; the item that completes the layer routes it (the
-        // reference's route_topk_f32 on one warp) and releases the layer's ids
+        // router logits.  The layer's last router item (claimed after the
+        // others) waits for their rows, routes the layer (the reference's
+        // route_topk_f32 on one warp) and releases the layer's ids; the
+        // others release their rows
         float* lg = a.rlog + (size_t)l * a.E;
         if (lane < nrows) lg[r0 + lane] = y;
         __syncwarp();
-        unsigned last = 0;
-        if (lane == 0) last = atom_add_acq_rel_gpu(ctr_route_rows(a, l), (unsigned)nrows) + nrows == (unsigned)a.E;
-        last = __shfl_sync(kFull, last, 0);
-        if (last) {
+        const bool last = r0 + nrows == a.E;
+        if (!last) {
+          if (lane == 0) red_release_gpu(ctr_route_rows(a, l), (unsigned)nrows);
+        } else {
+          // (a wait that runs out records kErrTimeout; the routing goes on)
+          if (lane == 0 && r0 > 0) wait_count(ctr_route_rows(a, l), (unsigned)r0);
           __syncwarp();
           const float* gb = reinterpret_cast<const float*>(a.layer_ptrs[6 * a.L + l]);
           int* io = const_cast<int*>(a.ids) + l * a.K;
@@ -580,7 +588,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
         if (w < nrows) {
           const float* gw = reinterpret_cast<const float*>(a.layer_ptrs[5 * a.L + l]) +
                             (size_t)(r0 + w) * a.hidden;
-          route_v = router_row(gw, a.xlin + (size_t)l * a.hidden, a.hidden, tid & 31);
+          route_v = router_row(gw, reinterpret_cast<const float*>(sp + kXOff), a.hidden, tid & 31);
         }
       } else if (kind == kItemPrep) {
         const int nu = a.hidden >> 5;

@@ -45,6 +45,8 @@ __device__ __forceinline__ float row_tree(float (&a)[8]) {
 // gemv_f32 (gpu_kernels.py:51-74): the same 256-chain walk, warp butterfly
 // and legacy combine as gemv_bf16 with fp32 weights.  One warp per row; lane
 // c owns chains 8c..8c+7 (two 128-bit loads per round).  Row sum in lane 0.
+// XS: x is in shared memory (plain loads); else global, read through L2.
+template <bool XS = false>
 __device__ __forceinline__ float f32_row(const float* __restrict__ wr, const float* __restrict__ x,
                                          int cols, int lane) {
   float acc[8];
@@ -56,8 +58,9 @@ __device__ __forceinline__ float f32_row(const float* __restrict__ wr, const flo
     const int k = 256 * i + 8 * lane;
     const float4 w0 = __ldcs(reinterpret_cast<const float4*>(wr + k));
     const float4 w1 = __ldcs(reinterpret_cast<const float4*>(wr + k + 4));
-    const float4 x0 = __ldcg(reinterpret_cast<const float4*>(x + k));
-    const float4 x1 = __ldcg(reinterpret_cast<const float4*>(x + k + 4));
+    const float4 x0 = XS ? *reinterpret_cast<const float4*>(x + k) : __ldcg(reinterpret_cast<const float4*>(x + k));
+    const float4 x1 =
+        XS ? *reinterpret_cast<const float4*>(x + k + 4) : __ldcg(reinterpret_cast<const float4*>(x + k + 4));
     const float2 a01 = fma2(make_float2(w0.x, w0.y), make_float2(x0.x, x0.y), make_float2(acc[0], acc[1]));
     const float2 a23 = fma2(make_float2(w0.z, w0.w), make_float2(x0.z, x0.w), make_float2(acc[2], acc[3]));
     const float2 a45 = fma2(make_float2(w1.x, w1.y), make_float2(x1.x, x1.y), make_float2(acc[4], acc[5]));
@@ -69,7 +72,7 @@ __device__ __forceinline__ float f32_row(const float* __restrict__ wr, const flo
     const int k = 256 * nfull + 8 * lane;
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      if (k + j < cols) acc[j] = fmaf(wr[k + j], __ldcg(x + k + j), acc[j]);
+      if (k + j < cols) acc[j] = fmaf(wr[k + j], XS ? x[k + j] : __ldcg(x + k + j), acc[j]);
   }
   return row_tree(acc);
 }
