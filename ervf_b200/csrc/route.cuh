@@ -53,7 +53,10 @@ __device__ __forceinline__ float f32_row(const float* __restrict__ wr, const flo
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
   const int nfull = cols >> 8;
-#pragma unroll 4
+  // x from shared memory leaves the weight loads as the only long ones: more
+  // of them in flight per round
+  constexpr int kUnroll = XS ? 5 : 4;
+#pragma unroll kUnroll
   for (int i = 0; i < nfull; ++i) {
     const int k = 256 * i + 8 * lane;
     const float4 w0 = __ldcs(reinterpret_cast<const float4*>(wr + k));
