@@ -62,7 +62,18 @@ namespace {
 // different warps overlap (4 issuers: ~30 cycles per MMA in aggregate).  So
 // kMmaIssuers warps issue a k-block's MMAs, each its own accumulator chain.
 constexpr int kMmaIssuers = 4;
-constexpr int kMmaWarps = 1 + kMmaIssuers + 8 + 4;
+#ifndef ERVF_MMA_DEC_WARPS
+#define ERVF_MMA_DEC_WARPS 8
+#endif
+// Decoders: kDecWarps warps, kDecWarps / 4 per tensor-memory lane quadrant,
+// each of a quadrant's warps on kDecCols of the k-block's 256 columns.
+constexpr int kDecWarps = ERVF_MMA_DEC_WARPS;
+constexpr int kDecGroups = kDecWarps / 4;
+constexpr int kDecCols = 256 / kDecGroups;  // columns per decoder thread and k-block
+constexpr int kDecSc = kDecCols / 16;       // their block-scale bytes
+constexpr int kDecSt = kDecCols / 64;       // their tcgen05.st of 32 columns
+static_assert(kDecWarps % 4 == 0 && kDecSt >= 1 && kDecSc % 4 == 0, "decoder split");
+constexpr int kMmaWarps = 1 + kMmaIssuers + kDecWarps + 4;
 constexpr int kMmaThreads = kMmaWarps * 32;
 constexpr int kM = 128;               // rows per unit (UMMA M)
 constexpr int kN = 16;                // batch columns (UMMA N)
@@ -86,7 +97,7 @@ constexpr int kDCol = 0;
 constexpr int kACol = 2 * kDAcc * kN;          // A stages: 128 + 128 a
 constexpr int kAStageCols = kKB / 2;          // 128 (two f16 per 32-bit column)
 static_assert(kACol + kAStages * kAStageCols <= kTmemCols, "tensor-memory columns");
-constexpr int kDecodeWarp0 = 1 + kMmaIssuers, kEpiWarp0 = kDecodeWarp0 + 8;
+constexpr int kDecodeWarp0 = 1 + kMmaIssuers, kEpiWarp0 = kDecodeWarp0 + kDecWarps;
 
 // shared memory: [0, 1024) barriers and slots, then the ring (1024-aligned
 // stages: the 128-byte swizzle repeats every 1024 bytes), then two scale buffers
@@ -275,14 +286,14 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       mbar_init(&empty[i], kMmaIssuers);
     }
     for (int i = 0; i < kAStages; ++i) {
-      mbar_init(&afull[i], 8);
+      mbar_init(&afull[i], kDecWarps);
       mbar_init(&aempty[i], kMmaIssuers);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&dfull[i], kMmaIssuers);
       mbar_init(&dempty[i], 4);
       mbar_init(&sfull[i], 1);
-      mbar_init(&sempty[i], 8);
+      mbar_init(&sempty[i], kDecWarps);
     }
     mbar_init(mma_done, kMmaIssuers);
     *dead = 0;
@@ -407,34 +418,35 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
           break;
         }
         const uint8_t* tile = ring + s * kStageBytes + r * 128;
-        // this half's 8 scale bytes (blocks 8h .. 8h+7 of the k-block).  Bytes
-        // past the row belong to the next row or to stale data: finite after
-        // the NaN mask, and their columns' codes are zero (TMA zero fill).
-        const int sc = kb * 16 + 8 * h;
-        uint32_t sq0, sq1;
+        // this group's kDecSc scale bytes (blocks kDecSc h .. of the
+        // k-block).  Bytes past the row belong to the next row or to stale
+        // data: finite after the NaN mask, and their columns' codes are zero
+        // (TMA zero fill).
+        const int sc = kb * 16 + kDecSc * h;
+        uint32_t sq[kDecSc / 4];
         if ((sb & 3) == 0) {
-          sq0 = *reinterpret_cast<const uint32_t*>(srow + sc);
-          sq1 = *reinterpret_cast<const uint32_t*>(srow + sc + 4);
+#pragma unroll
+          for (int j = 0; j < kDecSc / 4; ++j) sq[j] = *reinterpret_cast<const uint32_t*>(srow + sc + 4 * j);
         } else {
           const uint16_t* p2 = reinterpret_cast<const uint16_t*>(srow + sc);
-          sq0 = (uint32_t)p2[0] | ((uint32_t)p2[1] << 16);
-          sq1 = (uint32_t)p2[2] | ((uint32_t)p2[3] << 16);
-        }
-        uint32_t bc[8];
-        {
-          uint32_t t[4];
-          scales4(sq0, t);
-          bc[0] = t[0]; bc[1] = t[1]; bc[2] = t[2]; bc[3] = t[3];
-          scales4(sq1, t);
-          bc[4] = t[0]; bc[5] = t[1]; bc[6] = t[2]; bc[7] = t[3];
-        }
-        const uint32_t acol = tmem + ((uint32_t)(32 * q) << 16) + kACol + as * kAStageCols + 64 * h;
 #pragma unroll
-        for (int half2 = 0; half2 < 2; ++half2) {
+          for (int j = 0; j < kDecSc / 4; ++j) sq[j] = (uint32_t)p2[2 * j] | ((uint32_t)p2[2 * j + 1] << 16);
+        }
+        uint32_t bc[kDecSc];
+#pragma unroll
+        for (int j = 0; j < kDecSc / 4; ++j) {
+          uint32_t t[4];
+          scales4(sq[j], t);
+          bc[4 * j] = t[0]; bc[4 * j + 1] = t[1]; bc[4 * j + 2] = t[2]; bc[4 * j + 3] = t[3];
+        }
+        const uint32_t acol =
+            tmem + ((uint32_t)(32 * q) << 16) + kACol + as * kAStageCols + (kDecCols / 2) * h;
+#pragma unroll
+        for (int half2 = 0; half2 < kDecSt; ++half2) {
           uint32_t w[32];
 #pragma unroll
           for (int cc = 0; cc < 2; ++cc) {
-            const int c = 4 * h + 2 * half2 + cc;  // 16-byte chunk of the row (32 columns)
+            const int c = (kDecCols / 32) * h + 2 * half2 + cc;  // 16-byte chunk of the row (32 columns)
             const uint4 qv = *reinterpret_cast<const uint4*>(tile + ((c ^ (r & 7)) << 4));
             const uint32_t words[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
