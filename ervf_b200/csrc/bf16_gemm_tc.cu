@@ -18,10 +18,13 @@
 // stores them with tcgen05.st (row = lane; a bf16 pair is one 32-bit column,
 // K order): the A operand never touches the MMA's shared-memory path.  The X
 // halves go to a shared B tile in the canonical K-major core-matrix layout.
-// One thread issues four tcgen05.mma.kind::f16 (bf16 inputs, A from tensor
-// memory, M=128, N=16, K=16, f32 accumulate) per k-block and commits them to
-// the stage's mbarrier; two A / B stages overlap the next k-block's copies
-// with this one's MMAs.  The epilogue reads the accumulator with tcgen05.ld.
+// Four threads (lane 0 of warps 0..3) each issue one of the k-block's four
+// tcgen05.mma.kind::f16 (bf16 inputs, A from tensor memory, M=128, N=16,
+// K=16, f32 accumulate) into their own accumulator chain and commit it to the
+// stage's mbarrier -- an MMA takes its issuing thread ~95 cycles, and issuers
+// in different warps overlap; two A / B stages overlap the next k-block's
+// copies with this one's MMAs.  The epilogue reads the four chains with
+// tcgen05.ld and adds them in a fixed order.
 // Small matrices split K over several units per row tile so that every SM
 // works; the splits then add into the zeroed output with fp32 atomics, so the
 // last bits depend on their arrival order (within the tolerance above).
@@ -42,8 +45,9 @@ constexpr int kTcDepth = 4;                             // k-blocks of weights i
 constexpr int kTcRawStage = kTcM * kTcKB * 2;           // 16 KB of weight bytes
 constexpr int kTcSmem = 1024 + 2 * kTcBStage + kTcDepth * kTcRawStage;
 constexpr int kTcUnitBytes = 64;                        // per thread and k-block
-constexpr int kTcTmemCols = 128;     // D: columns 0..15; A stages: 32..63, 64..95
-constexpr int kTcACol = 32;
+constexpr int kTcIssuers = 4;        // MMA-issuing threads = accumulator chains
+constexpr int kTcTmemCols = 128;     // D: chains at columns 16 c (0..63); A stages: 64..95, 96..127
+constexpr int kTcACol = kTcIssuers * kTcN;
 constexpr int kTcAStageCols = kTcKB / 2;  // two bf16 per 32-bit column
 
 struct TcArgs {
@@ -105,9 +109,9 @@ __global__ void __launch_bounds__(kTcThreads) bf16_gemm_tc_kernel(TcArgs a) {
   const int nkb = (a.cols + kTcKB - 1) / kTcKB;
 
   if (tid == 0) {
-    mbar_init(&mb[0], 1);
-    mbar_init(&mb[1], 1);
-    mbar_init(&mb[2], 1);
+    mbar_init(&mb[0], kTcIssuers);
+    mbar_init(&mb[1], kTcIssuers);
+    mbar_init(&mb[2], kTcIssuers);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -204,19 +208,18 @@ __global__ void __launch_bounds__(kTcThreads) bf16_gemm_tc_kernel(TcArgs a) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncthreads();
-      if (tid == 0 && !dead) {
+      if (lane == 0 && warp < kTcIssuers && !dead) {
+        // issuer j: the k-block's MMA j (columns 16 j .. 16 j + 15) into chain j
+        const int j = warp;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t b0 = smem_u32(bst0 + s * kTcBStage);
-#pragma unroll
-        for (int j = 0; j < kTcKB / 16; ++j) {
-          const uint64_t db = umma_desc(b0 + 256 * j, 128, kTcBSBO);
-          const uint32_t accum = (kb > kb0 || j > 0) ? 1u : 0u;
-          asm volatile(
-              "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-              " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
-              ::"r"(tmem), "r"(tmem + kTcACol + s * kTcAStageCols + 8 * j), "l"(db), "r"(kTcIdesc),
-                "r"(accum) : "memory");
-        }
+        const uint64_t db = umma_desc(b0 + 256 * j, 128, kTcBSBO);
+        const uint32_t accum = kb > kb0 ? 1u : 0u;
+        asm volatile(
+            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+            " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
+            ::"r"(tmem + kTcN * j), "r"(tmem + kTcACol + s * kTcAStageCols + 8 * j), "l"(db), "r"(kTcIdesc),
+              "r"(accum) : "memory");
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                      ::"r"(smem_u32(&mb[s])) : "memory");
         if (kb + 1 == kb1)
@@ -224,26 +227,31 @@ __global__ void __launch_bounds__(kTcThreads) bf16_gemm_tc_kernel(TcArgs a) {
                        ::"r"(smem_u32(&mb[2])) : "memory");
       }
     }
-    // epilogue: accumulator (high + low halves) -> out
+    // epilogue: the four chains (high and low halves) -> out
     if (!dead) dead = !tc_wait(&mb[2], nacc & 1u);
     ++nacc;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (warp < 4) {
-      uint32_t v[16];
+      uint32_t v[kTcIssuers][16];
       const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-            "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-            "=r"(v[14]), "=r"(v[15])
-          : "r"(taddr));
+#pragma unroll
+      for (int c = 0; c < kTcIssuers; ++c)
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(v[c][0]), "=r"(v[c][1]), "=r"(v[c][2]), "=r"(v[c][3]), "=r"(v[c][4]), "=r"(v[c][5]),
+              "=r"(v[c][6]), "=r"(v[c][7]), "=r"(v[c][8]), "=r"(v[c][9]), "=r"(v[c][10]), "=r"(v[c][11]),
+              "=r"(v[c][12]), "=r"(v[c][13]), "=r"(v[c][14]), "=r"(v[c][15])
+            : "r"(taddr + kTcN * c));
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
       const int orow = tile * kTcM + warp * 32 + lane;
       if (!dead && orow < a.rows) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           if (j < a.n) {
-            const float y = __uint_as_float(v[j]) + __uint_as_float(v[j + 8]);
+            const auto f = [&](int c, int k) { return __uint_as_float(v[c][k]); };
+            const float hi = (f(0, j) + f(1, j)) + (f(2, j) + f(3, j));
+            const float lo = (f(0, j + 8) + f(1, j + 8)) + (f(2, j + 8) + f(3, j + 8));
+            const float y = hi + lo;
             float* o = a.out + (size_t)j * a.rows + orow;
             if (a.splits > 1) {
               atomicAdd(o, y);
