@@ -56,6 +56,8 @@ def parse():
                     help="expert-parallel exchange of the slot outputs (N > 1)")
     ap.add_argument("--gemv", type=int, nargs=2, metavar=("ROWS", "COLS"),
                     help="time one NVFP4 GEMV shape instead of the decode step")
+    ap.add_argument("--bf16-tc", type=int, nargs=3, metavar=("ROWS", "COLS", "N"),
+                    help="time one BF16 tensor-core GEMM shape and exit")
     ap.add_argument("--gemm-tc", type=int, nargs=3, metavar=("ROWS", "COLS", "N"),
                     help="time the tensor-core batched NVFP4 GEMM (N <= 16 tokens)")
     return ap.parse_args()
@@ -381,6 +383,33 @@ def bf16_gemvs(device, hbm):
     return res
 
 
+def bf16_tc_shape(device, hbm, rows, cols, n):
+    """One BF16 tensor-core GEMM shape [rows x cols] at batch n (config 3's
+    batched path), L2-cold replica pool, device time per call from a CUDA
+    graph; bytes as in bf16_gemvs."""
+    from ervf_b200 import GPUKernels
+
+    k = GPUKernels(device=device)
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    nbytes = 2 * rows * cols
+    reps = max(1, (8 * l2) // nbytes + 1) if nbytes < 2 * l2 else 2
+    w1 = (torch.randn(rows * cols, device=device) * 0.02).to(torch.bfloat16).view(torch.int16)
+    W = w1.reshape(1, -1).repeat(reps, 1)
+    del w1
+    x = torch.randn(n * cols, device=device)
+    out = torch.zeros(n * rows, device=device)
+
+    def call(i):
+        k.mm_bf16_tc(out, W[i % reps], x, rows, cols, n)
+
+    for i in range(3):
+        call(i)
+    ms = time_graph(call, max(16, 4 * reps), device)
+    algo = nbytes + 4 * cols * n + 4 * rows * n
+    return {"rows": rows, "cols": cols, "n": n, "us": round(ms * 1e3, 2), "gbs": round(algo / ms / 1e6, 1),
+            "frac": round(algo / ms / 1e6 / hbm, 4)}
+
+
 def batched_decode(dec, device, hbm, world=1, tokens=32, steps=20):
     """Config 4 at batch 32: a decode batch through all layers, expert-major on
     the tensor cores (each routed expert read once per layer for all its
@@ -549,6 +578,11 @@ def main():
         r = gemv_shape(device, hbm, args.gemv[0], args.gemv[1])
         r.update({"peak_gbs": hbm, "peak_kind": peak_kind})
         print(json.dumps({"gemv": r}))
+        return
+    if args.bf16_tc:
+        r = bf16_tc_shape(device, hbm, *args.bf16_tc)
+        r.update({"peak_gbs": hbm, "peak_kind": peak_kind})
+        print(json.dumps({"bf16_tc": r}))
         return
     if args.gemm_tc:
         r = gemm_tc_shape(device, hbm, *args.gemm_tc)
