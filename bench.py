@@ -453,6 +453,58 @@ def batched_decode(dec, device, hbm, world=1, tokens=32, steps=20):
                     + (", peer-memory exchange" if world > 1 else "")}
 
 
+def qwen_block_b16(device, hbm, tokens=16, layers=48, pools=4, steps=5):
+    """Config 2 at batch 16: the Qwen3-30B-A3B-shaped MoE layer (128 experts,
+    hidden 2048, moe intermediate 768, gate / up rows interleaved, softmax
+    top-8) as the expert-major batched block on the tensor cores with the
+    SwiGLU epilogue, `layers` layers per step cycling over `pools` expert
+    banks of seeded random record bytes (each bank 340 MB, larger than L2),
+    fresh router logits per layer; CUDA graph, device time.  Bytes per step:
+    the distinct (layer, expert) records the routing touches plus the
+    activations."""
+    from ervf_b200.fused_nvfp4 import FusedNVFP4
+
+    H, I, E, K = 2048, 768, 128, 8
+    up_c, up_s = 2 * I * H // 2, 2 * I * H // 16
+    dn_c, dn_s = H * I // 2, H * I // 16
+    g = torch.Generator(device=device)
+    banks = []
+    for p in range(pools):
+        g.manual_seed(9100 + p)
+        rb = lambda n, lo, hi: torch.randint(lo, hi, (n,), generator=g, device=device,
+                                             dtype=torch.int32).to(torch.uint8)
+        banks.append((rb(E * up_c, 0, 256), rb(E * up_s, 0x28, 0x38), rb(E * dn_c, 0, 256),
+                      rb(E * dn_s, 0x28, 0x38), torch.full((E, 2), 1.0 / 64.0, device=device)))
+    g.manual_seed(9200)
+    rlogs = torch.randn(layers, tokens, E, generator=g, device=device)
+    x0 = torch.randn(tokens, H, generator=g, device=device) * 0.1
+    ids = torch.zeros(layers, tokens, K, dtype=torch.int32, device=device)
+    w = torch.zeros(layers, tokens, K, device=device)
+    xs = [torch.empty(tokens, H, device=device) for _ in range(2)]
+    f = FusedNVFP4(device=device)
+
+    def step(i):
+        xs[0].copy_(x0)
+        for l in range(layers):
+            uc, us, dc, ds, gl = banks[l % pools]
+            f.route_topk_softmax(rlogs[l], ids[l], w[l], tokens, E, K)
+            f.moe_batched(uc, us, up_c, up_s, dc, ds, dn_c, dn_s, gl, ids[l], w[l], tokens, K, E,
+                          xs[l % 2], xs[(l + 1) % 2], H, I, swiglu=True)
+
+    step(0)
+    torch.cuda.synchronize(device)
+    distinct = sum(int(torch.unique(ids[l]).numel()) for l in range(layers))
+    rec = up_c + up_s + dn_c + dn_s
+    step_bytes = distinct * rec + layers * tokens * K * (H + I) * 4
+    ms = time_graph(step, steps, device)
+    return {"tokens_per_step": tokens, "layers": layers, "ms_per_step": round(ms, 4),
+            "us_per_layer": round(ms * 1e3 / layers, 2), "tok_s": round(tokens / (ms * 1e-3), 1),
+            "distinct_experts_per_layer": round(distinct / layers, 1), "step_bytes": step_bytes,
+            "gbs": round(step_bytes / ms / 1e6, 1), "frac": round(step_bytes / ms / 1e6 / hbm, 4),
+            "path": "softmax top-8 router + expert-major tcgen05 block, SwiGLU epilogue "
+                    "(tolerance), route-order sum; seeded random record bytes"}
+
+
 def routed_decode(dec, device, hbm, steps=50):
     """Config 4 at batch 1 with the router on the device between the layers
     (per layer: router GEMV fp32 [128 x 2688] + top-k in one launch, then up
@@ -704,7 +756,9 @@ def main():
                  "bf16_gemv_config3": bf16_gemvs(device, hbm),
                  # config 2 batch-16 variant on the tensor cores
                  "gemm_tc_config2_b16": {f"{r}x{c}": gemm_tc_shape(device, hbm, r, c, 16) for r, c in
-                                         ((1536, 2048), (2048, 768))}}
+                                         ((1536, 2048), (2048, 768))},
+                 # the whole config-2 MoE layer at batch 16 on the tensor cores
+                 "qwen_block_b16": qwen_block_b16(device, hbm)}
 
     if rank == 0:
         # bytes one token streams: distinct (layer, expert) pairs x expert bytes
@@ -720,10 +774,11 @@ def main():
                        "exchange": args.exchange if world > 1 else None,
                        "l2": "inputs larger than L2 (17.2 GB bank, 808 MB streamed per token)",
                        "cuda_graph": graph is not None},
-            # router + the one-launch token kernel on one GPU (router + per
-            # layer up, down(+route sum) without it); up, down, exchange(+route
-            # sum) or route sum after the all-gather with N > 1
-            "gpu_launches": ((2 if dec.token else 2 * L + 1) if world == 1 else 3 * L + 1) * args.steps,
+            # router + the one-launch token kernel (on every rank with N > 1:
+            # the expert-parallel token, slot rows exchanged inside it);
+            # without it router + per layer up, down(+route sum) on one GPU,
+            # up, down, exchange(+route sum) with N > 1
+            "gpu_launches": (2 if dec.token else (2 * L + 1 if world == 1 else 3 * L + 1)) * args.steps,
             "token_bytes": token_bytes,
             "token_roofline_frac": (token_bytes / (ms / args.steps / 1e3) / 1e9) / (hbm * world),
             "clocks": clocks,

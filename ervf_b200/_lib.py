@@ -60,6 +60,10 @@ SIGNATURES: dict[str, list] = {
     "ervf_moe_token": [_vp, _i, _sz, _sz, _sz, _sz, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _vp, _sz, _i,
                        _vp],
     "ervf_moe_token_scratch_bytes": [_i, _i, _i, _i],
+    "ervf_moe_token_ep": [_vp, _i, _sz, _sz, _sz, _sz, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _vp, _i,
+                          _i, _sz, _i, _i, _vp],
+    "ervf_moe_token_ep_scratch_bytes": [_i, _i, _i, _i],
+    "ervf_moe_token_ep_prepare": [_vp, _sz, _i, _i, _i, _i, _vp],
     "ervf_moe_token_router": [_vp, _i, _sz, _sz, _sz, _sz, _vp, _vp, _i, _i, _f, _i, _vp, _vp, _i, _i,
                               _vp, _sz, _i, _vp],
     "ervf_moe_down_routesum_static": [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp,
@@ -107,7 +111,7 @@ SIGNATURES: dict[str, list] = {
 }
 
 SIZE_RESULT = {"ervf_routesum_scratch_bytes", "ervf_nvfp4_gemm_tc_scratch_bytes",
-               "ervf_moe_token_scratch_bytes",
+               "ervf_moe_token_scratch_bytes", "ervf_moe_token_ep_scratch_bytes",
                "ervf_moe_batched_scratch_bytes", "ervf_ep_region_bytes"}
 
 _lib = None

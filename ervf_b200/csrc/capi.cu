@@ -410,6 +410,68 @@ size_t ervf_moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top
   return moe_token_scratch_bytes(n_layers, hidden, inter, top_k);
 }
 
+size_t ervf_moe_token_ep_scratch_bytes(int n_layers, int hidden, int inter, int top_k) {
+  if (n_layers <= 0 || hidden <= 0 || inter <= 0 || top_k <= 0) return 0;
+  return moe_token_ep_scratch_bytes(n_layers, hidden, inter, top_k);
+}
+
+int ervf_moe_token_ep_prepare(void* scratch, size_t scratch_bytes, int n_layers, int hidden, int inter,
+                              int top_k, void* stream) {
+  if (!scratch) return kErrNull;
+  if (n_layers <= 0 || hidden <= 0 || inter <= 0 || top_k <= 0) return kErrShape;
+  if (scratch_bytes < moe_token_ep_scratch_bytes(n_layers, hidden, inter, top_k)) return kErrArg;
+  if (!al(scratch, 256)) return kErrAlign;
+  return prepare_moe_token_ep(scratch, n_layers, hidden, inter, top_k, S(stream));
+}
+
+int ervf_moe_token_ep(const uint64_t* layer_ptrs, int n_layers, size_t up_code_stride,
+                      size_t up_scale_stride, size_t dn_code_stride, size_t dn_scale_stride,
+                      const int32_t* ids, const float* route_w, int top_k, int n_experts,
+                      const float* x, float* out, int hidden, int inter, const uint64_t* peer_scratch,
+                      int ep_ranks, int ep_rank, size_t scratch_bytes, int timeout_ms, int flags,
+                      void* stream) {
+  if (!layer_ptrs || !ids || !route_w || !x || !out || !peer_scratch) return kErrNull;
+  if (flags & ~ERVF_LAUNCH_PDL) return kErrArg;
+  if (ep_ranks < 2 || ep_ranks > 8 || ep_rank < 0 || ep_rank >= ep_ranks || timeout_ms <= 0)
+    return kErrArg;
+  if (n_layers <= 0 || top_k <= 0 || top_k > kMaxJobs || n_experts <= 0) return kErrShape;
+  if (hidden <= 0 || inter <= 0 || hidden % 32 || inter % 32 || hidden > 4096 || inter > 4096)
+    return kErrShape;
+  if (scratch_bytes < moe_token_ep_scratch_bytes(n_layers, hidden, inter, top_k)) return kErrArg;
+  for (int q = 0; q < ep_ranks; ++q) {
+    if (!peer_scratch[q]) return kErrNull;
+    if (peer_scratch[q] & 255u) return kErrAlign;
+  }
+  if (!al(x, 16) || !al(out, 4) || !al(layer_ptrs, 8) ||
+      ((up_code_stride | up_scale_stride | dn_code_stride | dn_scale_stride) & 15u))
+    return kErrAlign;
+  const size_t cb = (size_t)inter * hidden / 2, sb = (size_t)inter * hidden / 16;
+  if (up_code_stride < cb || up_scale_stride < sb || dn_code_stride < cb || dn_scale_stride < sb)
+    return kErrArg;
+  MoeTokenArgs a{};
+  a.layer_ptrs = reinterpret_cast<const unsigned long long*>(layer_ptrs);
+  a.up_code_stride = up_code_stride;
+  a.up_scale_stride = up_scale_stride;
+  a.dn_code_stride = dn_code_stride;
+  a.dn_scale_stride = dn_scale_stride;
+  a.ids = ids;
+  a.route_w = route_w;
+  a.x = x;
+  a.out = out;
+  a.n_layers = n_layers;
+  a.top_k = top_k;
+  a.n_experts = n_experts;
+  a.hidden = hidden;
+  a.inter = inter;
+  a.scratch = reinterpret_cast<void*>(peer_scratch[ep_rank]);
+  a.pdl = (flags & ERVF_LAUNCH_PDL) != 0;
+  a.ep_ranks = ep_ranks;
+  a.ep_rank = ep_rank;
+  a.peers = reinterpret_cast<const unsigned long long*>(peer_scratch);
+  a.timeout_ns = (unsigned long long)timeout_ms * 1000000ull;
+  return launch_moe_token(a, S(stream));
+}
+
 size_t ervf_routesum_scratch_bytes(int hidden, int top_k) {
   if (hidden <= 0 || top_k <= 0) return 0;
   return routesum_scratch_bytes(hidden, top_k);

@@ -197,9 +197,19 @@ struct MoeTokenArgs {
   bool route;
   float scaling;
   int bad_pick;
+  // expert parallelism (ep_ranks > 1, given routes only): scratch is this
+  // rank's moe_token_ep_scratch_bytes region, peers[q] (host array) every
+  // rank's region as mapped on this GPU, timeout_ns the limit of the waits
+  // on other ranks
+  int ep_ranks, ep_rank;
+  const unsigned long long* peers;
+  unsigned long long timeout_ns;
 };
 
 size_t moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top_k);
+size_t moe_token_ep_scratch_bytes(int n_layers, int hidden, int inter, int top_k);
+int prepare_moe_token_ep(void* scratch, int n_layers, int hidden, int inter, int top_k,
+                         cudaStream_t stream);
 int launch_moe_token(const MoeTokenArgs& a, cudaStream_t stream);
 
 // Expert-parallel exchange over NVLink peer memory (ep_p2p.cu).  Region

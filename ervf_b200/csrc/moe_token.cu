@@ -69,7 +69,8 @@ static_assert(128 + 16 * kPubRing <= kPubFullOff && kPubFullOff + 8 * kPubRing <
               "publisher ring layout");
 constexpr unsigned kFull = 0xffffffffu;
 
-enum : int { kItemPrep = 0, kItemUp = 1, kItemDown = 2, kItemEnd = 3, kItemRoute = 4 };
+enum : int { kItemPrep = 0, kItemUp = 1, kItemDown = 2, kItemEnd = 3, kItemRoute = 4, kItemSum = 5 };
+constexpr int kTokMaxRanks = 8;  // expert-parallel ranks of one token launch
 constexpr int kRouteRows = kCW;  // router rows per item: one per consumer warp
 constexpr int kTokMaxRouteExperts = 256;  // experts a layer's router items can route
 
@@ -105,7 +106,17 @@ struct TokArgs {
   float* xlin;     // [L][hidden]  x_l (x_0 = the input)
   float* xsw;      // [L][hidden]  x_l in the swizzled unit layout
   float* actsw;    // [2][K][inter] relu^2(up) per slot, swizzled
-  float* contrib;  // [2][K][hidden] down rows per slot
+  float* contrib;  // [2][K][hidden] down rows per slot ([L][K][hidden] with EP)
+  // Expert parallelism (EP instantiation): this rank owns the experts e with
+  // e % ep_n == ep_rank.  peer[q] is rank q's scratch as mapped on this GPU
+  // (peer[ep_rank] = this rank's own); every rank's scratch has the same
+  // layout, so a peer's counters sit at the same offsets as a.ctr's.
+  int ep_n, ep_rank;
+  unsigned long long peer[kTokMaxRanks];
+  size_t contrib_off;              // byte offset of contrib in every rank's scratch
+  size_t hello_off;                // byte offset of the token-entry flags [kTokMaxRanks] (never reset)
+  unsigned* hello;                 // this rank's entry flags; its epoch word 32 words later
+  unsigned long long timeout_ns;   // limit of the waits on other ranks
 };
 
 // Counter words.  The claim counter (hit by every claim), the exit counter
@@ -114,6 +125,8 @@ struct TokArgs {
 constexpr int kCtrLine = 32;
 __device__ __forceinline__ unsigned* ctr_claim(const TokArgs& a) { return a.ctr; }
 __device__ __forceinline__ unsigned* ctr_exited(const TokArgs& a) { return a.ctr + kCtrLine; }
+// EP: set by the first wait on another rank that runs out (same line)
+__device__ __forceinline__ unsigned* ctr_abort(const TokArgs& a) { return a.ctr + kCtrLine + 1; }
 __device__ __forceinline__ unsigned* ctr_xrows(const TokArgs& a, int l) {
   return a.ctr + kCtrLine * (2 + l);
 }
@@ -149,6 +162,11 @@ __host__ __device__ __forceinline__ size_t token_ctr_words(int L, int K, int B) 
 // expert id of every (layer, slot) and its (down, up) global scales -- the
 // producer then forms an item's addresses without a global-memory round trip.
 __host__ __device__ __forceinline__ int token_tab_bytes(int L, int K) { return 36 * L + 12 * L * K; }
+// With EP the table is followed by this rank's slot lists: owned slots
+// [L][K], item offsets of the layers [L + 1], owned-slot counts [L], total.
+__host__ __device__ __forceinline__ int token_tab_bytes_ep(int L, int K) {
+  return token_tab_bytes(L, K) + 4 * (L * K + 2 * L + 2);
+}
 
 // Float index of column j in the swizzled unit layout that x_slot / the
 // consumers use: unit t = j / 32 holds 8 float4 slots, slot k =
@@ -193,6 +211,46 @@ __device__ __forceinline__ void decode_item(const TokArgs& a, int idx, int& kind
   nrows = min(ph->krt, ph->rows - r0);
 }
 
+// EP: this rank's items.  Per layer l (item offset loff[l]): the UP items
+// of the slots it owns (own[l][0 .. nown[l]), in route order), their DOWN
+// items, then one SUM item per down row block (the route-order sum of that
+// block from every rank's slot rows).  `hint` is the layer of the caller's
+// previous decode (claims only grow).
+__device__ __forceinline__ void decode_item_ep(const TokArgs& a, const int* own, const int* loff,
+                                               const int* nown, int idx, int& hint, int& kind,
+                                               int& l, int& slot, int& r0, int& nrows) {
+  if (idx == 0) {
+    kind = kItemPrep;
+    l = slot = r0 = nrows = 0;
+    return;
+  }
+  const int i = idx - 1;
+  int ll = hint;
+  while (ll > 0 && i < loff[ll]) --ll;
+  while (ll + 1 < a.L && i >= loff[ll + 1]) ++ll;
+  hint = ll;
+  l = ll;
+  int j = i - loff[ll];
+  const int nu = nown[ll] * a.up.n_items, nd = nown[ll] * a.dn.n_items;
+  if (j < nu) {
+    kind = kItemUp;
+    slot = own[ll * a.K + j / a.up.n_items];
+    r0 = (j % a.up.n_items) * a.up.krt;
+    nrows = min(a.up.krt, a.up.rows - r0);
+  } else if (j < nu + nd) {
+    j -= nu;
+    kind = kItemDown;
+    slot = own[ll * a.K + j / a.dn.n_items];
+    r0 = (j % a.dn.n_items) * a.dn.krt;
+    nrows = min(a.dn.krt, a.dn.rows - r0);
+  } else {
+    kind = kItemSum;
+    slot = 0;
+    r0 = (j - nu - nd) * a.dn.krt;
+    nrows = min(a.dn.krt, a.hidden - r0);
+  }
+}
+
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -201,6 +259,62 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
 
 __device__ __forceinline__ void red_release_gpu(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Relaxed system-scope accesses of the slot rows other GPUs write.
+__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_relaxed_sys(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// EP: a contrib word not yet written for this token holds this pattern (a
+// NaN that no arithmetic result has: GPU arithmetic returns the canonical NaN
+// 0x7FFFFFFF); a row value with these bits is stored as 0x7FFFFFFF, which
+// gives the same (canonical NaN) route sum.
+constexpr unsigned kUnwritten = 0xFFFFFFFFu;
+
+__device__ __forceinline__ unsigned long long globaltimer_tok() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait until *p >= target for a counter that other GPUs add to
+// (acquire at system scope): false after timeout_ns (or 2^28 polls), and at
+// once when another wait of the launch has run out (*abort, zeroed with the
+// counters when the launch ends), so that a rank that never arrives costs
+// one timeout, not one per wait.
+__device__ __forceinline__ bool wait_count_sys(const unsigned* p, unsigned target,
+                                               unsigned long long timeout_ns, unsigned* abort) {
+  if (ld_acquire_sys(p) >= target) return true;
+  const unsigned long long t0 = globaltimer_tok();
+  for (unsigned it = 0;; ++it) {
+    if (ld_acquire_sys(p) >= target) return true;
+    if ((it & 15u) == 15u) {
+      if (*reinterpret_cast<volatile unsigned*>(abort)) return false;
+      if (it >= (1u << 28) || globaltimer_tok() - t0 > timeout_ns) {
+        atomicExch(&g_device_error, kErrTimeout);
+        atomicExch(abort, 1u);
+        return false;
+      }
+    }
+    nanosleep_ns(64);
+  }
 }
 
 // Orders this thread's generic-proxy view of global memory with its
@@ -283,7 +397,8 @@ __device__ __forceinline__ SegPlace seg_place(const TokPhase& ph, int tid) {
 
 // ROUTE: the launch has router items (ervf_moe_token_router); the plain
 // instantiation carries no router code at all.
-template <int H, bool ROUTE>
+// EP: expert-parallel rank of a token (given routes only; see TokArgs).
+template <int H, bool ROUTE, bool EP>
 __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_constant__ TokArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_last;
@@ -304,6 +419,11 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
   float2* tab_g = reinterpret_cast<float2*>(smem + kTabOff + 32 * a.L);                 // [L][K]
   int* tab_id = reinterpret_cast<int*>(smem + kTabOff + 32 * a.L + 8 * a.L * a.K);       // [L][K]
   int* tab_ok = tab_id + a.L * a.K;  // [L]: the layer's (id, g) entries are filled
+  // EP: this rank's slot lists (token_tab_bytes_ep)
+  int* ep_own = tab_ok + a.L;           // [L][K]
+  int* ep_loff = ep_own + a.L * a.K;    // [L + 1]
+  int* ep_nown = ep_loff + a.L + 1;     // [L]
+  int* ep_total = ep_nown + a.L;        // [1]
   uint8_t* stages = smem + a.stage_base;
 
   if (tid == 0) {
@@ -325,6 +445,22 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
     tab_id[i] = e;
     tab_g[i] = make_float2(gl[2 * e], gl[2 * e + 1]);
   }
+  if (EP) {
+    __syncthreads();
+    if (tid == 0) {
+      int off = 0;
+      for (int l = 0; l < a.L; ++l) {
+        int n = 0;
+        for (int s2 = 0; s2 < a.K; ++s2)
+          if (tab_id[l * a.K + s2] % a.ep_n == a.ep_rank) ep_own[l * a.K + n++] = s2;
+        ep_nown[l] = n;
+        ep_loff[l] = off;
+        off += n * (a.up.n_items + a.dn.n_items) + a.B;
+      }
+      ep_loff[a.L] = off;
+      *ep_total = 1 + off;
+    }
+  }
   __syncthreads();
 
   if (tid >= kProd && tid < kPub) {
@@ -336,16 +472,85 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
     // round trip is off the path from a free stage to its copies
     int next = 0;
     if (lane == 0) next = (int)atomicAdd(ctr_claim(a), 1u);
+    const int total = EP ? *ep_total : a.total;
+    int hint = 0;  // EP: layer of the last decode
     for (;;) {
+      if (EP) {
+        // a SUM item takes no stage: the producer warp runs it here.  Once
+        // every rank's slot rows of the block are in (count K, released by
+        // the owners' publishers at system scope), the route-order sum of
+        // the block: acc = fmaf(y_s, w_s, acc) over s = 0..K-1 from 0 and
+        // x_{l+1} = x_l + acc, the arithmetic of the one-GPU path.
+        const int idx0 = __shfl_sync(kFull, next, 0);
+        if (idx0 < total) {
+          int kind0, l0, s0, q0, n0;
+          decode_item_ep(a, ep_own, ep_loff, ep_nown, idx0, hint, kind0, l0, s0, q0, n0);
+          if (kind0 == kItemSum) {
+            if (lane == 0) {
+              next = (int)atomicAdd(ctr_claim(a), 1u);
+              // (a wait that runs out records kErrTimeout; the sum goes on)
+              // x_l of the block's rows is this rank's own (its SUM items of
+              // layer l - 1): with no slot of layer l here, nothing else
+              // orders them before this sum
+              wait_count_sys(ctr_xrows(a, l0), (unsigned)a.hidden, a.timeout_ns, ctr_abort(a));
+            }
+            __syncwarp();
+            const int r = q0 + lane;
+            if (lane < n0) {
+              // every slot's word of this row, written by its owner (peer
+              // stores, no fence): wait until none is unwritten, sum in
+              // route order, then mark the words unwritten for the next
+              // token (peers write them again only after every rank has
+              // entered that token)
+              unsigned* cw = reinterpret_cast<unsigned*>(a.contrib) + (size_t)l0 * a.K * a.hidden + r;
+              const unsigned long long t0 = globaltimer_tok();
+              unsigned polls = 0;
+              for (int s2 = 0; s2 < a.K;) {
+                if (ld_relaxed_sys(cw + (size_t)s2 * a.hidden) != kUnwritten) {
+                  ++s2;
+                  continue;
+                }
+                if ((++polls & 15u) == 0u) {
+                  if (*reinterpret_cast<volatile unsigned*>(ctr_abort(a))) break;
+                  if (polls >= (1u << 28) || globaltimer_tok() - t0 > a.timeout_ns) {
+                    atomicExch(&g_device_error, kErrTimeout);
+                    atomicExch(ctr_abort(a), 1u);
+                    break;
+                  }
+                }
+                nanosleep_ns(32);
+              }
+              float acc = 0.0f;
+              for (int s2 = 0; s2 < a.K; ++s2)
+                acc = fmaf(__uint_as_float(ld_relaxed_sys(cw + (size_t)s2 * a.hidden)),
+                           a.route_w[l0 * a.K + s2], acc);
+              for (int s2 = 0; s2 < a.K; ++s2) cw[(size_t)s2 * a.hidden] = kUnwritten;
+              const float xv = __ldcg(a.xlin + (size_t)l0 * a.hidden + r) + acc;
+              if (l0 + 1 < a.L) {
+                a.xlin[(size_t)(l0 + 1) * a.hidden + r] = xv;
+                a.xsw[(size_t)(l0 + 1) * a.hidden + sw_index(r)] = xv;
+              } else {
+                a.out[r] = xv;
+              }
+            }
+            __syncwarp();
+            if (lane == 0 && l0 + 1 < a.L) red_release_gpu(ctr_xrows(a, l0 + 1), (unsigned)n0);
+            continue;
+          }
+        }
+      }
       const int st = it % S;
       uint8_t* sp = stages + (size_t)st * a.stage_bytes;
       if (lane == 0) ok = mbar_wait(&empty[st], ((it / S) & 1) ^ 1);
       ok = __shfl_sync(kFull, ok, 0);
       if (!ok) break;
       const int idx = __shfl_sync(kFull, next, 0);
-      if (idx >= a.total) break;
+      if (idx >= total) break;
       int kind, l, slot, r0, nrows;
-      decode_item(a, idx, kind, l, slot, r0, nrows);
+      if (EP)
+        decode_item_ep(a, ep_own, ep_loff, ep_nown, idx, hint, kind, l, slot, r0, nrows);
+      else
+        decode_item(a, idx, kind, l, slot, r0, nrows);
       int* hdr = reinterpret_cast<int*>(sp);
       if (ROUTE && kind == kItemRoute) {
         // router rows: no weights to stage (the consumer warps read them
@@ -438,10 +643,13 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
         }
         if (s16) bulk_g2s(codes + ph.scale_off, ssrc, s16, &full[st]);
         next = (int)atomicAdd(ctr_claim(a), 1u);
-        if (a.prefetch && next < a.total) {
+        if (a.prefetch && next < total) {
           // its weight rows stream from HBM into L2 while this item waits
           int k2, l2, s2, q0, n2;
-          decode_item(a, next, k2, l2, s2, q0, n2);
+          if (EP)
+            decode_item_ep(a, ep_own, ep_loff, ep_nown, next, hint, k2, l2, s2, q0, n2);
+          else
+            decode_item(a, next, k2, l2, s2, q0, n2);
           if ((k2 == kItemUp || k2 == kItemDown) && (!ROUTE || tab_ok[l2])) {
             const bool up2 = k2 == kItemUp;
             const TokPhase& p2 = up2 ? a.up : a.dn;
@@ -499,6 +707,21 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
       // then bulk copy (after a proxy fence) or load with __ldcg.
       const float y = lane < nrows ? yv[lane] : 0.0f;
       if (kind == kItemPrep) {
+        if (EP) {
+          // Every rank enters the token before any slot row moves: a rank's
+          // counters are zeroed when its previous token ends, and no peer may
+          // add to them before.  Token t (this rank's epoch word, counted by
+          // its last CTA) writes t + 1 into entry[ep_rank] of every rank's
+          // entry flags (never reset; each entry has one writer, so a later
+          // token of one rank cannot stand in for another rank's entry),
+          // then lane q waits for entry[q] >= t + 1 here.
+          const unsigned epoch = *reinterpret_cast<volatile unsigned*>(a.hello + kCtrLine);
+          if (lane < a.ep_n) {
+            st_release_sys(reinterpret_cast<unsigned*>(a.peer[lane] + a.hello_off) + a.ep_rank, epoch + 1u);
+            wait_count_sys(a.hello + lane, epoch + 1u, a.timeout_ns, ctr_abort(a));
+          }
+          __syncwarp();
+        }
         if (lane == 0) red_release_gpu(ctr_xrows(a, 0), (unsigned)a.hidden);  // stores fenced by the consumers
       } else if (ROUTE && kind == kItemRoute) {
         // router logits.  The layer's last router item (claimed after the
@@ -529,6 +752,18 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
         }
         __syncwarp();
         if (lane == 0) red_release_gpu(ctr_act(a, l, slot), (unsigned)nrows);
+      } else if (EP) {
+        // a down block of an owned slot: its rows into every rank's
+        // contrib[l][slot] (peer stores over NVLink).  No fence and no
+        // counter: each word arrives whole, and the SUM items wait for the
+        // words themselves (see kUnwritten)
+        if (lane < nrows) {
+          const size_t at = ((size_t)l * a.K + slot) * a.hidden + r0 + lane;
+          unsigned u = __float_as_uint(y);
+          if (u == kUnwritten) u = 0x7FFFFFFFu;
+          for (int q2 = 0; q2 < a.ep_n; ++q2)
+            st_relaxed_sys(reinterpret_cast<unsigned*>(a.peer[q2] + a.contrib_off) + at, u);
+        }
       } else if (slot + 1 < a.K) {
         // a down block of slots 0..K-2: its rows, then the block's count
         if (lane < nrows) a.contrib[((size_t)(l & 1) * a.K + slot) * a.hidden + r0 + lane] = y;
@@ -674,6 +909,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(const __grid_
   if (s_last) {
     __threadfence();
     for (int i = tid; i < a.n_ctr; i += kTokThreads) a.ctr[i] = 0u;
+    if (EP && tid == 0) atomicAdd(a.hello + kCtrLine, 1u);  // this rank's next token
   }
 }
 
@@ -716,13 +952,13 @@ int set_smem_tok(K kernel, int bytes) {
   return kOk;
 }
 
-template <int H, bool ROUTE>
+template <int H, bool ROUTE, bool EP = false>
 int launch_token_h(const TokArgs& a, int smem, bool pdl, cudaStream_t stream) {
-  if (set_smem_tok(moe_token_kernel<H, ROUTE>, smem)) return kErrLaunch;
+  if (set_smem_tok(moe_token_kernel<H, ROUTE, EP>, smem)) return kErrLaunch;
   int dev = 0, sms = 0, occ = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, moe_token_kernel<H, ROUTE>, kTokThreads, smem) !=
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, moe_token_kernel<H, ROUTE, EP>, kTokThreads, smem) !=
       cudaSuccess)
     return kErrLaunch;
   if (occ < 1) return kErrShape;
@@ -737,7 +973,7 @@ int launch_token_h(const TokArgs& a, int smem, bool pdl, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, moe_token_kernel<H, ROUTE>, a) == cudaSuccess ? kOk : kErrLaunch;
+  return cudaLaunchKernelEx(&cfg, moe_token_kernel<H, ROUTE, EP>, a) == cudaSuccess ? kOk : kErrLaunch;
 }
 
 }  // namespace
@@ -747,6 +983,31 @@ size_t moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top_k) {
   const size_t ctr = (n_ctr * 4 + 255) / 256 * 256;
   return ctr + 4 * ((size_t)2 * n_layers * hidden + (size_t)2 * top_k * inter + (size_t)2 * top_k * hidden +
                     (size_t)n_layers * kTokMaxRouteExperts);
+}
+
+// EP scratch (the same on every rank): counters, the token-entry flags and
+// the epoch word (256 bytes, never reset), x_l linear and swizzled [L][hidden], act
+// [2][K][inter], contrib [L][K][hidden].
+size_t moe_token_ep_contrib_offset(int n_layers, int hidden, int inter, int top_k) {
+  const size_t n_ctr = token_ctr_words(n_layers, top_k, hidden / 2);
+  const size_t ctr = (n_ctr * 4 + 255) / 256 * 256;
+  return ctr + 256 + 4 * ((size_t)2 * n_layers * hidden + (size_t)2 * top_k * inter);
+}
+
+size_t moe_token_ep_scratch_bytes(int n_layers, int hidden, int inter, int top_k) {
+  return moe_token_ep_contrib_offset(n_layers, hidden, inter, top_k) +
+         4 * (size_t)n_layers * top_k * hidden;
+}
+
+// Counters, entry flags and epoch zero; every contrib word unwritten.
+int prepare_moe_token_ep(void* scratch, int n_layers, int hidden, int inter, int top_k,
+                         cudaStream_t stream) {
+  const size_t off = moe_token_ep_contrib_offset(n_layers, hidden, inter, top_k);
+  const size_t n = moe_token_ep_scratch_bytes(n_layers, hidden, inter, top_k) - off;
+  if (cudaMemsetAsync(scratch, 0, off, stream) != cudaSuccess ||
+      cudaMemsetAsync(reinterpret_cast<uint8_t*>(scratch) + off, 0xFF, n, stream) != cudaSuccess)
+    return kErrLaunch;
+  return kOk;
 }
 
 int launch_moe_token(const MoeTokenArgs& in, cudaStream_t stream) {
@@ -771,6 +1032,10 @@ int launch_moe_token(const MoeTokenArgs& in, cudaStream_t stream) {
   a.inter = in.inter;
   a.up = make_phase(in.inter, in.hidden);
   a.dn = make_phase(in.hidden, in.inter);
+  const bool ep = in.ep_ranks > 1;
+  if (ep && (a.route || in.ep_ranks > kTokMaxRanks || in.ep_rank < 0 || in.ep_rank >= in.ep_ranks ||
+             !in.peers))
+    return kErrArg;
   const int blk_u = row_block_tok(in.hidden), blk_d = row_block_tok(in.inter);
 
   int dev = 0, smem_sm = 0;
@@ -795,7 +1060,8 @@ int launch_moe_token(const MoeTokenArgs& in, cudaStream_t stream) {
     const int wd = kd * a.dn.cb + align_up_tok(kd * a.dn.sb, 16);
     const int stage = align_up_tok(codes_off + (wu > wd ? wu : wd), 128);
     const int kmax = ku > kd ? ku : kd;
-    const int part_off = align_up_tok(kTabOff + token_tab_bytes(in.n_layers, in.top_k), 128);
+    const int tab = ep ? token_tab_bytes_ep(in.n_layers, in.top_k) : token_tab_bytes(in.n_layers, in.top_k);
+    const int part_off = align_up_tok(kTabOff + tab, 128);
     const int base = align_up_tok(part_off + kmax * kRowPitch * 4, 128);
     int stages = (budget - base) / stage;
     if (stages > kTokMaxStages) stages = kTokMaxStages;
@@ -828,6 +1094,31 @@ int launch_moe_token(const MoeTokenArgs& in, cudaStream_t stream) {
   a.n_ctr = (int)token_ctr_words(a.L, a.K, a.B);
   a.ctr = reinterpret_cast<unsigned*>(s);
   s += (token_ctr_words(a.L, a.K, a.hidden / 2) * 4 + 255) / 256 * 256;
+  if (ep) {
+    const uint8_t* base = reinterpret_cast<const uint8_t*>(in.scratch);
+    a.ep_n = in.ep_ranks;
+    a.ep_rank = in.ep_rank;
+    for (int q = 0; q < in.ep_ranks; ++q) a.peer[q] = in.peers[q];
+    a.hello = reinterpret_cast<unsigned*>(s);
+    a.hello_off = (size_t)(s - base);
+    a.timeout_ns = in.timeout_ns;
+    s += 256;
+    a.xlin = reinterpret_cast<float*>(s);
+    s += (size_t)4 * a.L * a.hidden;
+    a.xsw = reinterpret_cast<float*>(s);
+    s += (size_t)4 * a.L * a.hidden;
+    a.actsw = reinterpret_cast<float*>(s);
+    s += (size_t)4 * 2 * a.K * a.inter;
+    a.contrib = reinterpret_cast<float*>(s);
+    a.contrib_off = (size_t)(s - base);
+    a.rlog = nullptr;
+    switch (h) {
+      case 4: return launch_token_h<4, false, true>(a, smem, in.pdl, stream);
+      case 3: return launch_token_h<3, false, true>(a, smem, in.pdl, stream);
+      case 2: return launch_token_h<2, false, true>(a, smem, in.pdl, stream);
+      default: return launch_token_h<1, false, true>(a, smem, in.pdl, stream);
+    }
+  }
   a.xlin = reinterpret_cast<float*>(s);
   s += (size_t)4 * a.L * a.hidden;
   a.xsw = reinterpret_cast<float*>(s);

@@ -45,7 +45,8 @@ class PeerExchange:
     frees the own region.
     """
 
-    def __init__(self, group, world: int, rank: int, hidden: int, n_slots: int, device):
+    def __init__(self, group, world: int, rank: int, hidden: int, n_slots: int, device,
+                 nbytes: int | None = None):
         import ctypes
 
         import torch
@@ -56,7 +57,8 @@ class PeerExchange:
         self.world, self.rank, self.hidden, self.n_slots = world, rank, hidden, n_slots
         self.group, self.device = group, device
         lib = _lib.load()
-        self.nbytes = int(lib.ervf_ep_region_bytes(hidden, n_slots))
+        # nbytes: a region of another layout (the one-launch token's scratch)
+        self.nbytes = int(lib.ervf_ep_region_bytes(hidden, n_slots)) if nbytes is None else int(nbytes)
         if self.nbytes == 0:
             raise ValueError("unsupported exchange shape")
         own = ctypes.c_void_p()

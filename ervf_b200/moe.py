@@ -29,6 +29,8 @@ rank's result is bit-identical to one GPU.
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import torch
 
@@ -170,19 +172,45 @@ class MoEDecoder:
         # One launch per token on one GPU (ervf_moe_token: every layer's up
         # and down rows as one claimed work list, bit-identical to the
         # per-layer launches); False runs the per-layer launches.
-        self.token = ep_ranks == 1
+        # With expert parallelism over peer memory (exchange "p2p", up to 8
+        # ranks) the token is one launch per rank too (ervf_moe_token_ep: each
+        # rank's slot rows go to every rank over NVLink inside the launch),
+        # bit-identical to one GPU; False runs the per-layer launches and one
+        # exchange kernel per layer.
+        self.token = ep_ranks == 1 or (exchange == "p2p" and ep_ranks <= 8)
         # step_with_router in one launch too (router items inside the token
         # kernel): bit-identical to the per-layer router + expert launches and,
         # on B200, 0.896 ms per 24-layer token against 0.930 ms for them
-        self.token_router = self.token
-        self.layer_ptrs = self.tok_scratch = None
+        self.token_router = ep_ranks == 1
+        self.layer_ptrs = self.tok_scratch = self.tok_xchg = None
         if self.token:
             addrs = ([ptr(t) for t in bank.up_codes] + [ptr(t) for t in bank.up_scales]
                      + [ptr(t) for t in bank.dn_codes] + [ptr(t) for t in bank.dn_scales]
                      + [ptr(t) for t in bank.globals])
             self.layer_ptrs = torch.tensor(addrs, dtype=torch.int64, device=d)
-            nb = _lib.load().ervf_moe_token_scratch_bytes(L, bank.hidden, bank.inter, k)
-            self.tok_scratch = torch.zeros(nb, dtype=torch.uint8, device=d)
+            if ep_ranks == 1:
+                nb = _lib.load().ervf_moe_token_scratch_bytes(L, bank.hidden, bank.inter, k)
+                self.tok_scratch = torch.zeros(nb, dtype=torch.uint8, device=d)
+            else:
+                from .ep import PeerExchange
+
+                nb = int(_lib.load().ervf_moe_token_ep_scratch_bytes(L, bank.hidden, bank.inter, k))
+                # every rank's token scratch, mapped on this GPU (CUDA IPC)
+                self.tok_xchg = PeerExchange(group, ep_ranks, ep_rank, bank.hidden, k, d, nbytes=nb)
+                self._tok_peers = (ctypes.c_uint64 * ep_ranks)(*self.tok_xchg.peers.cpu().tolist())
+                self.prepare_token_ep()
+
+    def prepare_token_ep(self) -> None:
+        """Resets this rank's expert-parallel token scratch (counters, entry
+        flags, unwritten slot rows) and waits until every rank has: before the
+        first token, and on every rank after a timeout.  Collective."""
+        import torch.distributed as dist
+
+        b = self.bank
+        _lib.call("ervf_moe_token_ep_prepare", self.tok_xchg.own, self.tok_xchg.nbytes, b.n_layers,
+                  b.hidden, b.inter, self.top_k, self._s())
+        torch.cuda.synchronize(b.device)
+        dist.barrier(group=self.group)
 
     def _s(self) -> int:
         return int(torch.cuda.current_stream(self.bank.device).cuda_stream)
@@ -250,6 +278,9 @@ class MoEDecoder:
         if self._bxchg is not None:
             self._bxchg.close()
             self._bxchg = None
+        if self.tok_xchg is not None:
+            self.tok_xchg.close()
+            self.tok_xchg = None
 
     def step_batch(self, x_in: torch.Tensor, rlogs: torch.Tensor) -> torch.Tensor:
         """A decode batch of T tokens through every layer, expert-major on the
@@ -347,9 +378,12 @@ class MoEDecoder:
         router logits of every layer.  Returns the buffer holding x after
         the last layer."""
         self.route(rlogs)
-        if self.token and self.ep_ranks == 1:
+        if self.token:
             out = self.xs[(self.bank.n_layers - 1) & 1]
-            self.token_step(x_in, out)
+            if self.ep_ranks == 1:
+                self.token_step(x_in, out)
+            else:
+                self.token_step_ep(x_in, out)
             return out
         cur = x_in
         for l in range(self.bank.n_layers):
@@ -395,6 +429,19 @@ class MoEDecoder:
                   int(b.up_scale_bytes), int(b.dn_code_bytes), int(b.dn_scale_bytes), ptr(self.ids),
                   ptr(self.w), self.top_k, b.n_experts, float(np.float32(self.scaling)), 0, ptr(x_in),
                   ptr(out), b.hidden, b.inter, ptr(self.tok_scratch), self.tok_scratch.numel(),
+                  _lib.LAUNCH_PDL if self.pdl else 0, self._s())
+
+    def token_step_ep(self, x_in: torch.Tensor, out: torch.Tensor) -> None:
+        """Every layer of one token in one launch on this rank of the
+        expert-parallel group (ervf_moe_token_ep), routes in self.ids /
+        self.w: every rank ends with the same out, bit-identical to one GPU.
+        Every rank must run the same tokens in the same order."""
+        b = self.bank
+        _lib.call("ervf_moe_token_ep", ptr(self.layer_ptrs), b.n_layers, int(b.up_code_bytes),
+                  int(b.up_scale_bytes), int(b.dn_code_bytes), int(b.dn_scale_bytes), ptr(self.ids),
+                  ptr(self.w), self.top_k, b.n_experts, ptr(x_in), ptr(out), b.hidden, b.inter,
+                  ctypes.cast(self._tok_peers, ctypes.c_void_p), self.ep_ranks, self.ep_rank,
+                  self.tok_xchg.nbytes, self.exchange_timeout_ms,
                   _lib.LAUNCH_PDL if self.pdl else 0, self._s())
 
     def token_step(self, x_in: torch.Tensor, out: torch.Tensor, ids: torch.Tensor | None = None,

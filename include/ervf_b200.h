@@ -208,6 +208,40 @@ ERVF_API int ervf_moe_token_router(const uint64_t* layer_ptrs, int n_layers, siz
 /* Bytes of scratch ervf_moe_token uses (counters and per-layer activations). */
 ERVF_API size_t ervf_moe_token_scratch_bytes(int n_layers, int hidden, int inter, int top_k);
 
+/* ervf_moe_token on one rank of ep_ranks (2..8) GPUs, experts sharded by id:
+ * this rank runs the up / down rows of the route slots whose expert it owns
+ * (ids[l][s] % ep_ranks == ep_rank; the bank holds at least those records,
+ * indexed by the global id), stores each down row into every rank's scratch
+ * over NVLink (peer stores, then a system-scope release of the block's count
+ * on every rank; no NCCL call, no multicast) and sums every row block of
+ * every layer itself, in route order, once all ranks' slot rows are in: every
+ * rank ends with the same out, bit-identical to ervf_moe_token on one GPU.
+ * The slot rows cross NVLink as plain peer stores (no fence, no counter):
+ * the summing rank waits for the words themselves, which hold 0xFFFFFFFF
+ * until written (a NaN pattern no arithmetic produces), and marks them
+ * unwritten again after its sum; one entry handshake per token keeps a fast
+ * rank from writing the next token's rows before every rank has entered it.
+ * peer_scratch: host array [ep_ranks] of every rank's scratch as mapped on
+ * this GPU (entry ep_rank = this rank's own; the others through CUDA IPC,
+ * ervf_ep_region_alloc / _open), each ervf_moe_token_ep_scratch_bytes long
+ * and 256-byte aligned; ervf_moe_token_ep_prepare must have run on every
+ * rank's scratch (and completed) before any rank's first token.  Every rank
+ * launches the same tokens with the same ids and route_w, in the same order;
+ * a wait on another rank gives up after timeout_ms (ERVF_ERR_TIMEOUT in
+ * ervf_device_status; prepare every rank's scratch again before the next
+ * token).  The reference is single-GPU; this is its routed block
+ * (runtime.py:705-746) expert-parallel, route-order contract
+ * runtime.py:588-596. */
+ERVF_API size_t ervf_moe_token_ep_scratch_bytes(int n_layers, int hidden, int inter, int top_k);
+ERVF_API int ervf_moe_token_ep_prepare(void* scratch, size_t scratch_bytes, int n_layers, int hidden,
+                                       int inter, int top_k, void* stream);
+ERVF_API int ervf_moe_token_ep(const uint64_t* layer_ptrs, int n_layers, size_t up_code_stride,
+                               size_t up_scale_stride, size_t dn_code_stride,
+                               size_t dn_scale_stride, const int32_t* ids, const float* route_w,
+                               int top_k, int n_experts, const float* x, float* out, int hidden,
+                               int inter, const uint64_t* peer_scratch, int ep_ranks, int ep_rank,
+                               size_t scratch_bytes, int timeout_ms, int flags, void* stream);
+
 /* ervf_moe_down_routesum without a scratch argument.  No counterpart in the
  * reference.  The scratch is a fixed device array inside the library, so the
  * call allocates nothing: hidden <= 8192 and top_k <= 8, else

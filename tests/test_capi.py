@@ -77,3 +77,36 @@ def test_token_entries_check_arguments_without_a_device():
     assert lib.ervf_moe_token_router(*r, 512, 1.0, 0, *tail) == _lib.ERR_SHAPE   # > 256 experts
     assert lib.ervf_moe_token_router(*r, 128, 1.0, 2, *tail) == _lib.ERR_ARG     # bad_pick
     assert lib.ervf_moe_token_router(*r, 4, 1.0, 0, *tail) == _lib.ERR_SHAPE     # top_k > experts
+
+
+def test_token_ep_entry_checks_arguments_without_a_device():
+    """ervf_moe_token_ep rejects bad rank counts, peer tables and sizes before
+    any CUDA call (the launch itself needs two or more GPUs)."""
+    lib = _lib.load()
+    nb = lib.ervf_moe_token_ep_scratch_bytes(24, 2688, 1856, 6)
+    assert nb > 0
+    assert lib.ervf_moe_token_ep_scratch_bytes(24, 2688, 1856, 0) == 0
+    buf = ctypes.create_string_buffer(4096)
+    p = ctypes.addressof(buf)
+    peers = (ctypes.c_uint64 * 2)(0x10000, 0x20000)
+    pp = ctypes.cast(peers, ctypes.c_void_p)
+    head = (p, 24, 2688 * 1856 // 2, 2688 * 1856 // 16, 2688 * 1856 // 2, 2688 * 1856 // 16, p, p, 6, 128,
+            p, p, 2688, 1856)
+
+    def call(peer=pp, ranks=2, rank=0, nbytes=nb, timeout=5000, flags=0, hd=head):
+        return lib.ervf_moe_token_ep(*hd, peer, ranks, rank, nbytes, timeout, flags, None)
+
+    assert call(peer=None) == _lib.ERR_NULL
+    assert call(ranks=1) == _lib.ERR_ARG      # one rank: ervf_moe_token
+    assert call(ranks=9) == _lib.ERR_ARG      # at most 8 ranks
+    assert call(rank=2) == _lib.ERR_ARG       # rank outside the group
+    assert call(timeout=0) == _lib.ERR_ARG
+    assert call(flags=0x40) == _lib.ERR_ARG   # unknown flag
+    assert call(nbytes=nb - 1) == _lib.ERR_ARG  # scratch too small
+    bad = list(head)
+    bad[12] = 100                             # hidden not a multiple of 32
+    assert call(hd=tuple(bad)) == _lib.ERR_SHAPE
+    zero = (ctypes.c_uint64 * 2)(0x10000, 0)
+    assert call(peer=ctypes.cast(zero, ctypes.c_void_p)) == _lib.ERR_NULL
+    odd = (ctypes.c_uint64 * 2)(0x10000, 0x20010)
+    assert call(peer=ctypes.cast(odd, ctypes.c_void_p)) == _lib.ERR_ALIGN

@@ -9,9 +9,10 @@ limit, reports ERVF_ERR_TIMEOUT and leaves the context usable.
 The batched block as one rank equals ervf_moe_batched bit for bit.
 
 Two or more GPUs (skipped otherwise): one process per GPU over NCCL, experts
-sharded by id, every layer's slots exchanged over NVLink; each rank's x after
-every layer must equal one GPU's bit for bit, eager and in a CUDA graph, and
-the batched block's likewise.
+sharded by id, every layer's slots exchanged over NVLink -- inside the
+one-launch token kernel (ervf_moe_token_ep) and by the per-layer exchange
+kernel; each rank's x after the last layer must equal one GPU's bit for bit,
+eager and in a CUDA graph, and the batched block's likewise.
 """
 
 from __future__ import annotations
@@ -238,30 +239,35 @@ def _worker(rank, world, port, q):
         bad = []
         x_in = torch.zeros(HIDDEN, device=dev)
         r_in = torch.zeros(L, E, device=dev)
-        for t in range(2):  # eager steps
-            x_in.copy_(xs[t])
-            r_in.copy_(rls[t])
-            want = one.step(x_in, r_in).clone()
-            got = ep.step(x_in, r_in).clone()
-            torch.cuda.synchronize()
-            if not torch.equal(want.view(torch.int32), got.view(torch.int32)):
-                bad.append(("eager", t))
-        graph = torch.cuda.CUDAGraph()
-        s = torch.cuda.Stream(dev)
-        s.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(s):
-            ep.step(x_in, r_in)
-        torch.cuda.current_stream(dev).wait_stream(s)
-        with torch.cuda.graph(graph):
-            y = ep.step(x_in, r_in)
-        for t in range(2, 4):
-            x_in.copy_(xs[t])
-            r_in.copy_(rls[t])
-            want = one.step(x_in, r_in).clone()
-            graph.replay()
-            torch.cuda.synchronize()
-            if not torch.equal(want.view(torch.int32), y.view(torch.int32)):
-                bad.append(("graph", t))
+        # the one-launch token (ervf_moe_token_ep, the default) and the
+        # per-layer launches with one exchange kernel per layer
+        for token in (True, False):
+            ep.token = token
+            for t in range(2):  # eager steps
+                x_in.copy_(xs[t])
+                r_in.copy_(rls[t])
+                want = one.step(x_in, r_in).clone()
+                got = ep.step(x_in, r_in).clone()
+                torch.cuda.synchronize()
+                if not torch.equal(want.view(torch.int32), got.view(torch.int32)):
+                    bad.append(("eager", token, t))
+            graph = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream(dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s):
+                ep.step(x_in, r_in)
+            torch.cuda.current_stream(dev).wait_stream(s)
+            with torch.cuda.graph(graph):
+                y = ep.step(x_in, r_in)
+            for t in range(2, 4):
+                x_in.copy_(xs[t])
+                r_in.copy_(rls[t])
+                want = one.step(x_in, r_in).clone()
+                graph.replay()
+                torch.cuda.synchronize()
+                if not torch.equal(want.view(torch.int32), y.view(torch.int32)):
+                    bad.append(("graph", token, t))
+            del graph
         # the batched block (expert-major, tensor cores), odd layer count; the
         # same K-split on both sides (results depend on it, not on the rank)
         one.batch_ksplit = ep.batch_ksplit
@@ -278,7 +284,6 @@ def _worker(rank, world, port, q):
         from ervf_b200 import _lib
 
         status = _lib.load().ervf_device_status()
-        del graph
         torch.cuda.synchronize()
         ep.close()
         dist.destroy_process_group()
