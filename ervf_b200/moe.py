@@ -173,17 +173,21 @@ class MoEDecoder:
         # and down rows as one claimed work list, bit-identical to the
         # per-layer launches); False runs the per-layer launches.
         # With expert parallelism over peer memory (exchange "p2p", up to 8
-        # ranks) the token is one launch per rank too (ervf_moe_token_ep: each
-        # rank's slot rows go to every rank over NVLink inside the launch),
-        # bit-identical to one GPU; False runs the per-layer launches and one
-        # exchange kernel per layer.
-        self.token = ep_ranks == 1 or (exchange == "p2p" and ep_ranks <= 8)
+        # ranks) the token can be one launch per rank too (ervf_moe_token_ep:
+        # each rank's slot rows go to every rank over NVLink inside the
+        # launch), bit-identical to one GPU; False runs the per-layer launches
+        # and one exchange kernel per layer.  Default: the one launch up to 4
+        # ranks (B200, batch 1: 1676 against 1569 tok/s at 2 ranks, 1640 for
+        # both at 4), the per-layer launches at 8 (1432 tok/s for the one
+        # launch against 1476-1752 measured for them).
+        token_ep = exchange == "p2p" and 1 < ep_ranks <= 8
+        self.token = ep_ranks == 1 or (token_ep and ep_ranks <= 4)
         # step_with_router in one launch too (router items inside the token
         # kernel): bit-identical to the per-layer router + expert launches and,
         # on B200, 0.896 ms per 24-layer token against 0.930 ms for them
         self.token_router = ep_ranks == 1
         self.layer_ptrs = self.tok_scratch = self.tok_xchg = None
-        if self.token:
+        if self.token or token_ep:
             addrs = ([ptr(t) for t in bank.up_codes] + [ptr(t) for t in bank.up_scales]
                      + [ptr(t) for t in bank.dn_codes] + [ptr(t) for t in bank.dn_scales]
                      + [ptr(t) for t in bank.globals])
