@@ -505,6 +505,17 @@ def qwen_block_b16(device, hbm, tokens=16, layers=48, pools=4, steps=5):
                     "(tolerance), route-order sum; seeded random record bytes"}
 
 
+def busiest_rank_slots(rlogs, world, top_k=TOP_K):
+    """Per token (rlogs [T][L][E] router logits), the sum over layers of the
+    most route slots that any one rank owns (expert e on rank e % world,
+    slots = the top_k experts of the layer's logits): the records the
+    busiest rank streams, which bounds an expert-parallel step.  [T] floats;
+    top_k * L for one rank."""
+    top = rlogs.topk(top_k, dim=-1).indices                                # [T, L, K]
+    counts = torch.nn.functional.one_hot(top % world, world).sum(dim=-2)   # [T, L, world]
+    return counts.max(dim=-1).values.sum(dim=-1).to(torch.float64)
+
+
 def routed_decode(dec, device, hbm, steps=50):
     """Config 4 at batch 1 with the router on the device between the layers
     (per layer: router GEMV fp32 [128 x 2688] + top-k in one launch, then up
@@ -760,9 +771,12 @@ def main():
                  # the whole config-2 MoE layer at batch 16 on the tensor cores
                  "qwen_block_b16": qwen_block_b16(device, hbm)}
 
+    # records of the busiest rank per timed token (load-imbalance-aware roofline)
+    busiest = float(busiest_rank_slots(rlogs[args.warmup:args.warmup + args.steps], world).mean())
     if rank == 0:
         # bytes one token streams: distinct (layer, expert) pairs x expert bytes
         token_bytes = L * TOP_K * bank.expert_bytes()
+        busiest_bytes = busiest * bank.expert_bytes()
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -781,6 +795,10 @@ def main():
             "gpu_launches": (2 if dec.token else (2 * L + 1 if world == 1 else 3 * L + 1)) * args.steps,
             "token_bytes": token_bytes,
             "token_roofline_frac": (token_bytes / (ms / args.steps / 1e3) / 1e9) / (hbm * world),
+            # against the busiest rank's records per token and one GPU's HBM
+            # (equal to token_roofline_frac on one GPU)
+            "busiest_rank_records_per_token": busiest,
+            "token_roofline_frac_busiest": (busiest_bytes / (ms / args.steps / 1e3) / 1e9) / hbm,
             "clocks": clocks,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": (HIDDEN + L * N_EXPERTS) * 4,
                     "d2h_bytes_per_step": HIDDEN * 4},
