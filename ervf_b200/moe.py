@@ -399,7 +399,10 @@ class MoEDecoder:
     def device_status(self) -> int:
         """Read and clear the library's device error words; after a timeout
         zero this decoder's scratch buffers (and the FusedNVFP4 caches) so the
-        next step starts from clean counters.  Returns the status."""
+        next step starts from clean counters.  Returns the status.  With
+        expert parallelism the token scratch is shared by all ranks: after a
+        timeout every rank calls ``prepare_token_ep()`` (collective) before
+        the next token."""
         st = self.fused.device_status()
         if st == _lib.ERR_TIMEOUT:
             self.scratch.zero_()
