@@ -41,6 +41,13 @@
 // router items: one consumer warp per expert row computes the reference's
 // gemv_f32 row, the item that completes the layer runs route_topk_f32 and
 // releases the layer's ids; expert items of that layer wait for them.
+// With expert parallelism (EP instantiation, ervf_moe_token_ep) each rank's
+// list holds only the UP / DOWN items of the slots whose expert it owns, plus
+// one SUM item per down row block per layer: DOWN rows go to every rank's
+// contrib[l][slot] as raw peer stores, and each rank's SUM items wait for the
+// words themselves (kUnwritten), add them in route order and write x_{l+1};
+// an entry handshake per token orders one token's writes after every rank's
+// previous token (see TokArgs and the PREP publisher).
 // The last CTA to leave zeroes every counter, so the scratch is ready for
 // the next token (also after a timeout, once all CTAs have left).
 #include <stdlib.h>
@@ -110,7 +117,7 @@ struct TokArgs {
   // Expert parallelism (EP instantiation): this rank owns the experts e with
   // e % ep_n == ep_rank.  peer[q] is rank q's scratch as mapped on this GPU
   // (peer[ep_rank] = this rank's own); every rank's scratch has the same
-  // layout, so a peer's counters sit at the same offsets as a.ctr's.
+  // layout, so a peer's contrib and entry flags sit at this rank's offsets.
   int ep_n, ep_rank;
   unsigned long long peer[kTokMaxRanks];
   size_t contrib_off;              // byte offset of contrib in every rank's scratch
