@@ -156,10 +156,12 @@ def time_region(fn, steps, device):
     return a.elapsed_time(b)
 
 
-def time_graph(fn, steps, device):
+def time_graph(fn, steps, device, barrier=None):
     """Device time per call (ms) of `steps` calls of fn captured in one CUDA
     graph, so that host launch cost does not hide short kernels; replayed
-    once untimed, then timed with CUDA events."""
+    once untimed, then timed with CUDA events.  `barrier` (ranks that wait
+    for one another inside fn): called before the timed replay so that every
+    rank starts it together."""
     s = torch.cuda.Stream(device)
     s.wait_stream(torch.cuda.current_stream(device))
     with torch.cuda.stream(s):
@@ -171,6 +173,8 @@ def time_graph(fn, steps, device):
             fn(i)
     g.replay()
     torch.cuda.synchronize(device)
+    if barrier is not None:
+        barrier()
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     a.record()
@@ -436,7 +440,15 @@ def batched_decode(dec, device, hbm, world=1, tokens=32, steps=20):
         busiest += max(int((u % world == r).sum()) for r in range(world))
     step_bytes = distinct * rec + L * act_bytes
     busiest_bytes = busiest * rec + L * act_bytes
-    ms = time_graph(lambda i: dec.step_batch(xb, rb), steps, device)
+    sync = None
+    if world > 1:
+        import torch.distributed as dist
+
+        def sync():
+            dist.barrier()
+            torch.cuda.synchronize(device)
+
+    ms = time_graph(lambda i: dec.step_batch(xb, rb), steps, device, barrier=sync)
     if world > 1:
         import torch.distributed as dist
 
@@ -713,6 +725,10 @@ def main():
         step(i)
     barrier()
     with Clocks(device.index) as clk:
+        # every rank's sampler is running: the ranks start the timed region
+        # together (they are coupled every token, so a rank that started
+        # late would otherwise add its delay to the others' time)
+        barrier()
         ms = time_region(lambda i: step(args.warmup + i), args.steps, device)
         barrier()
     clocks = clk.summary()
