@@ -173,15 +173,14 @@ class MoEDecoder:
         # and down rows as one claimed work list, bit-identical to the
         # per-layer launches); False runs the per-layer launches.
         # With expert parallelism over peer memory (exchange "p2p", up to 8
-        # ranks) the token can be one launch per rank too (ervf_moe_token_ep:
-        # each rank's slot rows go to every rank over NVLink inside the
-        # launch), bit-identical to one GPU; False runs the per-layer launches
-        # and one exchange kernel per layer.  Default: the one launch up to 4
-        # ranks (B200, batch 1: 1676 against 1569 tok/s at 2 ranks, 1640 for
-        # both at 4), the per-layer launches at 8 (1432 tok/s for the one
-        # launch against 1476-1752 measured for them).
+        # ranks) the token is one launch per rank too (ervf_moe_token_ep: each
+        # rank's slot rows go to every rank over NVLink inside the launch),
+        # bit-identical to one GPU; False runs the per-layer launches and one
+        # exchange kernel per layer.  B200, batch 1, through the public API:
+        # 1604 / 1568 / 1595 tok/s at 2 / 4 / 8 ranks for the one launch,
+        # 1457 / 1530 / 1602-1606 for the per-layer launches.
         token_ep = exchange == "p2p" and 1 < ep_ranks <= 8
-        self.token = ep_ranks == 1 or (token_ep and ep_ranks <= 4)
+        self.token = ep_ranks == 1 or token_ep
         # step_with_router in one launch too (router items inside the token
         # kernel): bit-identical to the per-layer router + expert launches and,
         # on B200, 0.896 ms per 24-layer token against 0.930 ms for them
