@@ -7,10 +7,11 @@ relu^2, down 2688x1856), all HBM-resident (17.24 GB), sigmoid top-6 routing
 from random logits per layer and token, x_{L+1} = x_L + moe_L(x_L) in fp32.
 A "step" is one token through all 24 layers.  Weights are seeded synthetic
 (N(0, 0.02) quantised to NVFP4 on the device): the real checkpoint is not
-available.  With --gpus N the experts are sharded by id (e % N); per layer
-one exchange kernel reads every route slot's output from its owner's memory
-over NVLink and adds the slots in route order (--exchange nccl: an NCCL
-all-gather and a route-sum launch instead).
+available.  With --gpus N the experts are sharded by id (e % N) and every
+rank runs the token in one launch that writes its route slots' rows into
+every rank's memory over NVLink and sums them in route order
+(--exchange nccl: per-layer launches with an NCCL all-gather and a
+route-sum launch instead).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
