@@ -110,3 +110,12 @@ def test_token_ep_entry_checks_arguments_without_a_device():
     assert call(peer=ctypes.cast(zero, ctypes.c_void_p)) == _lib.ERR_NULL
     odd = (ctypes.c_uint64 * 2)(0x10000, 0x20010)
     assert call(peer=ctypes.cast(odd, ctypes.c_void_p)) == _lib.ERR_ALIGN
+
+
+def test_token_ep_prepare_checks_arguments_without_a_device():
+    lib = _lib.load()
+    nb = lib.ervf_moe_token_ep_scratch_bytes(24, 2688, 1856, 6)
+    assert lib.ervf_moe_token_ep_prepare(None, nb, 24, 2688, 1856, 6, None) == _lib.ERR_NULL
+    assert lib.ervf_moe_token_ep_prepare(0x10000, nb, 0, 2688, 1856, 6, None) == _lib.ERR_SHAPE
+    assert lib.ervf_moe_token_ep_prepare(0x10000, nb - 1, 24, 2688, 1856, 6, None) == _lib.ERR_ARG
+    assert lib.ervf_moe_token_ep_prepare(0x10010, nb, 24, 2688, 1856, 6, None) == _lib.ERR_ALIGN
